@@ -1,0 +1,113 @@
+"""Sliding-window + global-token (Longformer-style) attention forward for NVIDIA B200.
+
+Drop-in for the reference package ``long_context_attention``
+(python/long_context_attention/__init__.py): same module name, same public function
+``sliding_window_attention(Q, K, V, window_size, global_tokens=(), scale=None,
+force_reference=False)`` and the same helper name ``_reference_sliding_window_attention``.
+
+Dispatch differs from the reference on purpose: CUDA tensors always go to the sm_100a
+kernels (``long_context_attention_kernels`` -> ``liblca_b200.so``), and a missing or
+unloadable native build raises instead of silently falling back to the dense O(n^2)
+computation.  The dense computation runs only when asked for explicitly
+(``force_reference=True``), which is also how CPU tensors are handled.
+"""
+from __future__ import annotations
+
+import math
+from typing import Sequence
+
+import torch
+
+from ._native import extension, native_error
+
+__all__ = ["sliding_window_attention", "sliding_window_attention_with_lse"]
+
+
+def _reference_sliding_window_attention(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    window_size: int,
+    global_tokens: Sequence[int],
+    scale: float,
+) -> torch.Tensor:
+    """Dense Longformer-mask attention (the reference's definition, O(n^2) memory).
+
+    Same mask and arithmetic as python/long_context_attention/__init__.py:24-53: key j
+    is visible to query i iff |i - j| <= window_size, or j or i is a global token;
+    fp32 scores, masked softmax, fp32 output.  Reached only through
+    ``force_reference=True`` or a direct call; never used as a fallback.
+    """
+    seq_len = Q.shape[2]
+    device = Q.device
+    idx = torch.arange(seq_len, device=device)
+    band = (idx[:, None] - idx[None, :]).abs() <= window_size
+    is_global = torch.zeros(seq_len, dtype=torch.bool, device=device)
+    if len(global_tokens) > 0:
+        is_global[list(global_tokens)] = True
+    visible = band | is_global[None, :] | is_global[:, None]
+    scores = torch.einsum("bhqd,bhkd->bhqk", Q.float(), K.float()) * scale
+    scores = scores.masked_fill(~visible[None, None, :, :], float("-inf"))
+    return torch.einsum("bhqk,bhkd->bhqd", torch.softmax(scores, dim=-1), V.float())
+
+
+def _prepare(Q: torch.Tensor, window_size: int, global_tokens: Sequence[int], scale):
+    if scale is None:
+        scale = 1.0 / math.sqrt(Q.shape[-1])
+    if not Q.is_cuda:
+        raise RuntimeError(
+            "long_context_attention: Q, K, V must be CUDA tensors on a B200 (sm_100a) GPU; "
+            "pass force_reference=True for the dense CPU definition"
+        )
+    tokens = [int(t) for t in global_tokens]
+    return float(scale), int(window_size), tokens
+
+
+def sliding_window_attention(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    window_size: int,
+    global_tokens: Sequence[int] = (),
+    scale: float | None = None,
+    force_reference: bool = False,
+) -> torch.Tensor:
+    """Longformer-style sparse attention forward.
+
+    Q, K, V: [batch, heads, seq_len, head_dim], fp16 or bf16, CUDA, contiguous,
+    head_dim 64 or 128.  window_size: band radius (|i - j| <= window_size is visible).
+    global_tokens: token indices with full rows and columns (negative indices count from
+    the end; duplicates are harmless).  scale defaults to 1/sqrt(head_dim).
+    Returns a new fp32 tensor [batch, heads, seq_len, head_dim] on Q's device, computed
+    on the current CUDA stream.
+    """
+    if force_reference:
+        if scale is None:
+            scale = 1.0 / math.sqrt(Q.shape[-1])
+        return _reference_sliding_window_attention(Q, K, V, window_size, global_tokens, scale)
+    scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
+    return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
+
+
+def sliding_window_attention_with_lse(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    window_size: int,
+    global_tokens: Sequence[int] = (),
+    scale: float | None = None,
+):
+    """As :func:`sliding_window_attention`, also returning the per-row log-sum-exp.
+
+    Returns ``(O, LSE)`` with LSE [batch, heads, seq_len] fp32, the natural log of the
+    sum of exp(scale * q.k) over each row's visible keys (the quantity a backward pass
+    or a cross-shard merge needs).  No counterpart in the reference.
+    """
+    scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
+    out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
+    return out, lse
+
+
+def device_error() -> int:
+    """Read and clear the device-side error word (synchronises the current device)."""
+    return native_error()

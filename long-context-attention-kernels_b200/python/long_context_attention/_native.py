@@ -1,0 +1,111 @@
+"""Loading of the native build: the torch extension ``long_context_attention_kernels``
+(which links ``liblca_b200.so``) and a ctypes handle on the C ABI itself.
+
+There is no fallback: if the native build is missing, every GPU entry point raises with
+the command that builds it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblca_b200.so")
+BUILD_HINT = "build it with: python long-context-attention-kernels_b200/build_native.py"
+
+_lock = threading.Lock()
+_ext = None
+_cabi = None
+
+
+def extension():
+    """The torch extension module (imported once); raises RuntimeError if unavailable."""
+    global _ext
+    if _ext is None:
+        with _lock:
+            if _ext is None:
+                try:
+                    import long_context_attention_kernels as mod  # noqa: PLC0415
+                except ImportError as e:  # pragma: no cover - exercised only without a build
+                    raise RuntimeError(
+                        f"long_context_attention: native extension not available ({e}); {BUILD_HINT}"
+                    ) from e
+                _ext = mod
+    return _ext
+
+
+def native_error() -> int:
+    return extension().device_error()
+
+
+class CABI:
+    """ctypes binding of include/lca.h (the same stub a non-Python caller would write)."""
+
+    OK = 0
+    ERR_INVALID_ARGUMENT = 1
+    ERR_INDEX = 2
+    ERR_UNSUPPORTED = 3
+    ERR_WORKSPACE = 4
+    ERR_CUDA = 5
+    ERR_DEVICE = 6
+    DTYPE_F16 = 0
+    DTYPE_BF16 = 1
+
+    def __init__(self, path: str = LIB_PATH):
+        if not os.path.exists(path):
+            raise RuntimeError(f"long_context_attention: {path} not found; {BUILD_HINT}")
+        lib = ctypes.CDLL(path)
+        i64, vp, sz = ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t
+        lib.lca_abi_version.restype = ctypes.c_int
+        lib.lca_abi_version.argtypes = []
+        lib.lca_status_string.restype = ctypes.c_char_p
+        lib.lca_status_string.argtypes = [ctypes.c_int]
+        lib.lca_last_error.restype = ctypes.c_char_p
+        lib.lca_last_error.argtypes = []
+        lib.lca_normalize_global_tokens.restype = ctypes.c_int
+        lib.lca_normalize_global_tokens.argtypes = [ctypes.POINTER(i64), i64, i64, ctypes.POINTER(ctypes.c_int32),
+                                                    ctypes.POINTER(i64)]
+        lib.lca_swa_workspace_size.restype = ctypes.c_int
+        lib.lca_swa_workspace_size.argtypes = [i64, i64, i64, i64, i64, ctypes.c_int, ctypes.POINTER(sz)]
+        lib.lca_swa_forward.restype = ctypes.c_int
+        lib.lca_swa_forward.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64, ctypes.c_float,
+                                        ctypes.POINTER(i64), i64, vp, sz, vp]
+        lib.lca_set_timing_events.restype = ctypes.c_int
+        lib.lca_set_timing_events.argtypes = [vp, vp]
+        lib.lca_device_error.restype = ctypes.c_int
+        lib.lca_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
+        self.lib = lib
+
+    def last_error(self) -> str:
+        return self.lib.lca_last_error().decode()
+
+    def normalize(self, tokens, seq_len: int):
+        n = len(tokens)
+        arr = (ctypes.c_int64 * max(n, 1))(*tokens)
+        out = (ctypes.c_int32 * max(n, 1))()
+        cnt = ctypes.c_int64(0)
+        st = self.lib.lca_normalize_global_tokens(arr, n, seq_len, out, ctypes.byref(cnt))
+        return st, [out[i] for i in range(cnt.value)]
+
+    def workspace_size(self, batch, heads, seq_len, head_dim, num_unique_global, dtype) -> tuple[int, int]:
+        out = ctypes.c_size_t(0)
+        st = self.lib.lca_swa_workspace_size(batch, heads, seq_len, head_dim, num_unique_global, dtype,
+                                             ctypes.byref(out))
+        return st, out.value
+
+    def forward(self, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim, window, scale,
+                tokens, ws_ptr, ws_bytes, stream_ptr) -> int:
+        n = len(tokens)
+        arr = (ctypes.c_int64 * max(n, 1))(*tokens)
+        return self.lib.lca_swa_forward(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim,
+                                        window, ctypes.c_float(scale), arr, n, ws_ptr, ws_bytes, stream_ptr)
+
+
+def cabi() -> CABI:
+    global _cabi
+    if _cabi is None:
+        with _lock:
+            if _cabi is None:
+                _cabi = CABI()
+    return _cabi

@@ -1,0 +1,89 @@
+"""CPU oracle for the sliding-window + global-token attention forward.
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker: only tests/, the smoke check in
+__graft_entry__.py and bench.py's CPU-baseline arm may import it.  The product path
+(long_context_attention -> liblca_b200.so) never calls it.
+
+It restates, in numpy, the reference's dense Longformer-mask implementation
+``_reference_sliding_window_attention`` (python/long_context_attention/__init__.py:24-53)
+row block by row block, so that it also runs at sequence lengths where the dense
+[n, n] score matrix would not fit:
+
+* mask (``__init__.py:39-47``): key j visible to query i iff |i - j| <= window_size, or
+  j is a global token, or i is a global token;
+* global-token list (``__init__.py:42-44``): ``global_mask[list(global_tokens)] = True``,
+  i.e. negative indices wrap, duplicates are idempotent, out-of-range raises IndexError;
+* arithmetic (``__init__.py:49-53``): scores = (Q K^T) * scale on float inputs,
+  masked_fill(-inf), softmax over keys, times V.  The reference does this in fp32; the
+  oracle defaults to fp64 so its own rounding sits far below the tolerances it checks.
+
+It additionally returns the natural-log log-sum-exp of each row's visible scaled scores
+(the reference computes it implicitly inside softmax).
+
+Parity of this restatement is pinned against outputs of the reference itself: see
+tests/golden/make_golden.py (generates fixtures by importing the reference) and
+tests/test_oracle.py.
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+import numpy as np
+
+
+def normalize_global_tokens(global_tokens: Sequence[int], seq_len: int) -> np.ndarray:
+    """Sorted unique global indices under the reference's indexing rules
+    (python/long_context_attention/__init__.py:42-44)."""
+    out = set()
+    for t in global_tokens:
+        t = int(t)
+        if t < -seq_len or t >= seq_len:
+            raise IndexError(f"index {t} is out of bounds for dimension 0 with size {seq_len}")
+        out.add(t + seq_len if t < 0 else t)
+    return np.asarray(sorted(out), dtype=np.int64)
+
+
+def visible_rows(rows: np.ndarray, seq_len: int, window_size: int, global_idx: np.ndarray) -> np.ndarray:
+    """Boolean [len(rows), seq_len] mask rows (python/long_context_attention/__init__.py:39-47)."""
+    rows = np.asarray(rows, dtype=np.int64)
+    keys = np.arange(seq_len, dtype=np.int64)
+    mask = np.abs(rows[:, None] - keys[None, :]) <= window_size
+    is_global = np.zeros(seq_len, dtype=bool)
+    if global_idx.size:
+        is_global[global_idx] = True
+    mask |= is_global[None, :]
+    mask |= is_global[rows][:, None]
+    return mask
+
+
+def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[int], scale: float,
+                             rows: Sequence[int] | None = None, dtype=np.float64, block_rows: int = 256):
+    """Dense-mask attention on the CPU.
+
+    Q, K, V: arrays [B, H, n, d] (any float dtype; converted to `dtype`).
+    rows: query rows to compute (default: all).  Returns (O, LSE) with O [B, H, len(rows), d]
+    and LSE [B, H, len(rows)] in `dtype`.
+    """
+    Q = np.asarray(Q)
+    K = np.asarray(K)
+    V = np.asarray(V)
+    B, H, n, d = Q.shape
+    g = normalize_global_tokens(global_tokens, n)
+    rows = np.arange(n, dtype=np.int64) if rows is None else np.asarray(rows, dtype=np.int64)
+    out = np.empty((B, H, rows.size, d), dtype=dtype)
+    lse = np.empty((B, H, rows.size), dtype=dtype)
+    for b in range(B):
+        for h in range(H):
+            k = K[b, h].astype(dtype, copy=False)
+            v = V[b, h].astype(dtype, copy=False)
+            for s in range(0, rows.size, block_rows):
+                r = rows[s:s + block_rows]
+                q = Q[b, h, r].astype(dtype, copy=False)
+                scores = (q @ k.T) * dtype(scale)
+                scores = np.where(visible_rows(r, n, window_size, g), scores, -np.inf)
+                m = scores.max(axis=1, keepdims=True)
+                p = np.exp(scores - m)
+                l = p.sum(axis=1, keepdims=True)
+                out[b, h, s:s + r.size] = (p @ v) / l
+                lse[b, h, s:s + r.size] = (m + np.log(l))[:, 0]
+    return out, lse

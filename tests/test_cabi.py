@@ -1,0 +1,55 @@
+"""The C ABI library loads and exports every entry point include/lca.h declares; argument
+validation that happens before any device work behaves as documented (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from long_context_attention import _native
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    hdr = open(os.path.join(REPO, "include", "lca.h")).read()
+    return re.findall(r"LCA_API\s+[\w\s\*]+?\b(lca_\w+)\s*\(", hdr)
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_functions()
+    assert "lca_swa_forward" in names and len(names) >= 7
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_abi_version_and_status_strings():
+    c = _native.cabi()
+    assert c.lib.lca_abi_version() == 1
+    for code in range(7):
+        assert c.lib.lca_status_string(code)
+    assert c.lib.lca_status_string(99) == b"unknown status"
+
+
+def _fwd(c, **kw):
+    args = dict(q_ptr=None, k_ptr=None, v_ptr=None, o_ptr=None, lse_ptr=None, dtype=c.DTYPE_BF16, batch=1,
+                heads=1, seq_len=128, head_dim=64, window=4, scale=0.125, tokens=[], ws_ptr=None, ws_bytes=0,
+                stream_ptr=None)
+    args.update(kw)
+    return c.forward(**args)
+
+
+def test_forward_validation_before_device_work():
+    c = _native.cabi()
+    assert _fwd(c, dtype=7) == c.ERR_UNSUPPORTED
+    assert _fwd(c, head_dim=96) == c.ERR_UNSUPPORTED
+    assert _fwd(c, window=-1) == c.ERR_INVALID_ARGUMENT
+    assert _fwd(c, tokens=[128]) == c.ERR_INDEX
+    assert _fwd(c, tokens=[-129]) == c.ERR_INDEX
+    # empty problems succeed without touching a device
+    assert _fwd(c, batch=0) == c.OK
+    assert _fwd(c, seq_len=0) == c.OK
+    # a NULL tensor pointer is rejected before any launch
+    assert _fwd(c) == c.ERR_INVALID_ARGUMENT
+    assert "non-NULL" in c.last_error()

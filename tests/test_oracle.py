@@ -1,0 +1,90 @@
+"""The CPU oracle, pinned against outputs of the reference implementation itself
+(tests/golden/*.npz, made by tests/golden/make_golden.py) and against the reference's
+own known-answer tests (tests/test_correctness.py:26-62 of the reference)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from lca_testutil import golden_names, load_golden, max_abs, rel_l2
+from oracle import swa_oracle
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_oracle_matches_reference_fixture(name):
+    c = load_golden(name)
+    out, lse = swa_oracle.sliding_window_attention(
+        c["q"].float().numpy(), c["k"].float().numpy(), c["v"].float().numpy(), c["window"], c["globals"],
+        c["scale"], rows=c["rows"])
+    # the reference computes in fp32, the oracle in fp64: agreement to fp32 rounding
+    assert max_abs(out, c["out"]) < 2e-6, name
+    assert rel_l2(out, c["out"]) < 1e-6, name
+    assert np.all(np.isfinite(lse))
+
+
+def _full_attention(q, k, v, scale):
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return np.einsum("bhqk,bhkd->bhqd", p, v)
+
+
+def test_unmasked_window_equals_full_attention():
+    # reference tests/test_correctness.py:26-40
+    rng = np.random.default_rng(0)
+    q, k, v = (rng.standard_normal((1, 2, 32, 16)) for _ in range(3))
+    out, _ = swa_oracle.sliding_window_attention(q, k, v, 32, [], 1 / math.sqrt(16))
+    np.testing.assert_allclose(out, _full_attention(q, k, v, 1 / math.sqrt(16)), atol=1e-12)
+
+
+def test_global_row_gets_full_context():
+    # reference tests/test_correctness.py:43-62
+    rng = np.random.default_rng(1)
+    q, k, v = (rng.standard_normal((1, 1, 64, 16)) for _ in range(3))
+    out, _ = swa_oracle.sliding_window_attention(q, k, v, 1, [0], 0.25)
+    full = _full_attention(q, k, v, 0.25)
+    np.testing.assert_allclose(out[:, :, 0], full[:, :, 0], atol=1e-12)
+    assert not np.allclose(out[:, :, 32], full[:, :, 32], atol=1e-3)
+
+
+def test_duplicates_and_negative_indices():
+    rng = np.random.default_rng(2)
+    q, k, v = (rng.standard_normal((1, 1, 40, 8)) for _ in range(3))
+    a, la = swa_oracle.sliding_window_attention(q, k, v, 3, [0, 0, 5], 0.3)
+    b, lb = swa_oracle.sliding_window_attention(q, k, v, 3, [5, 0], 0.3)
+    c, _ = swa_oracle.sliding_window_attention(q, k, v, 3, [-40, -35], 0.3)
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(la, lb)
+    np.testing.assert_array_equal(a, c)
+
+
+def test_out_of_range_index_raises():
+    q = np.zeros((1, 1, 10, 4))
+    with pytest.raises(IndexError):
+        swa_oracle.sliding_window_attention(q, q, q, 1, [10], 1.0)
+    with pytest.raises(IndexError):
+        swa_oracle.sliding_window_attention(q, q, q, 1, [-11], 1.0)
+
+
+def test_lse_matches_torch_logsumexp():
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 2, 70, 8, generator=g, dtype=torch.float64) for _ in range(3))
+    out, lse = swa_oracle.sliding_window_attention(q.numpy(), k.numpy(), v.numpy(), 5, [3, 60], 0.4)
+    mask = torch.from_numpy(swa_oracle.visible_rows(np.arange(70), 70, 5, np.array([3, 60])))
+    s = torch.einsum("bhqd,bhkd->bhqk", q, k) * 0.4
+    s = s.masked_fill(~mask, float("-inf"))
+    np.testing.assert_allclose(lse, torch.logsumexp(s, -1).numpy(), atol=1e-12)
+    np.testing.assert_allclose(out, torch.einsum("bhqk,bhkd->bhqd", torch.softmax(s, -1), v).numpy(),
+                               atol=1e-12)
+
+
+def test_row_subset_equals_full():
+    rng = np.random.default_rng(4)
+    q, k, v = (rng.standard_normal((2, 1, 300, 16)).astype(np.float32) for _ in range(3))
+    full, lf = swa_oracle.sliding_window_attention(q, k, v, 20, [7, 299], 0.25, block_rows=64)
+    rows = [0, 7, 150, 299]
+    sub, ls = swa_oracle.sliding_window_attention(q, k, v, 20, [7, 299], 0.25, rows=rows)
+    np.testing.assert_allclose(sub, full[:, :, rows], atol=1e-12)
+    np.testing.assert_allclose(ls, lf[:, :, rows], atol=1e-12)
