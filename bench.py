@@ -45,6 +45,8 @@ def parse_args(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-budget-s", type=float, default=10.0, help="CPU baseline sample budget (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="override heads per GPU (smaller cases for profiling; not the headline config)")
     return ap.parse_args(argv)
 
 
@@ -211,6 +213,8 @@ def run_ours(args):
     # seeded tensors with the seed offset by the rank
     import dataclasses
     w = dataclasses.replace(base, seed=base.seed + rank)
+    if args.heads is not None:
+        w = dataclasses.replace(w, heads=args.heads)
     q, k, v = w.inputs(device=dev)
     g = w.global_tokens()
     cabi = _native.cabi()

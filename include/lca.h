@@ -68,7 +68,7 @@ LCA_API int lca_normalize_global_tokens(const int64_t* tokens, int64_t count, in
  * global tokens).  `num_unique_global` is the count after normalisation.  Host-only.
  */
 LCA_API int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
-                           int64_t num_unique_global, int dtype, size_t* out_bytes);
+                                   int64_t window_size, int64_t num_unique_global, int dtype, size_t* out_bytes);
 
 /*
  * Sliding-window + global-token attention forward.

@@ -57,7 +57,8 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
     raise_status(lca_normalize_global_tokens(globals.data(), (int64_t)globals.size(), seq_len, norm.data(), &G),
                  "global_tokens");
     size_t ws_bytes = 0;
-    raise_status(lca_swa_workspace_size(batch, heads, seq_len, head_dim, G, dtype, &ws_bytes), "workspace size");
+    raise_status(lca_swa_workspace_size(batch, heads, seq_len, head_dim, window_size, G, dtype, &ws_bytes),
+                 "workspace size");
     torch::Tensor ws;
     void* ws_ptr = nullptr;
     if (ws_bytes > 0) {

@@ -44,6 +44,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_dev_mu;
 int g_dev_state[kMaxDevices];          // 0 unknown, 1 ok, -1 unsupported
 int* g_dev_err_word[kMaxDevices];      // device address of the error word
+int g_dev_sms[kMaxDevices];            // multiprocessor count
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -79,6 +80,8 @@ int check_device(int* dev_out, int** err_word) {
             e = lca::error_word_address(&addr);
             if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(error word)");
             g_dev_err_word[dev] = addr;
+            cudaDeviceGetAttribute(&g_dev_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+            if (g_dev_sms[dev] <= 0) g_dev_sms[dev] = 148;
             g_dev_state[dev] = 1;
         }
     }
@@ -92,7 +95,7 @@ int check_device(int* dev_out, int** err_word) {
 
 // ------------------------------------------------------------------ problem layout
 
-constexpr int kSplitTarget = 148;  // global-row work units aimed at one per SM
+constexpr int kMinGrowUnits = 148;  // at least one global-row unit per SM when possible
 constexpr size_t kAlign = 1024;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -103,7 +106,11 @@ struct Layout {
     size_t off_gidx = 0, off_qg = 0, off_kg = 0, off_vg = 0, off_po = 0, off_plse = 0, total = 0;
 };
 
-Layout make_layout(int64_t bh, int64_t n, int64_t d, int64_t G) {
+// Split of the n keys for the global-row units.  A unit covers `split_tiles` key tiles
+// (its two query-tile warpgroups take alternate tiles), sized at about twice a band
+// unit's work so units stay similar in length, but shrunk until there are enough units
+// to occupy every SM.  Each split yields two partial results (even / odd tiles).
+Layout make_layout(int64_t bh, int64_t n, int64_t d, int64_t G, int64_t window) {
     Layout L;
     L.bh = bh;
     L.n = n;
@@ -113,11 +120,15 @@ Layout make_layout(int64_t bh, int64_t n, int64_t d, int64_t G) {
     L.g_tiles = (int)((G + lca::kTileRows - 1) / lca::kTileRows);
     L.gpad = L.g_tiles * lca::kTileRows;
     L.key_tiles = (int)((n + lca::kTileRows - 1) / lca::kTileRows);
-    int64_t units = bh * L.g_tiles;
-    int64_t splits = (kSplitTarget + units - 1) / units;
-    splits = std::max<int64_t>(1, std::min<int64_t>(splits, L.key_tiles));
-    L.split_tiles = (int)((L.key_tiles + splits - 1) / splits);
+    const int64_t w = std::min(window, n);
+    const int64_t band_tiles = (2 * w + 2 * lca::kTileRows - 1) / lca::kTileRows + L.g_tiles;
+    int64_t split = std::max<int64_t>(4, std::min<int64_t>(64, 4 * band_tiles));
+    const int64_t units_per_split_count = bh * L.g_tiles;
+    while (split > 2 && units_per_split_count * ((L.key_tiles + split - 1) / split) < kMinGrowUnits) split -= 2;
+    split += split & 1;
+    L.split_tiles = (int)split;
     L.n_splits = (L.key_tiles + L.split_tiles - 1) / L.split_tiles;
+    const int64_t parts = 2 * (int64_t)L.n_splits;
     size_t off = 0;
     L.off_gidx = off;
     off = align_up(off + sizeof(int) * L.gpad, kAlign);
@@ -129,9 +140,9 @@ Layout make_layout(int64_t bh, int64_t n, int64_t d, int64_t G) {
     L.off_vg = off;
     off = align_up(off + gbytes, kAlign);
     L.off_po = off;
-    off = align_up(off + (size_t)L.n_splits * bh * L.gpad * d * 4, kAlign);
+    off = align_up(off + (size_t)parts * bh * L.gpad * d * 4, kAlign);
     L.off_plse = off;
-    off = align_up(off + (size_t)L.n_splits * bh * L.gpad * 4, kAlign);
+    off = align_up(off + (size_t)parts * bh * L.gpad * 4, kAlign);
     L.total = off;
     return L;
 }
@@ -212,7 +223,7 @@ int lca_normalize_global_tokens(const int64_t* tokens, int64_t count, int64_t se
     return LCA_OK;
 }
 
-int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
                            int64_t num_unique_global, int dtype, size_t* out_bytes) {
     if (out_bytes == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "out_bytes is NULL");
     if (batch < 0 || heads < 0 || seq_len < 0 || num_unique_global < 0)
@@ -220,7 +231,8 @@ int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_
     if (dtype != LCA_DTYPE_F16 && dtype != LCA_DTYPE_BF16) return fail(LCA_ERR_UNSUPPORTED, "dtype %d", dtype);
     if (head_dim != 64 && head_dim != 128)
         return fail(LCA_ERR_UNSUPPORTED, "head_dim %lld (supported: 64, 128)", (long long)head_dim);
-    *out_bytes = make_layout(batch * heads, seq_len, head_dim, std::min(num_unique_global, seq_len)).total;
+    if (window_size < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "window_size must be >= 0");
+    *out_bytes = make_layout(batch * heads, seq_len, head_dim, std::min(num_unique_global, seq_len), window_size).total;
     return LCA_OK;
 }
 
@@ -236,8 +248,8 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
         return fail(LCA_ERR_UNSUPPORTED, "head_dim %lld is not supported (64 or 128)", (long long)head_dim);
     if (batch < 0 || heads < 0 || seq_len < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "negative shape");
     if (window_size < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "window_size must be >= 0 (got %lld)", (long long)window_size);
-    if (seq_len > (int64_t)INT_MAX - 2 * lca::kTileRows)
-        return fail(LCA_ERR_UNSUPPORTED, "seq_len %lld too large", (long long)seq_len);
+    if (seq_len > ((int64_t)1 << 29))
+        return fail(LCA_ERR_UNSUPPORTED, "seq_len %lld too large (max 2^29)", (long long)seq_len);
     const int64_t bh = batch * heads;
     if (bh > INT_MAX / 64) return fail(LCA_ERR_UNSUPPORTED, "batch*heads %lld too large", (long long)bh);
     if (num_global_tokens < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "negative global token count");
@@ -264,7 +276,7 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
     st = check_device(&dev, &err_word);
     if (st != LCA_OK) return st;
 
-    const Layout L = make_layout(bh, seq_len, head_dim, G);
+    const Layout L = make_layout(bh, seq_len, head_dim, G, window_size);
     if (workspace_bytes < L.total) return fail(LCA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
     if (L.total > 0 && (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) % 256) != 0))
         return fail(LCA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
@@ -291,6 +303,9 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
     p.q_tiles = (n + lca::kTileRows - 1) / lca::kTileRows;
     p.num_global = (int)G;
     p.scale_log2 = scale * 1.4426950408889634f;
+    // scale == 0 gives every visible key the same weight; a tiny positive factor keeps
+    // that (scores * 1e-30 round to 0 in the exponent) while masked scores stay -inf.
+    if (p.scale_log2 == 0.f) p.scale_log2 = 1e-30f;
     p.lse = lse;
     p.err = err_word;
     p.timeout_ns = wait_timeout_ns();
@@ -300,7 +315,7 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
         p.gpad = L.gpad;
         p.n_splits = L.n_splits;
         p.split_tiles = L.split_tiles;
-        p.n_grow_ctas = (int)(bh * L.g_tiles * L.n_splits);
+        p.n_grow_units = (int)(bh * L.g_tiles * L.n_splits);
         p.gidx = reinterpret_cast<const int*>(ws + L.off_gidx);
         p.part_lse = reinterpret_cast<float*>(ws + L.off_plse);
         void* qg = ws + L.off_qg;
@@ -310,7 +325,7 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
         if ((st = encode_3d(&tm.kg, tdt, 2, kg, d, L.gpad, bh, 64, "k_global")) != LCA_OK) return st;
         if ((st = encode_3d(&tm.vg, tdt, 2, vg, d, L.gpad, bh, 64, "v_global")) != LCA_OK) return st;
         if ((st = encode_3d(&tm.po, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.off_po, d, L.gpad,
-                            (uint64_t)L.n_splits * bh, 32, "partial_out")) != LCA_OK)
+                            (uint64_t)2 * L.n_splits * bh, 32, "partial_out")) != LCA_OK)
             return st;
 
         // 1. gather the global rows (chunks of kGatherChunk indices per launch)
@@ -339,13 +354,16 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
     }
 
     // 2. band + global-row units
-    const long long grid = (long long)p.n_grow_ctas + (long long)bh * p.q_tiles;
-    if (grid > INT_MAX) return fail(LCA_ERR_UNSUPPORTED, "problem too large (%lld work units)", grid);
+    p.q_pairs = (p.q_tiles + 1) / 2;
+    const long long units = (long long)p.n_grow_units + (long long)bh * p.q_pairs;
+    if (units > INT_MAX) return fail(LCA_ERR_UNSUPPORTED, "problem too large (%lld work units)", units);
+    p.n_band_units = (int)(bh * p.q_pairs);
+    const int grid = (int)std::min<long long>(units, g_dev_sms[dev]);
     const bool timed = g_ev_before_main != nullptr && g_ev_after_main != nullptr;
     cudaError_t e;
     if (timed && (e = cudaEventRecord(g_ev_before_main, stream)) != cudaSuccess)
         return fail_cuda(e, "timing event record");
-    e = lca::launch_main(d, bf16, tm, p, (int)grid, stream);
+    e = lca::launch_main(d, bf16, tm, p, grid, stream);
     if (e != cudaSuccess) return fail_cuda(e, "main kernel launch");
     if (timed && (e = cudaEventRecord(g_ev_after_main, stream)) != cudaSuccess)
         return fail_cuda(e, "timing event record");
@@ -358,6 +376,7 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
         cp.gpad = L.gpad;
         cp.num_global = (int)G;
         cp.n_splits = L.n_splits;
+        cp.split_tiles = L.split_tiles;
         cp.gidx = p.gidx;
         cp.part_o = reinterpret_cast<const float*>(ws + L.off_po);
         cp.part_lse = p.part_lse;

@@ -5,30 +5,43 @@
 // i is a global token.  Output is fp32 softmax(scale * Q K^T restricted to that mask) V.
 //
 // Three launches per forward:
-//   1. lca_gather_globals   : copies the G global rows of Q, K, V into compact,
-//                             zero-padded [bh][gpad][d] buffers (gpad = 128 * ceil(G/128))
-//                             and writes the sorted index list.
-//   2. lca_swa_main         : one warp-specialised CTA per work unit.  Two unit kinds:
-//        band unit   : 128 query rows of one (batch, head).  Key tiles: the band
-//                      [q0 - w, q0 + 127 + w] in 128-key tiles (out-of-band tiles are
-//                      never issued), then the compact global-key tiles, masked so a
-//                      global key inside a row's band is counted only once (by the band).
-//                      Replaces csrc/sliding_window_attention.cu:48-160 and the
-//                      query-to-global-keys + combine kernels (csrc/global_attention.cu:
-//                      104-152, csrc/combine.cu:18-56) with their merge done in-register.
-//        global-row unit : 128 compact global queries against one contiguous split of
-//                      all n keys, producing a normalised partial O and its log-sum-exp.
-//                      Replaces csrc/global_attention.cu:29-96.
-//   3. lca_combine_global_rows : log-sum-exp merge of the splits, written over the
-//                      global rows of O (and LSE).
+//   1. lca_gather_globals : copies the G global rows of Q, K, V into compact,
+//                           zero-padded [bh][gpad][d] buffers (gpad = 128 * ceil(G/128))
+//                           and writes the sorted index list.
+//   2. lca_swa_main       : persistent, one CTA per SM, looping over work units:
+//        band unit      : two adjacent 128-row query tiles A, B of one (batch, head).
+//                         Key tiles: the band [q0 - w, q0 + 255 + w] in 128-key tiles
+//                         starting at q0 - w (A uses the first ceil((2w+128)/128) of
+//                         them, B the same count shifted by one; each tile is loaded
+//                         once for both), out-of-band and out-of-range tiles are never
+//                         issued; then the compact global-key tiles, masked so a global
+//                         key inside a row's band is counted once (by the band).
+//                         Replaces csrc/sliding_window_attention.cu:48-160 and the
+//                         query-to-global-keys + combine kernels (csrc/global_attention.cu:
+//                         104-152, csrc/combine.cu:18-56), merged in the online softmax.
+//        global-row unit: the compact global queries (one 128-row tile, loaded as both A
+//                         and B) against one contiguous split of all n keys, A taking the
+//                         even key tiles and B the odd ones; each writes a normalised
+//                         partial O and its log-sum-exp.  Replaces
+//                         csrc/global_attention.cu:29-96.
+//   3. lca_combine_global_rows : log-sum-exp merge of the partials, written over the
+//                           global rows of O (and LSE).
 //
-// Main-kernel CTA layout (192 threads):
-//   warps 0-3  softmax / epilogue: thread r owns query row r of the tile, which is TMEM
-//              lane r; S rows are read with tcgen05.ld, P is written to shared memory
-//              (bf16/f16, 128-byte swizzled K-major), O stays in TMEM.
-//   warp 4     TMA producer: Q tile once, then K_j / V_j tiles into a ring of slots.
-//   warp 5     TMEM allocator + single-thread tcgen05.mma issuer:
-//              S = Q K_j^T (M=128, N<=128, K=d) and O += P_j V_j (M=128, N=d, K<=128).
+// Main-kernel CTA layout (384 threads, launched at 168 registers per thread):
+//   warps 0-3  softmax + epilogue of query tile A (thread r <-> row r <-> TMEM lane r)
+//   warps 4-7  softmax + epilogue of query tile B
+//   warp 8     TMA producer: Q_A, Q_B per unit, then K_j / V_j into a ring of slots
+//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 10-11 idle
+// Register split (setmaxnreg): warpgroup 2 drops to 72, warpgroups 0-1 rise to 216;
+// 128*72 + 256*216 = 384*168, the launch allocation.
+// TMEM (512 columns): S_A [0,128), S_B [128,256), O_A [256, 256+d), O_B [256+d, 256+2d).
+// P overwrites S in place (packed 16-bit pairs) and feeds P*V as the TMEM A operand.
+// MMA issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one
+// tile's softmax runs, the tensor cores work for the other.  tcgen05 ops issued by one
+// thread execute in order, so S_X(j+1) never overwrites P_X(j) before PV_X(j) read it,
+// and the commit that signals S_X(j+1) also covers PV_X(j), so O_X is stable whenever
+// its softmax warps see a new S.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -48,11 +61,13 @@ namespace {
 
 constexpr int BM = 128;            // query rows per tile == TMEM lanes
 constexpr int BN = 128;            // keys per tile
-constexpr int kThreads = 192;
-constexpr int kSoftmaxThreads = 128;
-constexpr int kTmemCols = 256;     // S: columns [0,128), O: columns [128, 128 + d)
-constexpr int kSCol = 0;
-constexpr int kOCol = 128;
+constexpr int kThreads = 384;
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsSoftmax = 216;
+constexpr int kRegsControl = 72;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax == kThreads * kRegsLaunch, "register split");
+constexpr int kWgThreads = 128;
+constexpr int kTmemCols = 512;
 constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 bytes: one swizzle panel
 constexpr float kLn2 = 0.6931471805599453f;
 // The running max used for exponentiation is only raised when a new score exceeds it by
@@ -60,114 +75,125 @@ constexpr float kLn2 = 0.6931471805599453f;
 // accumulated against the same reference max.
 constexpr float kRescaleThreshold = 8.0f;
 
-// Shared-memory plan per CTA (all regions 1024-byte aligned):
-//   Q tile | K/V ring of kSlots tiles | P (one 128x128 16-bit tile, or two for split P) | control
-// For bf16 inputs P is kept as P_hi + P_lo (two bf16 tiles, P_hi = rn(p), P_lo = rn(p - P_hi))
-// and P*V is issued twice into the same accumulator: a single bf16 P would carry ~1.5e-3
-// relative L2 error into O, the split carries ~2^-16.  fp16 P is already accurate enough.
+// For bf16 inputs P is split as P_hi + P_lo (P_hi = rn_bf16(p), P_lo = rn_bf16(p - P_hi))
+// and P*V is issued twice into the same accumulator: a single bf16 P carries ~1.5e-3
+// relative L2 error into O, the split ~2^-16.  fp16 P is accurate enough on its own.
 template <int D, bool BF16>
 struct Cfg {
     static constexpr bool kSplitP = BF16;
     static constexpr int kPanels = D / 64;
     static constexpr int kTileBytes = BM * D * 2;
-    static constexpr int kSlots = 3;
-    static constexpr int kPTileBytes = BM * BN * 2;
-    static constexpr int kPBytes = kPTileBytes * (kSplitP ? 2 : 1);
+    static constexpr int kSlots = (D == 64) ? 4 : 3;
+    static constexpr int kStageBytes = 2 * kPanelBytes;  // per softmax warpgroup
     static constexpr int kOffQ = 0;
-    static constexpr int kOffSlots = kOffQ + kTileBytes;
-    static constexpr int kOffP = kOffSlots + kSlots * kTileBytes;
-    static constexpr int kOffCtl = kOffP + kPBytes;
+    static constexpr int kOffSlots = kOffQ + 2 * kTileBytes;
+    static constexpr int kOffStage = kOffSlots + kSlots * kTileBytes;
+    static constexpr int kOffCtl = kOffStage + 2 * kStageBytes;
     static constexpr int kCtlBytes = 1024;
     static constexpr int kSmemBytes = kOffCtl + kCtlBytes + 1024;  // +1024 for base alignment
-    static constexpr int kMinBlocks = (2 * (kSmemBytes + 1024) <= 228 * 1024) ? 2 : 1;
+    static constexpr int kOCol = 256;
 };
 
 struct Ctl {
-    uint64_t q_full;
-    uint64_t full[4];
-    uint64_t empty[4];
-    uint64_t s_full;
-    uint64_t s_free;
-    uint64_t p_full;
-    uint64_t pv_done;
+    uint64_t q_full[2];
+    uint64_t q_empty[2];
+    uint64_t kv_full[4];
+    uint64_t kv_empty[4];
+    uint64_t s_full[2];
+    uint64_t p_full[2];
+    uint64_t o_full[2];
+    uint64_t o_free[2];
     uint64_t mma_drained;
     uint32_t tmem_base;
     int abort_flag;
-    int epi_go;
-};
-
-// Description of one key tile of a work unit.
-struct TileInfo {
-    int row0;        // first key row (band/grow: absolute key index; global: compact row)
-    int ncols;       // columns handed to the MMA (multiple of 16)
-    bool global_key; // compact global-key tile
 };
 
 struct Unit {
-    bool grow;       // global-row unit
-    int bh;          // (batch * heads) index
-    int qrow0;       // first query row (band: absolute; grow: compact global row)
-    int split;       // grow: split index
-    int num_band;    // band tiles (or split tiles for grow)
-    int first_k0;    // key index of the first band/split tile
-    int num_gtiles;  // global-key tiles (band units only)
-    int ntiles;
+    bool grow;        // global-row unit
+    bool active[2];   // query tile A / B has work
+    int bh;           // (batch * heads) index
+    int qrow[2];      // first query row of A / B (band: absolute; grow: compact)
+    int ntiles;       // issued key tiles
+    int kstart;       // band: key index of pair tile 0 (= q0 - w)
+    int p_lo;         // band: first issued pair tile
+    int nA;           // band: pair tiles used by each query tile
+    int num_band;     // band: issued band tiles
+    int split;        // grow: split index
+    int k0;           // grow: first key of the split
 };
 
-__device__ __forceinline__ Unit decode_unit(const MainParams& p) {
-    Unit u;
-    int cta = blockIdx.x;
-    if (cta < p.n_grow_ctas) {
-        u.grow = true;
-        u.split = cta % p.n_splits;
-        int rest = cta / p.n_splits;
-        int gt = rest % p.g_tiles;
-        u.bh = rest / p.g_tiles;
-        u.qrow0 = gt * BM;
-        u.first_k0 = u.split * p.split_tiles * BN;
-        int remaining = (p.n - u.first_k0 + BN - 1) / BN;
-        u.num_band = remaining < p.split_tiles ? remaining : p.split_tiles;
-        u.num_gtiles = 0;
+struct Tile {
+    int row0;         // first key row (band/grow: absolute key; global: compact row)
+    int ncols;        // columns of S (multiple of 16)
+    bool global_key;  // compact global-key tile
+    bool mem[2];      // query tile A / B uses this key tile
+};
+
+__device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
+    Unit un;
+    if (u < p.n_grow_units) {
+        un.grow = true;
+        un.split = u % p.n_splits;
+        const int rest = u / p.n_splits;
+        const int gt = rest % p.g_tiles;
+        un.bh = rest / p.g_tiles;
+        un.qrow[0] = un.qrow[1] = gt * BM;
+        un.k0 = un.split * p.split_tiles * BN;
+        const int rem = (p.n - un.k0 + BN - 1) / BN;
+        un.ntiles = rem < p.split_tiles ? rem : p.split_tiles;
+        un.active[0] = true;
+        un.active[1] = un.ntiles >= 2;
+        un.kstart = un.p_lo = un.nA = un.num_band = 0;
     } else {
-        u.grow = false;
-        u.split = 0;
-        int t = cta - p.n_grow_ctas;
-        int qt = t % p.q_tiles;
-        u.bh = t / p.q_tiles;
-        u.qrow0 = qt * BM;
-        // Band span for rows [q0, q0+127] is keys [q0 - w, q0 + 127 + w]: (2w + 128) keys
-        // cut into 128-key tiles starting exactly at q0 - w, so the first and last tiles
-        // carry the triangular band edges.  Tiles wholly outside [0, n) are never issued.
-        long long kstart = (long long)u.qrow0 - p.window;
-        long long span_tiles = ((long long)2 * p.window + BM + BN - 1) / BN;
-        long long t_first = 0;
-        if (kstart < 0) t_first = (-kstart) / BN;  // first tile whose end is > 0
-        long long t_last = span_tiles - 1;
-        long long last_ok = ((long long)p.n - 1 - kstart);
-        if (last_ok / BN < t_last) t_last = last_ok / BN;
-        u.first_k0 = (int)(kstart + t_first * BN);
-        u.num_band = (int)(t_last - t_first + 1);
-        u.num_gtiles = p.g_tiles;
+        un.grow = false;
+        un.split = un.k0 = 0;
+        const int t = u - p.n_grow_units;
+        const int pair = t % p.q_pairs;
+        un.bh = t / p.q_pairs;
+        const int q0 = pair * 2 * BM;
+        un.qrow[0] = q0;
+        un.qrow[1] = q0 + BM;
+        un.active[0] = true;
+        un.active[1] = q0 + BM < p.n;
+        un.kstart = q0 - p.window;
+        un.nA = (2 * p.window + BM + BN - 1) / BN;
+        const int p_first = un.kstart < 0 ? (-un.kstart) / BN : 0;
+        int p_last = un.active[1] ? un.nA : un.nA - 1;
+        const int p_overlap_last = (p.n - 1 - un.kstart) / BN;
+        if (p_overlap_last < p_last) p_last = p_overlap_last;
+        un.p_lo = p_first;
+        un.num_band = p_last - p_first + 1;
+        un.ntiles = un.num_band + p.g_tiles;
     }
-    u.ntiles = u.num_band + u.num_gtiles;
-    return u;
+    return un;
 }
 
-__device__ __forceinline__ TileInfo tile_info(const MainParams& p, const Unit& u, int j) {
-    TileInfo ti;
-    if (j < u.num_band) {
-        ti.row0 = u.first_k0 + j * BN;
-        ti.ncols = BN;
-        ti.global_key = false;
+__device__ __forceinline__ Tile tile_of(const MainParams& p, const Unit& un, int j) {
+    Tile t;
+    if (un.grow) {
+        t.row0 = un.k0 + j * BN;
+        t.ncols = BN;
+        t.global_key = false;
+        t.mem[0] = (j & 1) == 0;
+        t.mem[1] = (j & 1) == 1;
+    } else if (j < un.num_band) {
+        const int pp = un.p_lo + j;
+        t.row0 = un.kstart + pp * BN;
+        t.ncols = BN;
+        t.global_key = false;
+        t.mem[0] = pp <= un.nA - 1;
+        t.mem[1] = un.active[1] && pp >= 1;
     } else {
-        int gt = j - u.num_band;
-        ti.row0 = gt * BN;
+        const int gt = j - un.num_band;
+        t.row0 = gt * BN;
         int cnt = p.num_global - gt * BN;
         if (cnt > BN) cnt = BN;
-        ti.ncols = (cnt + 15) & ~15;
-        ti.global_key = true;
+        t.ncols = (cnt + 15) & ~15;
+        t.global_key = true;
+        t.mem[0] = true;
+        t.mem[1] = un.active[1];
     }
-    return ti;
+    return t;
 }
 
 // All 32 lanes wait; the warp proceeds only if every lane saw the phase complete, so
@@ -184,7 +210,7 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk16) {
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kThreads, Cfg<D, BF16>::kMinBlocks)
+__global__ void __launch_bounds__(kThreads, 1)
     lca_swa_main(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qg,
                  const __grid_constant__ CUtensorMap tm_kg, const __grid_constant__ CUtensorMap tm_vg,
@@ -195,29 +221,32 @@ __global__ void __launch_bounds__(kThreads, Cfg<D, BF16>::kMinBlocks)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + C::kOffQ;
     uint8_t* sSlots = smem + C::kOffSlots;
-    uint8_t* sP = smem + C::kOffP;
     Ctl* ctl = reinterpret_cast<Ctl*>(smem + C::kOffCtl);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const Unit u = decode_unit(p);
     volatile int* abort_flag = &ctl->abort_flag;
+    const int n_units = p.n_grow_units + p.n_band_units;
+    const uint64_t tmo = p.timeout_ns;
 
     if (threadIdx.x == 0) {
-        ptx::mbar_init(&ctl->q_full, 1);
-        for (int s = 0; s < C::kSlots; ++s) {
-            ptx::mbar_init(&ctl->full[s], 1);
-            ptx::mbar_init(&ctl->empty[s], 1);
+        for (int x = 0; x < 2; ++x) {
+            ptx::mbar_init(&ctl->q_full[x], 1);
+            ptx::mbar_init(&ctl->q_empty[x], 1);
+            ptx::mbar_init(&ctl->s_full[x], 1);
+            ptx::mbar_init(&ctl->p_full[x], 4);
+            ptx::mbar_init(&ctl->o_full[x], 1);
+            ptx::mbar_init(&ctl->o_free[x], 4);
         }
-        ptx::mbar_init(&ctl->s_full, 1);
-        ptx::mbar_init(&ctl->s_free, 4);
-        ptx::mbar_init(&ctl->p_full, 4);
-        ptx::mbar_init(&ctl->pv_done, 1);
+        for (int s = 0; s < C::kSlots; ++s) {
+            ptx::mbar_init(&ctl->kv_full[s], 1);
+            ptx::mbar_init(&ctl->kv_empty[s], 1);
+        }
         ptx::mbar_init(&ctl->mma_drained, 1);
         ctl->abort_flag = 0;
         ptx::fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == 9) {
         ptx::tmem_alloc(&ctl->tmem_base, kTmemCols);
         ptx::tmem_relinquish();
     }
@@ -225,327 +254,387 @@ __global__ void __launch_bounds__(kThreads, Cfg<D, BF16>::kMinBlocks)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
-    const uint64_t tmo = p.timeout_ns;
-
-    if (warp == 4) {
-        // ------------------------------------------------------------ TMA producer
+    if (warp >= 8) {
+      ptx::setmaxnreg_dec<kRegsControl>();
+      if (warp == 8) {
+        // ============================================================ TMA producer
         if (ptx::elect_one()) {
-            const CUtensorMap* mq = u.grow ? &tm_qg : &tm_q;
-            ptx::prefetch_tmap(mq);
+            ptx::prefetch_tmap(&tm_q);
             ptx::prefetch_tmap(&tm_k);
             ptx::prefetch_tmap(&tm_v);
-            ptx::mbar_arrive_expect_tx(&ctl->q_full, C::kTileBytes);
-#pragma unroll
-            for (int pn = 0; pn < C::kPanels; ++pn)
-                ptx::tma_load_3d(sQ + pn * kPanelBytes, mq, &ctl->q_full, pn * 64, u.qrow0, u.bh);
-            int issued = 0;
+            int L = 0;       // K/V loads issued
+            int qn = 0;      // Q loads issued per tile buffer
             bool ok = true;
-            for (int j = 0; j < u.ntiles && ok; ++j) {
-                const TileInfo ti = tile_info(p, u, j);
-                for (int kv = 0; kv < 2; ++kv) {
-                    const int idx = 2 * j + kv;
-                    const int slot = idx % C::kSlots;
-                    if (idx >= C::kSlots) {
-                        if (!ptx::mbar_wait(&ctl->empty[slot], ((idx / C::kSlots) + 1) & 1, abort_flag, p.err,
-                                            LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const Unit un = decode_unit(p, u);
+                const CUtensorMap* mq = un.grow ? &tm_qg : &tm_q;
+                for (int x = 0; x < 2 && ok; ++x) {
+                    if (qn > 0 && !ptx::mbar_wait(&ctl->q_empty[x], (qn - 1) & 1, abort_flag, p.err,
+                                                  LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::mbar_arrive_expect_tx(&ctl->q_full[x], C::kTileBytes);
+#pragma unroll
+                    for (int pn = 0; pn < C::kPanels; ++pn)
+                        ptx::tma_load_3d(sQ + x * C::kTileBytes + pn * kPanelBytes, mq, &ctl->q_full[x], pn * 64,
+                                         un.qrow[x], un.bh);
+                }
+                if (!ok) break;
+                ++qn;
+                for (int j = 0; j < un.ntiles && ok; ++j) {
+                    const Tile t = tile_of(p, un, j);
+                    for (int kv = 0; kv < 2; ++kv) {
+                        const int slot = L % C::kSlots;
+                        if (L >= C::kSlots && !ptx::mbar_wait(&ctl->kv_empty[slot], ((L / C::kSlots) + 1) & 1,
+                                                              abort_flag, p.err, LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
                             ok = false;
                             break;
                         }
-                    }
-                    const CUtensorMap* m = ti.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
-                    uint8_t* dst = sSlots + slot * C::kTileBytes;
-                    ptx::mbar_arrive_expect_tx(&ctl->full[slot], C::kTileBytes);
+                        const CUtensorMap* m = t.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
+                        uint8_t* dst = sSlots + slot * C::kTileBytes;
+                        ptx::mbar_arrive_expect_tx(&ctl->kv_full[slot], C::kTileBytes);
 #pragma unroll
-                    for (int pn = 0; pn < C::kPanels; ++pn)
-                        ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->full[slot], pn * 64, ti.row0, u.bh);
-                    ++issued;
+                        for (int pn = 0; pn < C::kPanels; ++pn)
+                            ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64, t.row0, un.bh);
+                        ++L;
+                    }
                 }
             }
-            // Drain: every issued copy must land before the CTA may exit.
-            ptx::mbar_wait(&ctl->q_full, 0, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
-            int first = issued - C::kSlots;
-            if (first < 0) first = 0;
-            for (int idx = first; idx < issued; ++idx)
-                ptx::mbar_wait(&ctl->full[idx % C::kSlots], (idx / C::kSlots) & 1, nullptr, p.err,
+            // Drain: every issued copy lands before the CTA may exit.
+            if (qn > 0)
+                for (int x = 0; x < 2; ++x)
+                    ptx::mbar_wait(&ctl->q_full[x], (qn - 1) & 1, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
+            for (int idx = (L > C::kSlots ? L - C::kSlots : 0); idx < L; ++idx)
+                ptx::mbar_wait(&ctl->kv_full[idx % C::kSlots], (idx / C::kSlots) & 1, nullptr, p.err,
                                LCA_DEVERR_TIMEOUT_DRAIN, tmo);
         }
-    } else if (warp == 5) {
-        // ------------------------------------------------------------ MMA issuer
+      } else if (warp == 9) {
+        // ============================================================ MMA issuer
         if (ptx::elect_one()) {
-            const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, BN, false);
             const uint32_t sq = ptx::smem_u32(sQ);
-            const uint32_t sp = ptx::smem_u32(sP);
             const uint32_t sslots = ptx::smem_u32(sSlots);
-            bool ok = ptx::mbar_wait(&ctl->q_full, 0, abort_flag, p.err, LCA_DEVERR_TIMEOUT_MMA, tmo);
+            const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, BN, false);
+            const uint32_t idesc_pv = ptx::idesc_f16(BF16, BM, D, true);
+            int L = 0, qn = 0;
+            int pc0 = 0, pc1 = 0;   // p_full phases consumed
+            int oc0 = 0, oc1 = 0;   // o_full phases produced
+            bool ok = true;
 
-            auto issue_pv = [&](int j) -> bool {
-                const TileInfo ti = tile_info(p, u, j);
-                const int idx = 2 * j + 1;
-                const int slot = idx % C::kSlots;
-                if (!ptx::mbar_wait(&ctl->full[slot], (idx / C::kSlots) & 1, abort_flag, p.err,
-                                    LCA_DEVERR_TIMEOUT_MMA, tmo))
-                    return false;
-                if (!ptx::mbar_wait(&ctl->p_full, j & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_MMA, tmo))
-                    return false;
-                ptx::tc_fence_after();
-                const uint32_t idesc_pv = ptx::idesc_f16(BF16, BM, D, true);
-                const uint32_t vbase = sslots + slot * C::kTileBytes;
-                const int ksteps = ti.ncols / 16;
-#pragma unroll 1
-                for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
-                    const uint32_t pbase = sp + part * C::kPTileBytes;
-                    for (int kk = 0; kk < ksteps; ++kk) {
-                        const uint64_t adesc =
-                            ptx::smem_desc_sw128(pbase + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 0, 1024);
-                        const uint64_t bdesc = ptx::smem_desc_sw128(vbase + kk * 16 * 128, kPanelBytes, 1024);
-                        ptx::mma_f16_ss(tmem + kOCol, adesc, bdesc, idesc_pv,
-                                        (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
-                    }
-                }
-                ptx::mma_commit(&ctl->pv_done);
-                ptx::mma_commit(&ctl->empty[slot]);
-                return true;
+            auto W = [&](uint64_t* bar, int parity) -> bool {
+                if (!ok) return false;
+                ok = ptx::mbar_wait(bar, (uint32_t)parity & 1u, abort_flag, p.err, LCA_DEVERR_TIMEOUT_MMA, tmo);
+                if (ok) ptx::tc_fence_after();
+                return ok;
             };
-
-            for (int j = 0; j < u.ntiles && ok; ++j) {
-                const TileInfo ti = tile_info(p, u, j);
-                const int idx = 2 * j;
-                const int slot = idx % C::kSlots;
-                if (!ptx::mbar_wait(&ctl->full[slot], (idx / C::kSlots) & 1, abort_flag, p.err,
-                                    LCA_DEVERR_TIMEOUT_MMA, tmo)) {
-                    ok = false;
-                    break;
-                }
-                if (j > 0 &&
-                    !ptx::mbar_wait(&ctl->s_free, (j - 1) & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_MMA, tmo)) {
-                    ok = false;
-                    break;
-                }
-                ptx::tc_fence_after();
-                const uint32_t idesc_s = (ti.ncols == BN) ? idesc_s_full : ptx::idesc_f16(BF16, BM, ti.ncols, false);
+            auto issue_s = [&](int x, int slot, int ncols) {
+                const uint32_t idesc = (ncols == BN) ? idesc_s_full : ptx::idesc_f16(BF16, BM, ncols, false);
                 const uint32_t kbase = sslots + slot * C::kTileBytes;
+                const uint32_t qbase = sq + x * C::kTileBytes;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
                     const uint32_t off = (ks >> 2) * kPanelBytes + (ks & 3) * 32;
-                    const uint64_t adesc = ptx::smem_desc_sw128(sq + off, 0, 1024);
-                    const uint64_t bdesc = ptx::smem_desc_sw128(kbase + off, 0, 1024);
-                    ptx::mma_f16_ss(tmem + kSCol, adesc, bdesc, idesc_s, ks > 0 ? 1u : 0u);
+                    ptx::mma_f16_ss(tmem + x * 128, ptx::smem_desc_sw128(qbase + off, 0, 1024),
+                                    ptx::smem_desc_sw128(kbase + off, 0, 1024), idesc, ks > 0 ? 1u : 0u);
                 }
-                ptx::mma_commit(&ctl->s_full);
-                ptx::mma_commit(&ctl->empty[slot]);
-                if (j > 0 && !issue_pv(j - 1)) {
-                    ok = false;
-                    break;
+            };
+            auto issue_pv = [&](int x, int slot, int ncols, bool first) {
+                const uint32_t vbase = sslots + slot * C::kTileBytes;
+                const int ksteps = ncols / 16;
+#pragma unroll 1
+                for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
+                    for (int kk = 0; kk < ksteps; ++kk) {
+                        const uint64_t bdesc = ptx::smem_desc_sw128(vbase + kk * 16 * 128, kPanelBytes, 1024);
+                        ptx::mma_f16_ts(tmem + C::kOCol + x * D, tmem + x * 128 + part * 64 + kk * 8, bdesc,
+                                        idesc_pv, (!first || part > 0 || kk > 0) ? 1u : 0u);
+                    }
+                }
+            };
+
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const Unit un = decode_unit(p, u);
+                // Last key tile of each query tile: its S MMA is the last reader of that Q
+                // buffer, so the buffer is released to the producer right after it.
+                int last_s0 = -1, last_s1 = -1;
+                for (int j = 0; j < un.ntiles; ++j) {
+                    const Tile t = tile_of(p, un, j);
+                    if (t.mem[0]) last_s0 = j;
+                    if (t.mem[1]) last_s1 = j;
+                }
+                if (!W(&ctl->q_full[0], qn) || !W(&ctl->q_full[1], qn)) break;
+                ++qn;
+                if (last_s0 < 0) ptx::mma_commit(&ctl->q_empty[0]);
+                if (last_s1 < 0) ptx::mma_commit(&ctl->q_empty[1]);
+                auto s_and_release = [&](const int x, int slot, int ncols, int jj) {
+                    issue_s(x, slot, ncols);
+                    ptx::mma_commit(&ctl->s_full[x]);
+                    if (jj == (x ? last_s1 : last_s0)) ptx::mma_commit(&ctl->q_empty[x]);
+                };
+                bool first_pv0 = true, first_pv1 = true;
+                {
+                    const Tile t0 = tile_of(p, un, 0);
+                    if (!W(&ctl->kv_full[L % C::kSlots], L / C::kSlots)) break;
+                    if (t0.mem[0]) s_and_release(0, L % C::kSlots, t0.ncols, 0);
+                    if (t0.mem[1]) s_and_release(1, L % C::kSlots, t0.ncols, 0);
+                    ptx::mma_commit(&ctl->kv_empty[L % C::kSlots]);
+                }
+                for (int j = 0; j < un.ntiles && ok; ++j) {
+                    const Tile t = tile_of(p, un, j);
+                    const int lv = L + 2 * j + 1;
+                    const int lk = lv + 1;
+                    const bool has_next = j + 1 < un.ntiles;
+                    Tile tn = t;
+                    if (!W(&ctl->kv_full[lv % C::kSlots], lv / C::kSlots)) break;
+                    if (has_next) {
+                        tn = tile_of(p, un, j + 1);
+                        if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
+                    }
+                    auto step = [&](const int x, const bool mem_now, const bool mem_next, int& pcx, const int ocx,
+                                    bool& firstx) {
+                        if (mem_now && ok) {
+                            if (!W(&ctl->p_full[x], pcx)) return;
+                            ++pcx;
+                            if (firstx && ocx > 0 && !W(&ctl->o_free[x], ocx - 1)) return;
+                            issue_pv(x, lv % C::kSlots, t.ncols, firstx);
+                            firstx = false;
+                        }
+                        if (has_next && mem_next && ok) s_and_release(x, lk % C::kSlots, tn.ncols, j + 1);
+                    };
+                    step(0, t.mem[0], tn.mem[0], pc0, oc0, first_pv0);
+                    step(1, t.mem[1], tn.mem[1], pc1, oc1, first_pv1);
+                    if (!ok) break;
+                    ptx::mma_commit(&ctl->kv_empty[lv % C::kSlots]);
+                    if (has_next) ptx::mma_commit(&ctl->kv_empty[lk % C::kSlots]);
+                }
+                if (!ok) break;
+                L += 2 * un.ntiles;
+                if (!first_pv0) {
+                    ptx::mma_commit(&ctl->o_full[0]);
+                    ++oc0;
+                }
+                if (!first_pv1) {
+                    ptx::mma_commit(&ctl->o_full[1]);
+                    ++oc1;
                 }
             }
-            if (ok && u.ntiles > 0) issue_pv(u.ntiles - 1);
             // Drain: all tcgen05 ops issued by this thread complete before TMEM is freed.
             ptx::mma_commit(&ctl->mma_drained);
             ptx::mbar_wait(&ctl->mma_drained, 0, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
         }
+      }
     } else {
-        // ------------------------------------------------------------ softmax warps
-        const int r = threadIdx.x;  // row within the tile == TMEM lane
-        const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
-        const int qi = u.qrow0 + r;  // band: absolute query row
+        ptx::setmaxnreg_inc<kRegsSoftmax>();
+        // ============================================================ softmax warpgroups
+        const int X = warp >> 2;          // query tile of this warpgroup
+        const int wq = warp & 3;          // TMEM lane quarter
+        const int r = wq * 32 + lane;     // row within the tile == TMEM lane
+        const int bar_id = 1 + X;
+        const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+        const uint32_t s_col = X * 128;
+        const uint32_t o_col = C::kOCol + X * D;
+        uint8_t* stage = smem + C::kOffStage + X * C::kStageBytes;
+        // scale * log2(e) (the host passes a tiny positive value for scale == 0 so that
+        // visible scores stay finite and masked ones still map to -inf)
         const float sl2 = p.scale_log2;
-        const uint32_t sp = ptx::smem_u32(sP);
-        float m = -INFINITY;  // reference max (log2 units)
-        float l = 0.f;
-        bool ok = true;
-        int j = 0;
-        for (; j < u.ntiles; ++j) {
-            const TileInfo ti = tile_info(p, u, j);
-            if (!warp_wait(&ctl->s_full, j & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo)) {
-                ok = false;
-                break;
-            }
-            ptx::tc_fence_after();
-            float s[BN];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                if (c * 32 < ti.ncols) {
-                    float tmp[32];
-                    ptx::tmem_ld32(t_lane + kSCol + c * 32, tmp);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) s[c * 32 + e] = tmp[e];
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) s[c * 32 + e] = 0.f;
-                }
-            }
-            ptx::tmem_wait_ld();
-            ptx::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&ctl->s_free);
+        const bool neg_scale = sl2 < 0.f;
+        const float sent = neg_scale ? INFINITY : -INFINITY;
+        int sc = 0, oc = 0;
+        bool ok = true;   // warp-uniform; on failure the warp keeps the barrier schedule but skips work
 
-            // ---- mask + scale into log2 units
-            float mt = -INFINITY;
-            if (!ti.global_key) {
-                // visible columns kk in [lo, hi]
-                int lo, hi;
-                if (u.grow) {
-                    lo = 0;
-                    hi = p.n - 1 - ti.row0;
-                } else {
-                    int jlo = qi - p.window;
-                    if (jlo < 0) jlo = 0;
-                    long long jhi = (long long)qi + p.window;
-                    if (jhi > p.n - 1) jhi = p.n - 1;
-                    lo = jlo - ti.row0;
-                    hi = (int)(jhi - ti.row0);
-                }
-                if (lo <= 0 && hi >= BN - 1) {
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+            const Unit un = decode_unit(p, u);
+            const bool active_x = X ? un.active[1] : un.active[0];
+            if (!active_x) continue;
+            const int qrow_x = X ? un.qrow[1] : un.qrow[0];
+            const int qi = qrow_x + r;
+            const bool live = un.grow ? (qi < p.num_global) : (qi < p.n);
+            const bool warp_live = __any_sync(0xffffffffu, live);
+            float m = -INFINITY;  // reference max (log2 units)
+            float l = 0.f;
+            bool seen = false;    // a previous member tile of this unit was processed
+            for (int j = 0; j < un.ntiles; ++j) {
+                const Tile t = tile_of(p, un, j);
+                if (!(X ? t.mem[1] : t.mem[0])) continue;
+                if (ok) ok = warp_wait(&ctl->s_full[X], sc & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+                ++sc;
+                if (ok && warp_live) {
+                    ptx::tc_fence_after();
+                    float s[BN];
 #pragma unroll
-                    for (int c = 0; c < BN; ++c) {
-                        s[c] *= sl2;
-                        mt = fmaxf(mt, s[c]);
-                    }
-                } else {
+                    for (int c = 0; c < 4; ++c) {
+                        if (c * 32 < t.ncols) {
+                            float tmp[32];
+                            ptx::tmem_ld32(t_lane + s_col + c * 32, tmp);
 #pragma unroll
-                    for (int c = 0; c < BN; ++c) {
-                        const bool vis = (c >= lo) && (c <= hi);
-                        s[c] = vis ? s[c] * sl2 : -INFINITY;
-                        mt = fmaxf(mt, s[c]);
-                    }
-                }
-            } else {
-                const int gbase = ti.row0;
-                const int gcnt = p.num_global - gbase;
+                            for (int e = 0; e < 32; ++e) s[c * 32 + e] = tmp[e];
+                        } else {
 #pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    bool vis = false;
-                    if (c < gcnt) {
-                        const int g = __ldg(p.gidx + gbase + c);
-                        const int dlt = qi - g;
-                        vis = (dlt > p.window) || (dlt < -p.window);
+                            for (int e = 0; e < 32; ++e) s[c * 32 + e] = 0.f;
+                        }
                     }
-                    s[c] = vis ? s[c] * sl2 : -INFINITY;
-                    mt = fmaxf(mt, s[c]);
-                }
-            }
+                    ptx::tmem_wait_ld();
+                    // ---- mask: masked scores become `sent`, which the scale maps to -inf
+                    if (t.global_key) {
+                        // Globals inside this row's band form a contiguous run [c_lo, c_hi) of
+                        // the sorted list; the others (c < gcnt) are visible here.
+                        const int gcnt = p.num_global - t.row0 < BN ? p.num_global - t.row0 : BN;
+                        const int* gi = p.gidx + t.row0;
+                        int a = 0, b = gcnt;  // first c with g_c >= qi - w
+                        while (a < b) {
+                            const int mid = (a + b) >> 1;
+                            if (__ldg(gi + mid) < qi - p.window) a = mid + 1; else b = mid;
+                        }
+                        const int c_lo = a;
+                        b = gcnt;             // first c with g_c > qi + w
+                        while (a < b) {
+                            const int mid = (a + b) >> 1;
+                            if (__ldg(gi + mid) <= qi + p.window) a = mid + 1; else b = mid;
+                        }
+                        const int c_hi = a;
+#pragma unroll
+                        for (int c = 0; c < BN; ++c) s[c] = (c < gcnt && (c < c_lo || c >= c_hi)) ? s[c] : sent;
+                    } else {
+                        int lo, hi;  // visible columns [lo, hi]
+                        if (un.grow) {
+                            lo = 0;
+                            hi = p.n - 1 - t.row0;
+                        } else {
+                            const int jlo = qi - p.window > 0 ? qi - p.window : 0;
+                            const int jhi = (qi + p.window < p.n - 1) ? qi + p.window : p.n - 1;
+                            lo = jlo - t.row0;
+                            hi = jhi - t.row0;
+                        }
+                        if (__any_sync(0xffffffffu, lo > 0 || hi < BN - 1)) {
+#pragma unroll
+                            for (int c = 0; c < BN; ++c) s[c] = (c >= lo && c <= hi) ? s[c] : sent;
+                        }
+                    }
+                    // ---- row max of the scaled scores: max (or min, for a negative scale) of raw s
+                    float mr = sent;
+                    if (!neg_scale) {
+#pragma unroll
+                        for (int c = 0; c < BN; c += 2) mr = ptx::fmax3(mr, s[c], s[c + 1]);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < BN; c += 2) mr = ptx::fmin3(mr, s[c], s[c + 1]);
+                    }
+                    const float mt = (mr == sent) ? -INFINITY : mr * sl2;
 
-            // ---- online softmax with lazy rescale
-            float alpha = 1.f;
-            bool rescale = false;
-            if (mt > m + kRescaleThreshold || (m == -INFINITY && mt > -INFINITY)) {
-                const float m_new = mt;
-                alpha = (m == -INFINITY) ? 0.f : ptx::ex2(m - m_new);
-                rescale = (m != -INFINITY);
-                m = m_new;
-                l *= alpha;
-            }
-            const float m_use = (m == -INFINITY) ? 0.f : m;
-            float lsum = 0.f;
+                    // ---- online softmax with lazy rescale (O_X is stable: see header)
+                    bool rescale = false;
+                    float alpha = 1.f;
+                    if (mt > m + kRescaleThreshold || (m == -INFINITY && mt > -INFINITY)) {
+                        rescale = seen && (m != -INFINITY);
+                        alpha = (m == -INFINITY) ? 0.f : ptx::ex2(m - mt);
+                        m = mt;
+                        l *= alpha;
+                    }
+                    if (__any_sync(0xffffffffu, rescale)) {
+                        const float a = rescale ? alpha : 1.f;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                s[c] = ptx::ex2(s[c] - m_use);
-                lsum += s[c];
-            }
-            l += lsum;
+                        for (int c = 0; c < D / 32; ++c) {
+                            float o[32];
+                            ptx::tmem_ld32(t_lane + o_col + c * 32, o);
+                            ptx::tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) o[e] *= a;
+                            ptx::tmem_st32(t_lane + o_col + c * 32, o);
+                        }
+                    }
+                    // ---- p = 2^(s * scale * log2(e) - m), row sum
+                    const float neg_m = (m == -INFINITY) ? 0.f : -m;
+                    float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+                    for (int c = 0; c < BN; c += 2) {
+                        s[c] = ptx::ex2(fmaf(s[c], sl2, neg_m));
+                        s[c + 1] = ptx::ex2(fmaf(s[c + 1], sl2, neg_m));
+                        l0 += s[c];
+                        l1 += s[c + 1];
+                    }
+                    l += l0 + l1;
 
-            // ---- P buffer and O are in use by PV_{j-1} until it completes
-            if (j > 0) {
-                if (!warp_wait(&ctl->pv_done, (j - 1) & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo)) {
-                    ok = false;
-                    break;
-                }
-                ptx::tc_fence_after();
-                if (__any_sync(0xffffffffu, rescale)) {
-                    const float a = rescale ? alpha : 1.f;
+                    // ---- P into S's TMEM columns: 16-bit pairs, hi part at [0,64), lo at [64,128)
 #pragma unroll
-                    for (int c = 0; c < D / 32; ++c) {
-                        float o[32];
-                        ptx::tmem_ld32(t_lane + kOCol + c * 32, o);
-                        ptx::tmem_wait_ld();
+                    for (int h = 0; h < 4; ++h) {
+                        uint32_t w[16];
+                        if (BF16) {
+                            uint32_t lo[16];
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] *= a;
-                        ptx::tmem_st32(t_lane + kOCol + c * 32, o);
+                            for (int e = 0; e < 16; ++e) {
+                                const float a = s[h * 32 + 2 * e], b = s[h * 32 + 2 * e + 1];
+                                w[e] = ptx::pack_bf16x2(a, b);
+                                lo[e] = ptx::pack_bf16x2(a - __uint_as_float(w[e] << 16),
+                                                         b - __uint_as_float(w[e] & 0xFFFF0000u));
+                            }
+                            ptx::tmem_st16u(t_lane + s_col + 64 + h * 16, lo);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) w[e] = ptx::pack_f16x2(s[h * 32 + 2 * e], s[h * 32 + 2 * e + 1]);
+                        }
+                        ptx::tmem_st16u(t_lane + s_col + h * 16, w);
                     }
                     ptx::tmem_wait_st();
                 }
+                seen = true;
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&ctl->p_full[X]);
             }
-            // ---- write P (row r, keys 0..127) into the swizzled K-major P buffer(s)
-#pragma unroll
-            for (int cc = 0; cc < BN / 8; ++cc) {
-                const uint32_t off = (cc >> 3) * kPanelBytes + swz128(r, cc & 7);
-                uint32_t w[4];
-                if (BF16) {
-                    uint32_t lo[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float a = s[cc * 8 + 2 * e], b = s[cc * 8 + 2 * e + 1];
-                        w[e] = ptx::pack_bf16x2(a, b);
-                        const float ha = __uint_as_float(w[e] << 16);
-                        const float hb = __uint_as_float(w[e] & 0xFFFF0000u);
-                        lo[e] = ptx::pack_bf16x2(a - ha, b - hb);
-                    }
-                    ptx::st_shared_v4(sp + C::kPTileBytes + off, lo[0], lo[1], lo[2], lo[3]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) w[e] = ptx::pack_f16x2(s[cc * 8 + 2 * e], s[cc * 8 + 2 * e + 1]);
-                }
-                ptx::st_shared_v4(sp + off, w[0], w[1], w[2], w[3]);
-            }
-            ptx::fence_proxy_async_smem();
-            ptx::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&ctl->p_full);
-        }
 
-        // ---- wait for the last PV, then decide CTA-uniformly (among the softmax warps)
-        // whether to run the epilogue: it contains named barriers, so either all four
-        // warps enter it or none does.
-        if (ok && u.ntiles > 0)
-            warp_wait(&ctl->pv_done, (u.ntiles - 1) & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
-        ptx::named_bar_sync(1, kSoftmaxThreads);
-        if (threadIdx.x == 0) ctl->epi_go = (*abort_flag == 0) ? 1 : 0;
-        ptx::named_bar_sync(1, kSoftmaxThreads);
-
-        // ---- epilogue: O / l -> fp32 via swizzled staging panels + TMA store
-        if (ctl->epi_go && u.ntiles > 0) {
-            ptx::tc_fence_after();
+            // ---- epilogue: O / l -> fp32 rows via swizzled staging panels + TMA store
+            if (ok) ok = warp_wait(&ctl->o_full[X], oc & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+            ++oc;
+            if (ok) ptx::tc_fence_after();
+            // staging from the previous unit must have been read by its TMA stores
+            if (r == 0) ptx::tma_store_wait_read<0>();
+            ptx::named_bar_sync(bar_id, kWgThreads);
             const float inv_l = 1.f / l;
-            const CUtensorMap* mo = u.grow ? &tm_po : &tm_o;
-            const int oz = u.grow ? (u.split * p.bh + u.bh) : u.bh;
+            const CUtensorMap* mo = un.grow ? &tm_po : &tm_o;
+            const int oz = un.grow ? ((2 * un.split + X) * p.bh + un.bh) : un.bh;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
-                uint8_t* stage = sP + (c & 1) * kPanelBytes;
+                uint8_t* panel = stage + (c & 1) * kPanelBytes;
                 if (c >= 2) {
-                    if (threadIdx.x == 0) ptx::tma_store_wait_read<1>();
-                    ptx::named_bar_sync(1, kSoftmaxThreads);
+                    if (r == 0) ptx::tma_store_wait_read<1>();
+                    ptx::named_bar_sync(bar_id, kWgThreads);
                 }
-                float o[32];
-                ptx::tmem_ld32(t_lane + kOCol + c * 32, o);
-                ptx::tmem_wait_ld();
-                const uint32_t sbase = ptx::smem_u32(stage);
+                if (ok) {
+                    float o[32];
+                    ptx::tmem_ld32(t_lane + o_col + c * 32, o);
+                    ptx::tmem_wait_ld();
+                    const uint32_t sbase = ptx::smem_u32(panel);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    ptx::st_shared_v4(sbase + swz128(r, q), __float_as_uint(o[q * 4 + 0] * inv_l),
-                                      __float_as_uint(o[q * 4 + 1] * inv_l), __float_as_uint(o[q * 4 + 2] * inv_l),
-                                      __float_as_uint(o[q * 4 + 3] * inv_l));
+                    for (int q = 0; q < 8; ++q)
+                        ptx::st_shared_v4(sbase + swz128(r, q), __float_as_uint(o[q * 4 + 0] * inv_l),
+                                          __float_as_uint(o[q * 4 + 1] * inv_l), __float_as_uint(o[q * 4 + 2] * inv_l),
+                                          __float_as_uint(o[q * 4 + 3] * inv_l));
                 }
                 ptx::fence_proxy_async_smem();
-                ptx::named_bar_sync(1, kSoftmaxThreads);
-                if (threadIdx.x == 0) {
-                    ptx::tma_store_3d(mo, stage, c * 32, u.qrow0, oz);
+                ptx::named_bar_sync(bar_id, kWgThreads);
+                if (r == 0 && ok) {
+                    ptx::tma_store_3d(mo, panel, c * 32, qrow_x, oz);
                     ptx::tma_store_commit();
                 }
             }
-            const float lse = (((m == -INFINITY) ? 0.f : m) + __log2f(l)) * kLn2;
-            if (u.grow) {
-                p.part_lse[((size_t)u.split * p.bh + u.bh) * p.gpad + u.qrow0 + r] = lse;
-            } else if (p.lse != nullptr && qi < p.n) {
-                p.lse[(size_t)u.bh * p.n + qi] = lse;
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&ctl->o_free[X]);
+            if (ok) {
+                const float lse = (((m == -INFINITY) ? 0.f : m) + __log2f(l)) * kLn2;
+                if (un.grow) {
+                    p.part_lse[((size_t)(2 * un.split + X) * p.bh + un.bh) * p.gpad + qi] = lse;
+                } else if (p.lse != nullptr && qi < p.n) {
+                    p.lse[(size_t)un.bh * p.n + qi] = lse;
+                }
             }
-            if (threadIdx.x == 0) ptx::tma_store_wait_all();
         }
+        if (r == 0) ptx::tma_store_wait_all();
     }
 
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
-    if (warp == 5) ptx::tmem_dealloc(tmem, kTmemCols);
+    if (warp == 9) ptx::tmem_dealloc(tmem, kTmemCols);
 }
 
 // ------------------------------------------------------------------------ gather
@@ -582,27 +671,37 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
 
 template <int D>
 __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp) {
-    // one warp per (bh, global row)
+    // one warp per (bh, global row); partial 2*s + x covers the key tiles of split s
+    // with parity x, and exists only if that split has more than x tiles
     const long long w = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= (long long)cp.num_global * cp.bh) return;
     const int g = (int)(w % cp.num_global);
     const int bh = (int)(w / cp.num_global);
     constexpr int kPer = D / 32;
+    const int n_parts = 2 * cp.n_splits;
+    auto valid = [&](int part) {
+        const int s = part >> 1;
+        const int first_key = s * cp.split_tiles * 128;
+        int tiles = (cp.n - first_key + 127) / 128;
+        if (tiles > cp.split_tiles) tiles = cp.split_tiles;
+        return tiles > (part & 1);
+    };
     float mx = -INFINITY;
-    for (int s = 0; s < cp.n_splits; ++s)
-        mx = fmaxf(mx, cp.part_lse[((size_t)s * cp.bh + bh) * cp.gpad + g]);
+    for (int s = 0; s < n_parts; ++s)
+        if (valid(s)) mx = fmaxf(mx, cp.part_lse[((size_t)s * cp.bh + bh) * cp.gpad + g]);
     float acc[kPer];
 #pragma unroll
     for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
     float wsum = 0.f;
-    for (int s = 0; s < cp.n_splits; ++s) {
+    for (int s = 0; s < n_parts; ++s) {
+        if (!valid(s)) continue;
         const size_t prow = (size_t)s * cp.bh + bh;
-        const float w = __expf(cp.part_lse[prow * cp.gpad + g] - mx);
-        wsum += w;
+        const float wt = __expf(cp.part_lse[prow * cp.gpad + g] - mx);
+        wsum += wt;
         const float* po = cp.part_o + (prow * cp.gpad + g) * D;
 #pragma unroll
-        for (int e = 0; e < kPer; ++e) acc[e] += w * po[lane + 32 * e];
+        for (int e = 0; e < kPer; ++e) acc[e] += wt * po[lane + 32 * e];
     }
     const int row = cp.gidx[g];
     float* out = cp.o + ((size_t)bh * cp.n + row) * D;

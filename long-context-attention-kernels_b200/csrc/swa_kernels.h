@@ -25,7 +25,7 @@ struct TensorMaps {
     CUtensorMap q, k, v;     // inputs [bh][n][d] (bf16 / f16), box 64 x 128 rows, 128B swizzle
     CUtensorMap qg, kg, vg;  // compact global rows [bh][gpad][d]
     CUtensorMap o;           // output [bh][n][d] fp32, box 32 x 128 rows, 128B swizzle
-    CUtensorMap po;          // global-row partial outputs [splits*bh][gpad][d] fp32
+    CUtensorMap po;          // global-row partial outputs [2*splits*bh][gpad][d] fp32
 };
 
 struct MainParams {
@@ -38,11 +38,13 @@ struct MainParams {
     int gpad;         // g_tiles * 128
     int n_splits;     // key splits per (bh, global tile)
     int split_tiles;  // key tiles per split
-    int n_grow_ctas;  // bh * g_tiles * n_splits
+    int n_grow_units; // bh * g_tiles * n_splits global-row units (scheduled first)
+    int n_band_units; // bh * q_pairs band units
+    int q_pairs;      // ceil(q_tiles / 2): band units per (batch, head)
     float scale_log2; // scale * log2(e)
     const int* gidx;  // [gpad] sorted global indices (padding = INT_MAX)
     float* lse;       // [bh][n] natural-log LSE, or nullptr
-    float* part_lse;  // [n_splits][bh][gpad]
+    float* part_lse;  // [2 * n_splits][bh][gpad]
     int* err;         // device error word (first error wins)
     unsigned long long timeout_ns;  // per-wait budget
 };
@@ -56,7 +58,7 @@ struct GatherParams {
 };
 
 struct CombineParams {
-    int n, bh, gpad, num_global, n_splits;
+    int n, bh, gpad, num_global, n_splits, split_tiles;
     const int* gidx;
     const float* part_o;
     const float* part_lse;

@@ -67,7 +67,7 @@ class CABI:
         lib.lca_normalize_global_tokens.argtypes = [ctypes.POINTER(i64), i64, i64, ctypes.POINTER(ctypes.c_int32),
                                                     ctypes.POINTER(i64)]
         lib.lca_swa_workspace_size.restype = ctypes.c_int
-        lib.lca_swa_workspace_size.argtypes = [i64, i64, i64, i64, i64, ctypes.c_int, ctypes.POINTER(sz)]
+        lib.lca_swa_workspace_size.argtypes = [i64, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.POINTER(sz)]
         lib.lca_swa_forward.restype = ctypes.c_int
         lib.lca_swa_forward.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64, ctypes.c_float,
                                         ctypes.POINTER(i64), i64, vp, sz, vp]
@@ -88,9 +88,9 @@ class CABI:
         st = self.lib.lca_normalize_global_tokens(arr, n, seq_len, out, ctypes.byref(cnt))
         return st, [out[i] for i in range(cnt.value)]
 
-    def workspace_size(self, batch, heads, seq_len, head_dim, num_unique_global, dtype) -> tuple[int, int]:
+    def workspace_size(self, batch, heads, seq_len, head_dim, window, num_unique_global, dtype) -> tuple[int, int]:
         out = ctypes.c_size_t(0)
-        st = self.lib.lca_swa_workspace_size(batch, heads, seq_len, head_dim, num_unique_global, dtype,
+        st = self.lib.lca_swa_workspace_size(batch, heads, seq_len, head_dim, window, num_unique_global, dtype,
                                              ctypes.byref(out))
         return st, out.value
 
