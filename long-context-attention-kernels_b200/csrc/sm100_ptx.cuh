@@ -58,32 +58,33 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+// One potentially-suspending probe: the thread sleeps in hardware until the phase
+// completes or `suspend_ns` elapse, so waiting warps do not spin on issue slots.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity, uint32_t suspend_ns) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar_addr), "r"(parity)
+        : "r"(bar_addr), "r"(parity), "r"(suspend_ns)
         : "memory");
     return ok != 0;
 }
 
 // Bounded wait on phase `parity` of `bar`.  `abort_flag` is a CTA-shared word: once
-// any role of the CTA gives up, every other wait returns false promptly.  On timeout
-// the CTA-wide abort flag and the device-wide error word are set.
+// any role of the CTA gives up, every other wait returns false promptly (within one
+// suspend period).  On timeout the CTA-wide abort flag and the device-wide error word
+// are set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err_word, int err_code, uint64_t timeout_ns) {
+    constexpr uint32_t kSuspendNs = 1000000;  // 1 ms per hardware sleep
     const uint32_t addr = smem_u32(bar);
-#pragma unroll 1
-    for (int i = 0; i < 256; ++i) {
-        if (mbar_try_wait(addr, parity)) return true;
-    }
+    if (mbar_try_wait(addr, parity, kSuspendNs)) return true;
     const uint64_t t0 = global_timer_ns();
 #pragma unroll 1
     while (true) {
-        if (mbar_try_wait(addr, parity)) return true;
+        if (mbar_try_wait(addr, parity, kSuspendNs)) return true;
         if (abort_flag != nullptr && *abort_flag) return false;
         if (global_timer_ns() - t0 > timeout_ns) {
             if (abort_flag != nullptr) *abort_flag = 1;

@@ -27,21 +27,24 @@
 //   3. lca_combine_global_rows : log-sum-exp merge of the partials, written over the
 //                           global rows of O (and LSE).
 //
-// Main-kernel CTA layout (384 threads, launched at 168 registers per thread):
-//   warps 0-3  softmax + epilogue of query tile A (thread r <-> row r <-> TMEM lane r)
-//   warps 4-7  softmax + epilogue of query tile B
-//   warp 8     TMA producer: Q_A, Q_B per unit, then K_j / V_j into a ring of slots
-//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 10-11 idle
-// Register split (setmaxnreg): warpgroup 2 drops to 72, warpgroups 0-1 rise to 216;
-// 128*72 + 256*216 = 384*168, the launch allocation.
-// TMEM (512 columns): S_A [0,128), S_B [128,256), O_A [256, 256+d), O_B [256+d, 256+2d).
-// P overwrites S in place (packed 16-bit pairs) and feeds P*V as the TMEM A operand.
-// MMA issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one
-// tile's softmax runs, the tensor cores work for the other.  tcgen05 ops issued by one
-// thread execute in order, so S_X(j+1) never overwrites P_X(j) before PV_X(j) read it,
-// and the commit that signals S_X(j+1) also covers PV_X(j), so O_X is stable whenever
-// its softmax warps see a new S.
+// Main-kernel CTA layout.  Each query tile X (A or B) is served by H softmax warpgroups
+// (H = 2 for d = 64, 1 for d = 128); warpgroup (X, h) owns key columns
+// [128h/H, 128(h+1)/H) of every S tile of X and runs an independent online softmax over
+// them into its own accumulator O_{X,h}; the H partial results of a row are merged by
+// log-sum-exp in the epilogue.  Thread r of a warpgroup <-> query row r <-> TMEM lane r.
+//   d = 64 : warps 0-15 softmax (A0, A1, B0, B1), warp 16 TMA producer, warp 17 MMA
+//            (576 threads, no register split)
+//   d = 128: warps 0-7 softmax (A, B), warp 8 TMA, warp 9 MMA, warps 10-11 idle
+//            (384 threads; setmaxnreg: warpgroup 2 drops to 72 registers, warpgroups 0-1
+//            rise to 216; 128*72 + 256*216 = 384*168, the launch allocation)
+// TMEM (512 columns): S_A [0,128), S_B [128,256), then O_{A,0..H-1}, O_{B,0..H-1}, d each.
+// P overwrites S in place: warpgroup (X, h) writes its 16-bit P (hi pairs, then lo pairs
+// for bf16) into its own S columns, and P*V reads it as the TMEM A operand.
+// MMA issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one tile's
+// softmax runs, the tensor cores work for the other.  tcgen05 ops issued by one thread
+// execute in order, so S_X(j+1) never overwrites P_X(j) before PV_X(j) read it, and the
+// commit that signals S_X(j+1) also covers PV_X(j), so O_X is stable whenever its softmax
+// warps see a new S.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -61,11 +64,6 @@ namespace {
 
 constexpr int BM = 128;            // query rows per tile == TMEM lanes
 constexpr int BN = 128;            // keys per tile
-constexpr int kThreads = 384;
-constexpr int kRegsLaunch = 168;
-constexpr int kRegsSoftmax = 216;
-constexpr int kRegsControl = 72;
-static_assert(128 * kRegsControl + 256 * kRegsSoftmax == kThreads * kRegsLaunch, "register split");
 constexpr int kWgThreads = 128;
 constexpr int kTmemCols = 512;
 constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 bytes: one swizzle panel
@@ -81,17 +79,31 @@ constexpr float kRescaleThreshold = 8.0f;
 template <int D, bool BF16>
 struct Cfg {
     static constexpr bool kSplitP = BF16;
+    static constexpr int kHalves = 1;                      // softmax warpgroups per query tile
+    static constexpr int kCols = BN / kHalves;             // S columns per softmax thread
+    static constexpr int kSoftmaxWarps = 8 * kHalves;
+    static constexpr int kTmaWarp = kSoftmaxWarps;
+    static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+    static constexpr bool kRegSplit = (kHalves == 1);
+    static constexpr int kThreads = kRegSplit ? 384 : (kSoftmaxWarps + 2) * 32;
+    static constexpr int kRegsLaunch = 168, kRegsSoftmax = 216, kRegsControl = 72;
+    static constexpr int kEpiCols = D / kHalves;           // output columns per warpgroup
     static constexpr int kPanels = D / 64;
     static constexpr int kTileBytes = BM * D * 2;
     static constexpr int kSlots = (D == 64) ? 4 : 3;
-    static constexpr int kStageBytes = 2 * kPanelBytes;  // per softmax warpgroup
+    static constexpr int kStageBytes = 2 * kPanelBytes / kHalves;  // per softmax warpgroup
     static constexpr int kOffQ = 0;
     static constexpr int kOffSlots = kOffQ + 2 * kTileBytes;
     static constexpr int kOffStage = kOffSlots + kSlots * kTileBytes;
-    static constexpr int kOffCtl = kOffStage + 2 * kStageBytes;
+    static constexpr int kOffCtl = kOffStage + 2 * kHalves * kStageBytes;
     static constexpr int kCtlBytes = 1024;
-    static constexpr int kSmemBytes = kOffCtl + kCtlBytes + 1024;  // +1024 for base alignment
+    static constexpr int kOffXchg = kOffCtl + kCtlBytes;    // (m, l) rows exchanged by the halves
+    static constexpr int kXchgBytes = (kHalves == 2) ? 2 * 2 * 2 * 128 * 2 * 4 : 0;
+    static constexpr int kSmemBytes = kOffXchg + kXchgBytes + 1024;  // +1024 for base alignment
     static constexpr int kOCol = 256;
+    static_assert(!kRegSplit || 128 * kRegsControl + 256 * kRegsSoftmax == kThreads * kRegsLaunch,
+                  "register split must match the launch allocation");
+    static_assert(kOCol + 2 * kHalves * D <= kTmemCols, "TMEM columns");
 };
 
 struct Ctl {
@@ -210,13 +222,15 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk16) {
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
     lca_swa_main(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qg,
                  const __grid_constant__ CUtensorMap tm_kg, const __grid_constant__ CUtensorMap tm_vg,
                  const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_po,
                  const MainParams p) {
     using C = Cfg<D, BF16>;
+    constexpr int H = C::kHalves;
+    constexpr int KC = C::kCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + C::kOffQ;
@@ -234,9 +248,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&ctl->q_full[x], 1);
             ptx::mbar_init(&ctl->q_empty[x], 1);
             ptx::mbar_init(&ctl->s_full[x], 1);
-            ptx::mbar_init(&ctl->p_full[x], 4);
+            ptx::mbar_init(&ctl->p_full[x], 4 * H);
             ptx::mbar_init(&ctl->o_full[x], 1);
-            ptx::mbar_init(&ctl->o_free[x], 4);
+            ptx::mbar_init(&ctl->o_free[x], 4 * H);
         }
         for (int s = 0; s < C::kSlots; ++s) {
             ptx::mbar_init(&ctl->kv_full[s], 1);
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ctl->abort_flag = 0;
         ptx::fence_mbar_init();
     }
-    if (warp == 9) {
+    if (warp == C::kMmaWarp) {
         ptx::tmem_alloc(&ctl->tmem_base, kTmemCols);
         ptx::tmem_relinquish();
     }
@@ -254,192 +268,208 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
-    if (warp >= 8) {
-      ptx::setmaxnreg_dec<kRegsControl>();
-      if (warp == 8) {
-        // ============================================================ TMA producer
-        if (ptx::elect_one()) {
-            ptx::prefetch_tmap(&tm_q);
-            ptx::prefetch_tmap(&tm_k);
-            ptx::prefetch_tmap(&tm_v);
-            int L = 0;       // K/V loads issued
-            int qn = 0;      // Q loads issued per tile buffer
-            bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const Unit un = decode_unit(p, u);
-                const CUtensorMap* mq = un.grow ? &tm_qg : &tm_q;
-                for (int x = 0; x < 2 && ok; ++x) {
-                    if (qn > 0 && !ptx::mbar_wait(&ctl->q_empty[x], (qn - 1) & 1, abort_flag, p.err,
-                                                  LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
-                        ok = false;
-                        break;
-                    }
-                    ptx::mbar_arrive_expect_tx(&ctl->q_full[x], C::kTileBytes);
-#pragma unroll
-                    for (int pn = 0; pn < C::kPanels; ++pn)
-                        ptx::tma_load_3d(sQ + x * C::kTileBytes + pn * kPanelBytes, mq, &ctl->q_full[x], pn * 64,
-                                         un.qrow[x], un.bh);
-                }
-                if (!ok) break;
-                ++qn;
-                for (int j = 0; j < un.ntiles && ok; ++j) {
-                    const Tile t = tile_of(p, un, j);
-                    for (int kv = 0; kv < 2; ++kv) {
-                        const int slot = L % C::kSlots;
-                        if (L >= C::kSlots && !ptx::mbar_wait(&ctl->kv_empty[slot], ((L / C::kSlots) + 1) & 1,
-                                                              abort_flag, p.err, LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
+
+    if (warp >= C::kSoftmaxWarps) {
+        if constexpr (C::kRegSplit) ptx::setmaxnreg_dec<C::kRegsControl>();
+        if (warp == C::kTmaWarp) {
+            // ======================================================== TMA producer
+            if (ptx::elect_one()) {
+                ptx::prefetch_tmap(&tm_q);
+                ptx::prefetch_tmap(&tm_k);
+                ptx::prefetch_tmap(&tm_v);
+                int L = 0;   // K/V loads issued
+                int qn = 0;  // Q loads issued per tile buffer
+                bool ok = true;
+                for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                    const Unit un = decode_unit(p, u);
+                    const CUtensorMap* mq = un.grow ? &tm_qg : &tm_q;
+                    for (int x = 0; x < 2 && ok; ++x) {
+                        if (qn > 0 && !ptx::mbar_wait(&ctl->q_empty[x], (qn - 1) & 1, abort_flag, p.err,
+                                                      LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
                             ok = false;
                             break;
                         }
-                        const CUtensorMap* m = t.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
-                        uint8_t* dst = sSlots + slot * C::kTileBytes;
-                        ptx::mbar_arrive_expect_tx(&ctl->kv_full[slot], C::kTileBytes);
+                        ptx::mbar_arrive_expect_tx(&ctl->q_full[x], C::kTileBytes);
 #pragma unroll
                         for (int pn = 0; pn < C::kPanels; ++pn)
-                            ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64, t.row0, un.bh);
-                        ++L;
+                            ptx::tma_load_3d(sQ + x * C::kTileBytes + pn * kPanelBytes, mq, &ctl->q_full[x],
+                                             pn * 64, x ? un.qrow[1] : un.qrow[0], un.bh);
                     }
-                }
-            }
-            // Drain: every issued copy lands before the CTA may exit.
-            if (qn > 0)
-                for (int x = 0; x < 2; ++x)
-                    ptx::mbar_wait(&ctl->q_full[x], (qn - 1) & 1, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
-            for (int idx = (L > C::kSlots ? L - C::kSlots : 0); idx < L; ++idx)
-                ptx::mbar_wait(&ctl->kv_full[idx % C::kSlots], (idx / C::kSlots) & 1, nullptr, p.err,
-                               LCA_DEVERR_TIMEOUT_DRAIN, tmo);
-        }
-      } else if (warp == 9) {
-        // ============================================================ MMA issuer
-        if (ptx::elect_one()) {
-            const uint32_t sq = ptx::smem_u32(sQ);
-            const uint32_t sslots = ptx::smem_u32(sSlots);
-            const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, BN, false);
-            const uint32_t idesc_pv = ptx::idesc_f16(BF16, BM, D, true);
-            int L = 0, qn = 0;
-            int pc0 = 0, pc1 = 0;   // p_full phases consumed
-            int oc0 = 0, oc1 = 0;   // o_full phases produced
-            bool ok = true;
-
-            auto W = [&](uint64_t* bar, int parity) -> bool {
-                if (!ok) return false;
-                ok = ptx::mbar_wait(bar, (uint32_t)parity & 1u, abort_flag, p.err, LCA_DEVERR_TIMEOUT_MMA, tmo);
-                if (ok) ptx::tc_fence_after();
-                return ok;
-            };
-            auto issue_s = [&](int x, int slot, int ncols) {
-                const uint32_t idesc = (ncols == BN) ? idesc_s_full : ptx::idesc_f16(BF16, BM, ncols, false);
-                const uint32_t kbase = sslots + slot * C::kTileBytes;
-                const uint32_t qbase = sq + x * C::kTileBytes;
-#pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t off = (ks >> 2) * kPanelBytes + (ks & 3) * 32;
-                    ptx::mma_f16_ss(tmem + x * 128, ptx::smem_desc_sw128(qbase + off, 0, 1024),
-                                    ptx::smem_desc_sw128(kbase + off, 0, 1024), idesc, ks > 0 ? 1u : 0u);
-                }
-            };
-            auto issue_pv = [&](int x, int slot, int ncols, bool first) {
-                const uint32_t vbase = sslots + slot * C::kTileBytes;
-                const int ksteps = ncols / 16;
-#pragma unroll 1
-                for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
-                    for (int kk = 0; kk < ksteps; ++kk) {
-                        const uint64_t bdesc = ptx::smem_desc_sw128(vbase + kk * 16 * 128, kPanelBytes, 1024);
-                        ptx::mma_f16_ts(tmem + C::kOCol + x * D, tmem + x * 128 + part * 64 + kk * 8, bdesc,
-                                        idesc_pv, (!first || part > 0 || kk > 0) ? 1u : 0u);
-                    }
-                }
-            };
-
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const Unit un = decode_unit(p, u);
-                // Last key tile of each query tile: its S MMA is the last reader of that Q
-                // buffer, so the buffer is released to the producer right after it.
-                int last_s0 = -1, last_s1 = -1;
-                for (int j = 0; j < un.ntiles; ++j) {
-                    const Tile t = tile_of(p, un, j);
-                    if (t.mem[0]) last_s0 = j;
-                    if (t.mem[1]) last_s1 = j;
-                }
-                if (!W(&ctl->q_full[0], qn) || !W(&ctl->q_full[1], qn)) break;
-                ++qn;
-                if (last_s0 < 0) ptx::mma_commit(&ctl->q_empty[0]);
-                if (last_s1 < 0) ptx::mma_commit(&ctl->q_empty[1]);
-                auto s_and_release = [&](const int x, int slot, int ncols, int jj) {
-                    issue_s(x, slot, ncols);
-                    ptx::mma_commit(&ctl->s_full[x]);
-                    if (jj == (x ? last_s1 : last_s0)) ptx::mma_commit(&ctl->q_empty[x]);
-                };
-                bool first_pv0 = true, first_pv1 = true;
-                {
-                    const Tile t0 = tile_of(p, un, 0);
-                    if (!W(&ctl->kv_full[L % C::kSlots], L / C::kSlots)) break;
-                    if (t0.mem[0]) s_and_release(0, L % C::kSlots, t0.ncols, 0);
-                    if (t0.mem[1]) s_and_release(1, L % C::kSlots, t0.ncols, 0);
-                    ptx::mma_commit(&ctl->kv_empty[L % C::kSlots]);
-                }
-                for (int j = 0; j < un.ntiles && ok; ++j) {
-                    const Tile t = tile_of(p, un, j);
-                    const int lv = L + 2 * j + 1;
-                    const int lk = lv + 1;
-                    const bool has_next = j + 1 < un.ntiles;
-                    Tile tn = t;
-                    if (!W(&ctl->kv_full[lv % C::kSlots], lv / C::kSlots)) break;
-                    if (has_next) {
-                        tn = tile_of(p, un, j + 1);
-                        if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
-                    }
-                    auto step = [&](const int x, const bool mem_now, const bool mem_next, int& pcx, const int ocx,
-                                    bool& firstx) {
-                        if (mem_now && ok) {
-                            if (!W(&ctl->p_full[x], pcx)) return;
-                            ++pcx;
-                            if (firstx && ocx > 0 && !W(&ctl->o_free[x], ocx - 1)) return;
-                            issue_pv(x, lv % C::kSlots, t.ncols, firstx);
-                            firstx = false;
-                        }
-                        if (has_next && mem_next && ok) s_and_release(x, lk % C::kSlots, tn.ncols, j + 1);
-                    };
-                    step(0, t.mem[0], tn.mem[0], pc0, oc0, first_pv0);
-                    step(1, t.mem[1], tn.mem[1], pc1, oc1, first_pv1);
                     if (!ok) break;
-                    ptx::mma_commit(&ctl->kv_empty[lv % C::kSlots]);
-                    if (has_next) ptx::mma_commit(&ctl->kv_empty[lk % C::kSlots]);
+                    ++qn;
+                    for (int j = 0; j < un.ntiles && ok; ++j) {
+                        const Tile t = tile_of(p, un, j);
+                        for (int kv = 0; kv < 2; ++kv) {
+                            const int slot = L % C::kSlots;
+                            if (L >= C::kSlots &&
+                                !ptx::mbar_wait(&ctl->kv_empty[slot], ((L / C::kSlots) + 1) & 1, abort_flag, p.err,
+                                                LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
+                                ok = false;
+                                break;
+                            }
+                            const CUtensorMap* m = t.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
+                            uint8_t* dst = sSlots + slot * C::kTileBytes;
+                            ptx::mbar_arrive_expect_tx(&ctl->kv_full[slot], C::kTileBytes);
+#pragma unroll
+                            for (int pn = 0; pn < C::kPanels; ++pn)
+                                ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64, t.row0,
+                                                 un.bh);
+                            ++L;
+                        }
+                    }
                 }
-                if (!ok) break;
-                L += 2 * un.ntiles;
-                if (!first_pv0) {
-                    ptx::mma_commit(&ctl->o_full[0]);
-                    ++oc0;
-                }
-                if (!first_pv1) {
-                    ptx::mma_commit(&ctl->o_full[1]);
-                    ++oc1;
-                }
+                // Drain: every issued copy lands before the CTA may exit.
+                if (qn > 0)
+                    for (int x = 0; x < 2; ++x)
+                        ptx::mbar_wait(&ctl->q_full[x], (qn - 1) & 1, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
+                for (int idx = (L > C::kSlots ? L - C::kSlots : 0); idx < L; ++idx)
+                    ptx::mbar_wait(&ctl->kv_full[idx % C::kSlots], (idx / C::kSlots) & 1, nullptr, p.err,
+                                   LCA_DEVERR_TIMEOUT_DRAIN, tmo);
             }
-            // Drain: all tcgen05 ops issued by this thread complete before TMEM is freed.
-            ptx::mma_commit(&ctl->mma_drained);
-            ptx::mbar_wait(&ctl->mma_drained, 0, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
+        } else if (warp == C::kMmaWarp) {
+            // ======================================================== MMA issuer
+            if (ptx::elect_one()) {
+                const uint32_t sq = ptx::smem_u32(sQ);
+                const uint32_t sslots = ptx::smem_u32(sSlots);
+                const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, BN, false);
+                const uint32_t idesc_pv = ptx::idesc_f16(BF16, BM, D, true);
+                int L = 0, qn = 0;
+                int pc0 = 0, pc1 = 0;  // p_full phases consumed
+                int oc0 = 0, oc1 = 0;  // o_full phases produced
+                bool ok = true;
+
+                auto W = [&](uint64_t* bar, int parity) -> bool {
+                    if (!ok) return false;
+                    ok = ptx::mbar_wait(bar, (uint32_t)parity & 1u, abort_flag, p.err, LCA_DEVERR_TIMEOUT_MMA, tmo);
+                    if (ok) ptx::tc_fence_after();
+                    return ok;
+                };
+                auto issue_s = [&](int x, int slot, int ncols) {
+                    const uint32_t idesc = (ncols == BN) ? idesc_s_full : ptx::idesc_f16(BF16, BM, ncols, false);
+                    const uint32_t kbase = sslots + slot * C::kTileBytes;
+                    const uint32_t qbase = sq + x * C::kTileBytes;
+#pragma unroll
+                    for (int ks = 0; ks < D / 16; ++ks) {
+                        const uint32_t off = (ks >> 2) * kPanelBytes + (ks & 3) * 32;
+                        ptx::mma_f16_ss(tmem + x * 128, ptx::smem_desc_sw128(qbase + off, 0, 1024),
+                                        ptx::smem_desc_sw128(kbase + off, 0, 1024), idesc, ks > 0 ? 1u : 0u);
+                    }
+                };
+                // O_x += P_x V.  P_x lives in S_x's TMEM columns: keys [32c, 32c + 32) of
+                // the tile occupy columns [32c, 32c + 32), hi pairs in the first 16 and, for
+                // bf16, lo pairs in the next 16 (two 16-bit elements per 32-bit column).
+                auto issue_pv = [&](int x, int slot, int ncols, bool first) {
+                    const uint32_t vbase = sslots + slot * C::kTileBytes;
+                    const uint32_t dcol = tmem + C::kOCol + x * D;
+                    const int ksteps = ncols / 16;
+#pragma unroll 1
+                    for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
+                        for (int kk = 0; kk < ksteps; ++kk) {
+                            const uint32_t acol = tmem + x * 128 + (kk >> 1) * 32 + part * 16 + (kk & 1) * 8;
+                            const uint64_t bdesc = ptx::smem_desc_sw128(vbase + kk * 16 * 128, kPanelBytes, 1024);
+                            ptx::mma_f16_ts(dcol, acol, bdesc, idesc_pv, (!first || part > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    }
+                };
+
+                for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                    const Unit un = decode_unit(p, u);
+                    // Last key tile of each query tile: its S MMA is the last reader of that Q
+                    // buffer, so the buffer is released to the producer right after it.
+                    int last_s0 = -1, last_s1 = -1;
+                    for (int j = 0; j < un.ntiles; ++j) {
+                        const Tile t = tile_of(p, un, j);
+                        if (t.mem[0]) last_s0 = j;
+                        if (t.mem[1]) last_s1 = j;
+                    }
+                    if (!W(&ctl->q_full[0], qn) || !W(&ctl->q_full[1], qn)) break;
+                    ++qn;
+                    if (last_s0 < 0) ptx::mma_commit(&ctl->q_empty[0]);
+                    if (last_s1 < 0) ptx::mma_commit(&ctl->q_empty[1]);
+                    auto s_and_release = [&](const int x, int slot, int ncols, int jj) {
+                        issue_s(x, slot, ncols);
+                        ptx::mma_commit(&ctl->s_full[x]);
+                        if (jj == (x ? last_s1 : last_s0)) ptx::mma_commit(&ctl->q_empty[x]);
+                    };
+                    bool first_pv0 = true, first_pv1 = true;
+                    {
+                        const Tile t0 = tile_of(p, un, 0);
+                        if (!W(&ctl->kv_full[L % C::kSlots], L / C::kSlots)) break;
+                        if (t0.mem[0]) s_and_release(0, L % C::kSlots, t0.ncols, 0);
+                        if (t0.mem[1]) s_and_release(1, L % C::kSlots, t0.ncols, 0);
+                        ptx::mma_commit(&ctl->kv_empty[L % C::kSlots]);
+                    }
+                    for (int j = 0; j < un.ntiles && ok; ++j) {
+                        const Tile t = tile_of(p, un, j);
+                        const int lv = L + 2 * j + 1;
+                        const int lk = lv + 1;
+                        const bool has_next = j + 1 < un.ntiles;
+                        const Tile tn = has_next ? tile_of(p, un, j + 1) : t;
+                        if (!W(&ctl->kv_full[lv % C::kSlots], lv / C::kSlots)) break;
+                        bool k_next_ready = false;  // K_{j+1} is awaited right before its first use
+                        auto step = [&](const int x, const bool mem_now, const bool mem_next, int& pcx,
+                                        const int ocx, bool& firstx) {
+                            if (mem_now && ok) {
+                                if (!W(&ctl->p_full[x], pcx)) return;
+                                ++pcx;
+                                if (firstx && ocx > 0 && !W(&ctl->o_free[x], ocx - 1)) return;
+                                issue_pv(x, lv % C::kSlots, t.ncols, firstx);
+                                firstx = false;
+                            }
+                            if (has_next && mem_next && ok) {
+                                if (!k_next_ready) {
+                                    if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) return;
+                                    k_next_ready = true;
+                                }
+                                s_and_release(x, lk % C::kSlots, tn.ncols, j + 1);
+                            }
+                        };
+                        step(0, t.mem[0], tn.mem[0], pc0, oc0, first_pv0);
+                        step(1, t.mem[1], tn.mem[1], pc1, oc1, first_pv1);
+                        if (!ok) break;
+                        ptx::mma_commit(&ctl->kv_empty[lv % C::kSlots]);
+                        // every issued tile has a member, so K_{j+1} was consumed above
+                        if (has_next) ptx::mma_commit(&ctl->kv_empty[lk % C::kSlots]);
+                    }
+                    if (!ok) break;
+                    L += 2 * un.ntiles;
+                    if (!first_pv0) {
+                        ptx::mma_commit(&ctl->o_full[0]);
+                        ++oc0;
+                    }
+                    if (!first_pv1) {
+                        ptx::mma_commit(&ctl->o_full[1]);
+                        ++oc1;
+                    }
+                }
+                // Drain: all tcgen05 ops issued by this thread complete before TMEM is freed.
+                ptx::mma_commit(&ctl->mma_drained);
+                ptx::mbar_wait(&ctl->mma_drained, 0, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
+            }
         }
-      }
     } else {
-        ptx::setmaxnreg_inc<kRegsSoftmax>();
+        if constexpr (C::kRegSplit) ptx::setmaxnreg_inc<C::kRegsSoftmax>();
         // ============================================================ softmax warpgroups
-        const int X = warp >> 2;          // query tile of this warpgroup
+        const int sw = warp >> 2;         // softmax warpgroup
+        const int X = sw / H;             // query tile of this warpgroup
+        const int hh = sw % H;            // key-column half of this warpgroup
         const int wq = warp & 3;          // TMEM lane quarter
         const int r = wq * 32 + lane;     // row within the tile == TMEM lane
-        const int bar_id = 1 + X;
+        const int tile_bar = 1 + X;       // named barrier: all warpgroups of tile X
+        const int wg_bar = 3 + sw;        // named barrier: this warpgroup
         const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
-        const uint32_t s_col = X * 128;
-        const uint32_t o_col = C::kOCol + X * D;
-        uint8_t* stage = smem + C::kOffStage + X * C::kStageBytes;
+        const uint32_t s_col = X * 128 + KC * hh;            // this warpgroup's S / P columns
+        const uint32_t o_col = C::kOCol + (X * H + hh) * D;  // this warpgroup's accumulator
+        const uint32_t o_col0 = C::kOCol + (X * H) * D;      // accumulator of half 0 of tile X
+        uint8_t* stage = smem + C::kOffStage + sw * C::kStageBytes;
+        float* xchg = reinterpret_cast<float*>(smem + C::kOffXchg);
         // scale * log2(e) (the host passes a tiny positive value for scale == 0 so that
         // visible scores stay finite and masked ones still map to -inf)
         const float sl2 = p.scale_log2;
         const bool neg_scale = sl2 < 0.f;
         const float sent = neg_scale ? INFINITY : -INFINITY;
         int sc = 0, oc = 0;
-        bool ok = true;   // warp-uniform; on failure the warp keeps the barrier schedule but skips work
+        bool ok = true;  // warp-uniform; on failure the warp keeps the barrier schedule but skips work
 
         for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
             const Unit un = decode_unit(p, u);
@@ -449,6 +479,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int qi = qrow_x + r;
             const bool live = un.grow ? (qi < p.num_global) : (qi < p.n);
             const bool warp_live = __any_sync(0xffffffffu, live);
+            // row's visible keys in band / split tiles: [jlo, jhi] (absolute key index)
+            int jlo = 0, jhi = p.n - 1;
+            // run [g_lo, g_hi) of sorted global indices inside the row's band (band units)
+            int g_lo = 0, g_hi = 0;
+            if (!un.grow) {
+                jlo = qi - p.window > 0 ? qi - p.window : 0;
+                jhi = (qi + p.window < p.n - 1) ? qi + p.window : p.n - 1;
+                if (p.g_tiles > 0) {
+                    int a = 0, b = p.num_global;
+                    while (a < b) {
+                        const int mid = (a + b) >> 1;
+                        if (__ldg(p.gidx + mid) < qi - p.window) a = mid + 1; else b = mid;
+                    }
+                    g_lo = a;
+                    b = p.num_global;
+                    while (a < b) {
+                        const int mid = (a + b) >> 1;
+                        if (__ldg(p.gidx + mid) <= qi + p.window) a = mid + 1; else b = mid;
+                    }
+                    g_hi = a;
+                }
+            }
             float m = -INFINITY;  // reference max (log2 units)
             float l = 0.f;
             bool seen = false;    // a previous member tile of this unit was processed
@@ -457,70 +509,68 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!(X ? t.mem[1] : t.mem[0])) continue;
                 if (ok) ok = warp_wait(&ctl->s_full[X], sc & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
                 ++sc;
-                if (ok && warp_live) {
+                const int col0 = t.row0 + KC * hh;  // key (band) or compact global row of column 0
+                const int ncols_h = t.ncols - KC * hh;
+                if (ok && warp_live && ncols_h > 0) {
                     ptx::tc_fence_after();
+                    // visible columns of this row in this tile: [lo, hi] minus the hole [h_lo, h_hi)
+                    int lo, hi, h_lo = 0, h_hi = 0;
+                    if (t.global_key) {
+                        lo = 0;
+                        hi = p.num_global - 1 - col0;
+                        h_lo = g_lo - col0;
+                        h_hi = g_hi - col0;
+                    } else {
+                        lo = jlo - col0;
+                        hi = jhi - col0;
+                    }
+                    if (hi > t.ncols - 1) hi = t.ncols - 1;
+                    const int nchunks = (t.ncols + 31) >> 5;
+                    // ---- pass 1: S row into registers, masked row max
                     float s[BN];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        if (c * 32 < t.ncols) {
+                        if (c < nchunks) {
                             float tmp[32];
                             ptx::tmem_ld32(t_lane + s_col + c * 32, tmp);
 #pragma unroll
                             for (int e = 0; e < 32; ++e) s[c * 32 + e] = tmp[e];
                         } else {
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) s[c * 32 + e] = 0.f;
+                            for (int e = 0; e < 32; ++e) s[c * 32 + e] = sent;
                         }
                     }
+                    const bool need = lo > 0 || hi < BN - 1 || (h_lo < h_hi && h_hi > 0 && h_lo < BN);
+                    const bool any_mask = __any_sync(0xffffffffu, need);
                     ptx::tmem_wait_ld();
-                    // ---- mask: masked scores become `sent`, which the scale maps to -inf
-                    if (t.global_key) {
-                        // Globals inside this row's band form a contiguous run [c_lo, c_hi) of
-                        // the sorted list; the others (c < gcnt) are visible here.
-                        const int gcnt = p.num_global - t.row0 < BN ? p.num_global - t.row0 : BN;
-                        const int* gi = p.gidx + t.row0;
-                        int a = 0, b = gcnt;  // first c with g_c >= qi - w
-                        while (a < b) {
-                            const int mid = (a + b) >> 1;
-                            if (__ldg(gi + mid) < qi - p.window) a = mid + 1; else b = mid;
-                        }
-                        const int c_lo = a;
-                        b = gcnt;             // first c with g_c > qi + w
-                        while (a < b) {
-                            const int mid = (a + b) >> 1;
-                            if (__ldg(gi + mid) <= qi + p.window) a = mid + 1; else b = mid;
-                        }
-                        const int c_hi = a;
+                    if (any_mask) {
 #pragma unroll
-                        for (int c = 0; c < BN; ++c) s[c] = (c < gcnt && (c < c_lo || c >= c_hi)) ? s[c] : sent;
-                    } else {
-                        int lo, hi;  // visible columns [lo, hi]
-                        if (un.grow) {
-                            lo = 0;
-                            hi = p.n - 1 - t.row0;
-                        } else {
-                            const int jlo = qi - p.window > 0 ? qi - p.window : 0;
-                            const int jhi = (qi + p.window < p.n - 1) ? qi + p.window : p.n - 1;
-                            lo = jlo - t.row0;
-                            hi = jhi - t.row0;
-                        }
-                        if (__any_sync(0xffffffffu, lo > 0 || hi < BN - 1)) {
-#pragma unroll
-                            for (int c = 0; c < BN; ++c) s[c] = (c >= lo && c <= hi) ? s[c] : sent;
-                        }
+                        for (int c = 0; c < BN; ++c)
+                            s[c] = (c >= lo && c <= hi && (c < h_lo || c >= h_hi)) ? s[c] : sent;
                     }
-                    // ---- row max of the scaled scores: max (or min, for a negative scale) of raw s
-                    float mr = sent;
+                    float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
                     if (!neg_scale) {
 #pragma unroll
-                        for (int c = 0; c < BN; c += 2) mr = ptx::fmax3(mr, s[c], s[c + 1]);
+                        for (int c = 0; c < BN; c += 8) {
+                            r0 = ptx::fmax3(r0, s[c + 0], s[c + 1]);
+                            r1 = ptx::fmax3(r1, s[c + 2], s[c + 3]);
+                            r2 = ptx::fmax3(r2, s[c + 4], s[c + 5]);
+                            r3 = ptx::fmax3(r3, s[c + 6], s[c + 7]);
+                        }
                     } else {
 #pragma unroll
-                        for (int c = 0; c < BN; c += 2) mr = ptx::fmin3(mr, s[c], s[c + 1]);
+                        for (int c = 0; c < BN; c += 8) {
+                            r0 = ptx::fmin3(r0, s[c + 0], s[c + 1]);
+                            r1 = ptx::fmin3(r1, s[c + 2], s[c + 3]);
+                            r2 = ptx::fmin3(r2, s[c + 4], s[c + 5]);
+                            r3 = ptx::fmin3(r3, s[c + 6], s[c + 7]);
+                        }
                     }
+                    const float mr =
+                        neg_scale ? fminf(fminf(r0, r1), fminf(r2, r3)) : fmaxf(fmaxf(r0, r1), fmaxf(r2, r3));
                     const float mt = (mr == sent) ? -INFINITY : mr * sl2;
 
-                    // ---- online softmax with lazy rescale (O_X is stable: see header)
+                    // ---- online softmax with lazy rescale (O is stable: see header)
                     bool rescale = false;
                     float alpha = 1.f;
                     if (mt > m + kRescaleThreshold || (m == -INFINITY && mt > -INFINITY)) {
@@ -531,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (__any_sync(0xffffffffu, rescale)) {
                         const float a = rescale ? alpha : 1.f;
-#pragma unroll
+#pragma unroll 1
                         for (int c = 0; c < D / 32; ++c) {
                             float o[32];
                             ptx::tmem_ld32(t_lane + o_col + c * 32, o);
@@ -541,38 +591,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ptx::tmem_st32(t_lane + o_col + c * 32, o);
                         }
                     }
-                    // ---- p = 2^(s * scale * log2(e) - m), row sum
+                    // ---- pass 2, one 32-key chunk at a time (S re-read from TMEM): p = 2^(s *
+                    // scale * log2(e) - m), row sum, 16-bit pairs written over the chunk's own
+                    // S columns (hi pairs, then lo pairs for bf16)
                     const float neg_m = (m == -INFINITY) ? 0.f : -m;
-                    float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-                    for (int c = 0; c < BN; c += 2) {
-                        s[c] = ptx::ex2(fmaf(s[c], sl2, neg_m));
-                        s[c + 1] = ptx::ex2(fmaf(s[c + 1], sl2, neg_m));
-                        l0 += s[c];
-                        l1 += s[c + 1];
-                    }
-                    l += l0 + l1;
-
-                    // ---- P into S's TMEM columns: 16-bit pairs, hi part at [0,64), lo at [64,128)
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) {
+                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 1
+                    for (int c = 0; c < nchunks; ++c) {
+                        const int c0 = c * 32;
+                        const bool in_none = hi < c0 || lo > c0 + 31 || (h_lo <= c0 && h_hi > c0 + 31);
+                        const bool in_full = lo <= c0 && hi >= c0 + 31 && (h_hi <= c0 || h_lo > c0 + 31);
                         uint32_t w[16];
-                        if (BF16) {
-                            uint32_t lo[16];
+                        uint32_t wl[16];
+                        if (__all_sync(0xffffffffu, in_none)) {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) w[e] = wl[e] = 0u;
+                        } else {
+                            float v[32];
+                            ptx::tmem_ld32(t_lane + s_col + c0, v);
+                            const bool part = !__all_sync(0xffffffffu, in_full);
+                            ptx::tmem_wait_ld();
+                            if (part) {
+#pragma unroll
+                                for (int e = 0; e < 32; ++e) {
+                                    const int col = c0 + e;
+                                    v[e] = (col >= lo && col <= hi && (col < h_lo || col >= h_hi)) ? v[e] : sent;
+                                }
+                            }
+#pragma unroll
+                            for (int e = 0; e < 32; e += 4) {
+                                v[e + 0] = ptx::ex2(fmaf(v[e + 0], sl2, neg_m));
+                                v[e + 1] = ptx::ex2(fmaf(v[e + 1], sl2, neg_m));
+                                v[e + 2] = ptx::ex2(fmaf(v[e + 2], sl2, neg_m));
+                                v[e + 3] = ptx::ex2(fmaf(v[e + 3], sl2, neg_m));
+                                a0 += v[e + 0];
+                                a1 += v[e + 1];
+                                a2 += v[e + 2];
+                                a3 += v[e + 3];
+                            }
 #pragma unroll
                             for (int e = 0; e < 16; ++e) {
-                                const float a = s[h * 32 + 2 * e], b = s[h * 32 + 2 * e + 1];
-                                w[e] = ptx::pack_bf16x2(a, b);
-                                lo[e] = ptx::pack_bf16x2(a - __uint_as_float(w[e] << 16),
-                                                         b - __uint_as_float(w[e] & 0xFFFF0000u));
+                                if (BF16) {
+                                    w[e] = ptx::pack_bf16x2(v[2 * e], v[2 * e + 1]);
+                                    wl[e] = ptx::pack_bf16x2(v[2 * e] - __uint_as_float(w[e] << 16),
+                                                             v[2 * e + 1] - __uint_as_float(w[e] & 0xFFFF0000u));
+                                } else {
+                                    w[e] = ptx::pack_f16x2(v[2 * e], v[2 * e + 1]);
+                                }
                             }
-                            ptx::tmem_st16u(t_lane + s_col + 64 + h * 16, lo);
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < 16; ++e) w[e] = ptx::pack_f16x2(s[h * 32 + 2 * e], s[h * 32 + 2 * e + 1]);
                         }
-                        ptx::tmem_st16u(t_lane + s_col + h * 16, w);
+                        ptx::tmem_st16u(t_lane + s_col + c0, w);
+                        if (BF16) ptx::tmem_st16u(t_lane + s_col + c0 + 16, wl);
                     }
+                    l += (a0 + a1) + (a2 + a3);
                     ptx::tmem_wait_st();
                 }
                 seen = true;
@@ -581,46 +652,73 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) ptx::mbar_arrive(&ctl->p_full[X]);
             }
 
-            // ---- epilogue: O / l -> fp32 rows via swizzled staging panels + TMA store
+            // ---- epilogue: merge the halves, O / l -> fp32 rows via staging + TMA store
             if (ok) ok = warp_wait(&ctl->o_full[X], oc & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
-            ++oc;
             if (ok) ptx::tc_fence_after();
-            // staging from the previous unit must have been read by its TMA stores
+            float M = m, Lsum = l, w_own = 1.f, w_oth = 0.f;
+            if constexpr (H == 2) {
+                float* xb = xchg + (((oc & 1) * 2 + X) * 2) * 256;  // [half][row][2]
+                xb[(hh * 128 + r) * 2 + 0] = m;
+                xb[(hh * 128 + r) * 2 + 1] = l;
+                ptx::named_bar_sync(tile_bar, H * kWgThreads);
+                const float mo = xb[((1 - hh) * 128 + r) * 2 + 0];
+                const float lo2 = xb[((1 - hh) * 128 + r) * 2 + 1];
+                M = fmaxf(m, mo);
+                w_own = (m == -INFINITY) ? 0.f : ptx::ex2(m - M);
+                w_oth = (mo == -INFINITY) ? 0.f : ptx::ex2(mo - M);
+                Lsum = l * w_own + lo2 * w_oth;
+            }
+            ++oc;
+            // staging from this warpgroup's previous unit must have been read by its TMA stores
             if (r == 0) ptx::tma_store_wait_read<0>();
-            ptx::named_bar_sync(bar_id, kWgThreads);
-            const float inv_l = 1.f / l;
+            ptx::named_bar_sync(wg_bar, kWgThreads);
+            const float inv_l = 1.f / Lsum;
+            // weights of the half-0 and half-1 accumulators for this row
+            const float w0 = (hh == 0) ? w_own : w_oth;
+            const float w1 = (hh == 0) ? w_oth : w_own;
             const CUtensorMap* mo = un.grow ? &tm_po : &tm_o;
             const int oz = un.grow ? ((2 * un.split + X) * p.bh + un.bh) : un.bh;
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < C::kEpiCols / 32; ++c) {
+                const int ocol = hh * C::kEpiCols + c * 32;  // output column of this chunk
                 uint8_t* panel = stage + (c & 1) * kPanelBytes;
                 if (c >= 2) {
                     if (r == 0) ptx::tma_store_wait_read<1>();
-                    ptx::named_bar_sync(bar_id, kWgThreads);
+                    ptx::named_bar_sync(wg_bar, kWgThreads);
                 }
                 if (ok) {
                     float o[32];
-                    ptx::tmem_ld32(t_lane + o_col + c * 32, o);
-                    ptx::tmem_wait_ld();
+                    ptx::tmem_ld32(t_lane + o_col0 + ocol, o);
+                    if constexpr (H == 2) {
+                        float o1[32];
+                        ptx::tmem_ld32(t_lane + o_col0 + D + ocol, o1);
+                        ptx::tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = (o[e] * w0 + o1[e] * w1) * inv_l;
+                    } else {
+                        ptx::tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] *= inv_l;
+                    }
                     const uint32_t sbase = ptx::smem_u32(panel);
 #pragma unroll
                     for (int q = 0; q < 8; ++q)
-                        ptx::st_shared_v4(sbase + swz128(r, q), __float_as_uint(o[q * 4 + 0] * inv_l),
-                                          __float_as_uint(o[q * 4 + 1] * inv_l), __float_as_uint(o[q * 4 + 2] * inv_l),
-                                          __float_as_uint(o[q * 4 + 3] * inv_l));
+                        ptx::st_shared_v4(sbase + swz128(r, q), __float_as_uint(o[q * 4 + 0]),
+                                          __float_as_uint(o[q * 4 + 1]), __float_as_uint(o[q * 4 + 2]),
+                                          __float_as_uint(o[q * 4 + 3]));
                 }
                 ptx::fence_proxy_async_smem();
-                ptx::named_bar_sync(bar_id, kWgThreads);
+                ptx::named_bar_sync(wg_bar, kWgThreads);
                 if (r == 0 && ok) {
-                    ptx::tma_store_3d(mo, panel, c * 32, qrow_x, oz);
+                    ptx::tma_store_3d(mo, panel, ocol, qrow_x, oz);
                     ptx::tma_store_commit();
                 }
             }
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&ctl->o_free[X]);
-            if (ok) {
-                const float lse = (((m == -INFINITY) ? 0.f : m) + __log2f(l)) * kLn2;
+            if (ok && hh == 0) {
+                const float lse = (((M == -INFINITY) ? 0.f : M) + __log2f(Lsum)) * kLn2;
                 if (un.grow) {
                     p.part_lse[((size_t)(2 * un.split + X) * p.bh + un.bh) * p.gpad + qi] = lse;
                 } else if (p.lse != nullptr && qi < p.n) {
@@ -634,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
-    if (warp == 9) ptx::tmem_dealloc(tmem, kTmemCols);
+    if (warp == C::kMmaWarp) ptx::tmem_dealloc(tmem, kTmemCols);
 }
 
 // ------------------------------------------------------------------------ gather
@@ -721,7 +819,7 @@ static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int 
     const int smem = Cfg<D, BF16>::kSmemBytes;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.qg, tm.kg, tm.vg, tm.o, tm.po, p);
+    kern<<<grid, Cfg<D, BF16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.qg, tm.kg, tm.vg, tm.o, tm.po, p);
     return cudaGetLastError();
 }
 
