@@ -97,6 +97,28 @@ LCA_API int lca_swa_forward(const void* q, const void* k, const void* v, float* 
                     size_t workspace_bytes, void* stream);
 
 /*
+ * Bytes of the fixed device scratch array used by lca_swa_forward_noalloc.
+ */
+#define LCA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/*
+ * Same computation and arguments as lca_swa_forward, minus the workspace: for callers
+ * that cannot allocate device memory (a serving loop whose memory belongs to its own pool
+ * allocator, a plugin inside a runtime that forbids allocation after start-up, a loop
+ * that must not risk the synchronisation a cudaFree can cause).  No counterpart in the
+ * reference.  The scratch is a fixed LCA_NOALLOC_SCRATCH_BYTES device array inside the
+ * library: each GPU that uses this entry point holds it from the first call until the
+ * process exits; the first call on a device looks up the array's device address and
+ * should come before any stream capture on that device.  All calls on a device share the
+ * array, so calls that can overlap on the GPU race: order them.  Problems needing more
+ * scratch than the array holds return LCA_ERR_UNSUPPORTED before any work is enqueued.
+ */
+LCA_API int lca_swa_forward_noalloc(const void* q, const void* k, const void* v, float* out, float* lse, int dtype,
+                                    int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                                    int64_t window_size, float scale, const int64_t* global_tokens,
+                                    int64_t num_global_tokens, void* stream);
+
+/*
  * Measurement hook (no counterpart in the reference): when both events are non-NULL,
  * subsequent lca_swa_forward calls made on THIS thread record `before_main` immediately
  * before and `after_main` immediately after the launch of the main attention kernel, on

@@ -30,7 +30,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CABI_SOURCES = ["swa_kernels.cu", "capi.cpp"]
+CABI_SOURCES = ["swa_kernels.cu", "capi.cpp", "noalloc.cu"]
 CABI_HEADERS = ["sm100_ptx.cuh", "swa_kernels.h"]
 LIB_NAME = "liblca_b200.so"
 EXT_NAME = "long_context_attention_kernels"

@@ -34,6 +34,20 @@ int fail(int status, const char* fmt, ...) {
     return status;
 }
 
+}  // namespace
+
+int lca::report_error(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+namespace {
+
 int fail_cuda(cudaError_t e, const char* what) {
     return fail(LCA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }

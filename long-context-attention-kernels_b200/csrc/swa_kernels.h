@@ -72,6 +72,10 @@ cudaError_t launch_gather(int head_dim, const void* q, const void* k, const void
                           int bh, cudaStream_t stream);
 cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t stream);
 int main_smem_bytes(int head_dim, bool bf16);
+// Record `status` and a printf-style detail message as this thread's last C-ABI error
+// (what lca_last_error() returns); returns `status`.
+int report_error(int status, const char* fmt, ...);
+
 // Device address (on the current device) of the device-side error word.
 cudaError_t error_word_address(int** out);
 

@@ -71,6 +71,9 @@ class CABI:
         lib.lca_swa_forward.restype = ctypes.c_int
         lib.lca_swa_forward.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64, ctypes.c_float,
                                         ctypes.POINTER(i64), i64, vp, sz, vp]
+        lib.lca_swa_forward_noalloc.restype = ctypes.c_int
+        lib.lca_swa_forward_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64,
+                                                ctypes.c_float, ctypes.POINTER(i64), i64, vp]
         lib.lca_set_timing_events.restype = ctypes.c_int
         lib.lca_set_timing_events.argtypes = [vp, vp]
         lib.lca_device_error.restype = ctypes.c_int
@@ -100,6 +103,14 @@ class CABI:
         arr = (ctypes.c_int64 * max(n, 1))(*tokens)
         return self.lib.lca_swa_forward(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim,
                                         window, ctypes.c_float(scale), arr, n, ws_ptr, ws_bytes, stream_ptr)
+
+
+    def forward_noalloc(self, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim, window,
+                        scale, tokens, stream_ptr) -> int:
+        n = len(tokens)
+        arr = (ctypes.c_int64 * max(n, 1))(*tokens)
+        return self.lib.lca_swa_forward_noalloc(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len,
+                                                head_dim, window, ctypes.c_float(scale), arr, n, stream_ptr)
 
 
 def cabi() -> CABI:
