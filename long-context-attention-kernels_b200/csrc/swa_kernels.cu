@@ -32,19 +32,20 @@
 // [128h/H, 128(h+1)/H) of every S tile of X and runs an independent online softmax over
 // them into its own accumulator O_{X,h}; the H partial results of a row are merged by
 // log-sum-exp in the epilogue.  Thread r of a warpgroup <-> query row r <-> TMEM lane r.
-//   d = 64 : warps 0-15 softmax (A0, A1, B0, B1), warp 16 TMA producer, warp 17 MMA
-//            (576 threads, no register split)
-//   d = 128: warps 0-7 softmax (A, B), warp 8 TMA, warp 9 MMA, warps 10-11 idle
+//   d = 64 : warps 0-15 softmax (A0, A1, B0, B1), warp 16 TMA producer, warps 17/18 MMA
+//            issuers for A/B (608 threads, no register split)
+//   d = 128: warps 0-7 softmax (A, B), warp 8 TMA, warps 9/10 MMA issuers for A/B, warp 11
+//            idle
 //            (384 threads; setmaxnreg: warpgroup 2 drops to 72 registers, warpgroups 0-1
 //            rise to 216; 128*72 + 256*216 = 384*168, the launch allocation)
 // TMEM (512 columns): S_A [0,128), S_B [128,256), then O_{A,0..H-1}, O_{B,0..H-1}, d each.
 // P overwrites S in place: warpgroup (X, h) writes its 16-bit P (hi pairs, then lo pairs
 // for bf16) into its own S columns, and P*V reads it as the TMEM A operand.
-// MMA issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one tile's
-// softmax runs, the tensor cores work for the other.  tcgen05 ops issued by one thread
-// execute in order, so S_X(j+1) never overwrites P_X(j) before PV_X(j) read it, and the
-// commit that signals S_X(j+1) also covers PV_X(j), so O_X is stable whenever its softmax
-// warps see a new S.
+// Each query tile has its own MMA-issuing thread, which issues PV_X(j) then S_X(j+1):
+// while one tile's softmax runs, the tensor cores work for the other.  tcgen05 ops
+// issued by one thread execute in order, so S_X(j+1) never overwrites P_X(j) before
+// PV_X(j) read it, and the commit that signals S_X(j+1) also covers PV_X(j), so O_X is
+// stable whenever its softmax warps see a new S.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -79,13 +80,13 @@ constexpr float kRescaleThreshold = 8.0f;
 template <int D, bool BF16>
 struct Cfg {
     static constexpr bool kSplitP = BF16;
-    static constexpr int kHalves = 1;                      // softmax warpgroups per query tile
+    static constexpr int kHalves = (D == 64) ? 2 : 1;      // softmax warpgroups per query tile
     static constexpr int kCols = BN / kHalves;             // S columns per softmax thread
     static constexpr int kSoftmaxWarps = 8 * kHalves;
     static constexpr int kTmaWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
     static constexpr bool kRegSplit = (kHalves == 1);
-    static constexpr int kThreads = kRegSplit ? 384 : (kSoftmaxWarps + 2) * 32;
+    static constexpr int kThreads = kRegSplit ? 384 : (kSoftmaxWarps + 3) * 32;
     static constexpr int kRegsLaunch = 168, kRegsSoftmax = 216, kRegsControl = 72;
     static constexpr int kEpiCols = D / kHalves;           // output columns per warpgroup
     static constexpr int kPanels = D / 64;
@@ -115,7 +116,7 @@ struct Ctl {
     uint64_t p_full[2];
     uint64_t o_full[2];
     uint64_t o_free[2];
-    uint64_t mma_drained;
+    uint64_t mma_drained[2];
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -254,9 +255,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
         }
         for (int s = 0; s < C::kSlots; ++s) {
             ptx::mbar_init(&ctl->kv_full[s], 1);
-            ptx::mbar_init(&ctl->kv_empty[s], 1);
+            ptx::mbar_init(&ctl->kv_empty[s], 2);  // one release per MMA issuer
         }
-        ptx::mbar_init(&ctl->mma_drained, 1);
+        ptx::mbar_init(&ctl->mma_drained[0], 1);
+        ptx::mbar_init(&ctl->mma_drained[1], 1);
         ctl->abort_flag = 0;
         ptx::fence_mbar_init();
     }
@@ -326,16 +328,25 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     ptx::mbar_wait(&ctl->kv_full[idx % C::kSlots], (idx / C::kSlots) & 1, nullptr, p.err,
                                    LCA_DEVERR_TIMEOUT_DRAIN, tmo);
             }
-        } else if (warp == C::kMmaWarp) {
-            // ======================================================== MMA issuer
+        } else if (warp == C::kMmaWarp || warp == C::kMmaWarp + 1) {
+            // ======================================================== MMA issuers
+            // One issuing thread per query tile X, so the two tiles' MMA streams progress
+            // independently.  Every K/V slot use is released once by each issuer (the
+            // kv_empty barriers count 2): by a commit after the issuer's last MMA reading
+            // it, or by a plain arrive if the tile is not one of its members.  An issuer
+            // always waits for a slot's data to land before releasing it, so its releases
+            // can never run ahead into the slot's next phase.
+            const int X = warp - C::kMmaWarp;
             if (ptx::elect_one()) {
-                const uint32_t sq = ptx::smem_u32(sQ);
                 const uint32_t sslots = ptx::smem_u32(sSlots);
+                // descriptor high words are loop-invariant (128-byte swizzle, 1024-byte 8-row
+                // groups); a k-step only advances the low word's start address
+                const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
+                const uint32_t qlo = ptx::smem_desc_sw128_lo(ptx::smem_u32(sQ) + X * C::kTileBytes, 0);
                 const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, BN, false);
                 const uint32_t idesc_pv = ptx::idesc_f16(BF16, BM, D, true);
-                int L = 0, qn = 0;
-                int pc0 = 0, pc1 = 0;  // p_full phases consumed
-                int oc0 = 0, oc1 = 0;  // o_full phases produced
+                const uint32_t sx = tmem + X * 128;
+                int L = 0, qn = 0, pc = 0, oc = 0;
                 bool ok = true;
 
                 auto W = [&](uint64_t* bar, int parity) -> bool {
@@ -344,107 +355,98 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     if (ok) ptx::tc_fence_after();
                     return ok;
                 };
-                auto issue_s = [&](int x, int slot, int ncols) {
+                // S_X = Q_X K^T
+                auto issue_s = [&](int slot, int ncols) {
                     const uint32_t idesc = (ncols == BN) ? idesc_s_full : ptx::idesc_f16(BF16, BM, ncols, false);
-                    const uint32_t kbase = sslots + slot * C::kTileBytes;
-                    const uint32_t qbase = sq + x * C::kTileBytes;
+                    const uint32_t klo = ptx::smem_desc_sw128_lo(sslots + slot * C::kTileBytes, 0);
 #pragma unroll
                     for (int ks = 0; ks < D / 16; ++ks) {
-                        const uint32_t off = (ks >> 2) * kPanelBytes + (ks & 3) * 32;
-                        ptx::mma_f16_ss(tmem + x * 128, ptx::smem_desc_sw128(qbase + off, 0, 1024),
-                                        ptx::smem_desc_sw128(kbase + off, 0, 1024), idesc, ks > 0 ? 1u : 0u);
+                        const uint32_t off = ((ks >> 2) * kPanelBytes + (ks & 3) * 32) >> 4;
+                        ptx::mma_f16_ss(sx, ptx::desc_join(qlo + off, dhi), ptx::desc_join(klo + off, dhi), idesc,
+                                        ks > 0 ? 1u : 0u);
                     }
                 };
-                // O_x += P_x V.  P_x lives in S_x's TMEM columns: keys [32c, 32c + 32) of
-                // the tile occupy columns [32c, 32c + 32), hi pairs in the first 16 and, for
-                // bf16, lo pairs in the next 16 (two 16-bit elements per 32-bit column).
-                auto issue_pv = [&](int x, int slot, int ncols, bool first) {
-                    const uint32_t vbase = sslots + slot * C::kTileBytes;
-                    const uint32_t dcol = tmem + C::kOCol + x * D;
-                    const int ksteps = ncols / 16;
-#pragma unroll 1
-                    for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
-                        for (int kk = 0; kk < ksteps; ++kk) {
-                            const uint32_t acol = tmem + x * 128 + (kk >> 1) * 32 + part * 16 + (kk & 1) * 8;
-                            const uint64_t bdesc = ptx::smem_desc_sw128(vbase + kk * 16 * 128, kPanelBytes, 1024);
-                            ptx::mma_f16_ts(dcol, acol, bdesc, idesc_pv, (!first || part > 0 || kk > 0) ? 1u : 0u);
+                // O_{X,h} += P_{X,h} V[keys of half h].  P lives in S_X's TMEM columns: keys
+                // [32c, 32c + 32) of the tile occupy columns [32c, 32c + 32), hi pairs in the
+                // first 16 and, for bf16, lo pairs in the next 16 (two 16-bit elements per
+                // 32-bit column).  Half h owns keys [KC*h, KC*(h+1)) and accumulates into O_{X,h}.
+                auto issue_pv = [&](int slot, int ncols, bool first) {
+                    const uint32_t vlo = ptx::smem_desc_sw128_lo(sslots + slot * C::kTileBytes, kPanelBytes);
+#pragma unroll
+                    for (int h = 0; h < H; ++h) {
+                        const uint32_t dcol = tmem + C::kOCol + (X * H + h) * D;
+#pragma unroll
+                        for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
+#pragma unroll
+                            for (int kk = 0; kk < KC / 16; ++kk) {
+                                const int key = KC * h + 16 * kk;  // first key of this k-step
+                                if (key < ncols) {
+                                    const uint32_t acol = sx + (key >> 5) * 32 + part * 16 + ((key >> 4) & 1) * 8;
+                                    ptx::mma_f16_ts(dcol, acol, ptx::desc_join(vlo + ((key * 128) >> 4), dhi),
+                                                    idesc_pv, (!first || part > 0 || kk > 0) ? 1u : 0u);
+                                }
+                            }
                         }
                     }
                 };
 
                 for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                     const Unit un = decode_unit(p, u);
-                    // Last key tile of each query tile: its S MMA is the last reader of that Q
-                    // buffer, so the buffer is released to the producer right after it.
-                    int last_s0 = -1, last_s1 = -1;
-                    for (int j = 0; j < un.ntiles; ++j) {
-                        const Tile t = tile_of(p, un, j);
-                        if (t.mem[0]) last_s0 = j;
-                        if (t.mem[1]) last_s1 = j;
-                    }
-                    if (!W(&ctl->q_full[0], qn) || !W(&ctl->q_full[1], qn)) break;
+                    const bool act = X ? un.active[1] : un.active[0];
+                    if (!W(&ctl->q_full[X], qn)) break;
                     ++qn;
-                    if (last_s0 < 0) ptx::mma_commit(&ctl->q_empty[0]);
-                    if (last_s1 < 0) ptx::mma_commit(&ctl->q_empty[1]);
-                    auto s_and_release = [&](const int x, int slot, int ncols, int jj) {
-                        issue_s(x, slot, ncols);
-                        ptx::mma_commit(&ctl->s_full[x]);
-                        if (jj == (x ? last_s1 : last_s0)) ptx::mma_commit(&ctl->q_empty[x]);
+                    bool first = true;       // next P*V starts the accumulator
+                    int pend_lv = -1;        // slot use of V for the member tile whose P*V is pending
+                    int pend_cols = 0;
+                    // P*V of the pending member tile; it precedes the next S MMA, which
+                    // overwrites the TMEM columns holding that tile's P
+                    auto pv_step = [&]() -> bool {
+                        if (!W(&ctl->p_full[X], pc)) return false;
+                        ++pc;
+                        if (first && oc > 0 && !W(&ctl->o_free[X], oc - 1)) return false;
+                        if (!W(&ctl->kv_full[pend_lv % C::kSlots], pend_lv / C::kSlots)) return false;
+                        issue_pv(pend_lv % C::kSlots, pend_cols, first);
+                        first = false;
+                        ptx::mma_commit(&ctl->kv_empty[pend_lv % C::kSlots]);
+                        return true;
                     };
-                    bool first_pv0 = true, first_pv1 = true;
-                    {
-                        const Tile t0 = tile_of(p, un, 0);
-                        if (!W(&ctl->kv_full[L % C::kSlots], L / C::kSlots)) break;
-                        if (t0.mem[0]) s_and_release(0, L % C::kSlots, t0.ncols, 0);
-                        if (t0.mem[1]) s_and_release(1, L % C::kSlots, t0.ncols, 0);
-                        ptx::mma_commit(&ctl->kv_empty[L % C::kSlots]);
-                    }
                     for (int j = 0; j < un.ntiles && ok; ++j) {
                         const Tile t = tile_of(p, un, j);
-                        const int lv = L + 2 * j + 1;
-                        const int lk = lv + 1;
-                        const bool has_next = j + 1 < un.ntiles;
-                        const Tile tn = has_next ? tile_of(p, un, j + 1) : t;
-                        if (!W(&ctl->kv_full[lv % C::kSlots], lv / C::kSlots)) break;
-                        bool k_next_ready = false;  // K_{j+1} is awaited right before its first use
-                        auto step = [&](const int x, const bool mem_now, const bool mem_next, int& pcx,
-                                        const int ocx, bool& firstx) {
-                            if (mem_now && ok) {
-                                if (!W(&ctl->p_full[x], pcx)) return;
-                                ++pcx;
-                                if (firstx && ocx > 0 && !W(&ctl->o_free[x], ocx - 1)) return;
-                                issue_pv(x, lv % C::kSlots, t.ncols, firstx);
-                                firstx = false;
-                            }
-                            if (has_next && mem_next && ok) {
-                                if (!k_next_ready) {
-                                    if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) return;
-                                    k_next_ready = true;
-                                }
-                                s_and_release(x, lk % C::kSlots, tn.ncols, j + 1);
-                            }
-                        };
-                        step(0, t.mem[0], tn.mem[0], pc0, oc0, first_pv0);
-                        step(1, t.mem[1], tn.mem[1], pc1, oc1, first_pv1);
-                        if (!ok) break;
-                        ptx::mma_commit(&ctl->kv_empty[lv % C::kSlots]);
-                        // every issued tile has a member, so K_{j+1} was consumed above
-                        if (has_next) ptx::mma_commit(&ctl->kv_empty[lk % C::kSlots]);
+                        const bool mem = act && (X ? t.mem[1] : t.mem[0]);
+                        const int lk = L + 2 * j, lv = lk + 1;
+                        // The pending P*V goes first: it releases its V slot, which the producer
+                        // may need before it can load this tile (a 3-slot ring holds one tile
+                        // plus one V), and it must precede the next S MMA in any case.
+                        if (pend_lv >= 0) {
+                            if (!pv_step()) break;
+                            pend_lv = -1;
+                        }
+                        if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
+                        if (mem) {
+                            issue_s(lk % C::kSlots, t.ncols);
+                            ptx::mma_commit(&ctl->s_full[X]);
+                            ptx::mma_commit(&ctl->kv_empty[lk % C::kSlots]);
+                            pend_lv = lv;
+                            pend_cols = t.ncols;
+                        } else {
+                            ptx::mbar_arrive(&ctl->kv_empty[lk % C::kSlots]);
+                            if (!W(&ctl->kv_full[lv % C::kSlots], lv / C::kSlots)) break;
+                            ptx::mbar_arrive(&ctl->kv_empty[lv % C::kSlots]);
+                        }
                     }
                     if (!ok) break;
+                    // every S MMA of this unit has been issued: Q_X may be refilled once they complete
+                    ptx::mma_commit(&ctl->q_empty[X]);
+                    if (pend_lv >= 0 && !pv_step()) break;
+                    if (!first) {
+                        ptx::mma_commit(&ctl->o_full[X]);
+                        ++oc;
+                    }
                     L += 2 * un.ntiles;
-                    if (!first_pv0) {
-                        ptx::mma_commit(&ctl->o_full[0]);
-                        ++oc0;
-                    }
-                    if (!first_pv1) {
-                        ptx::mma_commit(&ctl->o_full[1]);
-                        ++oc1;
-                    }
                 }
                 // Drain: all tcgen05 ops issued by this thread complete before TMEM is freed.
-                ptx::mma_commit(&ctl->mma_drained);
-                ptx::mbar_wait(&ctl->mma_drained, 0, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
+                ptx::mma_commit(&ctl->mma_drained[X]);
+                ptx::mbar_wait(&ctl->mma_drained[X], 0, nullptr, p.err, LCA_DEVERR_TIMEOUT_DRAIN, tmo);
             }
         }
     } else {
@@ -524,12 +526,12 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                         lo = jlo - col0;
                         hi = jhi - col0;
                     }
-                    if (hi > t.ncols - 1) hi = t.ncols - 1;
-                    const int nchunks = (t.ncols + 31) >> 5;
+                    if (hi > ncols_h - 1) hi = ncols_h - 1;
+                    const int nchunks = ((ncols_h < KC ? ncols_h : KC) + 31) >> 5;
                     // ---- pass 1: S row into registers, masked row max
-                    float s[BN];
+                    float s[KC];
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < KC / 32; ++c) {
                         if (c < nchunks) {
                             float tmp[32];
                             ptx::tmem_ld32(t_lane + s_col + c * 32, tmp);
@@ -540,18 +542,18 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                             for (int e = 0; e < 32; ++e) s[c * 32 + e] = sent;
                         }
                     }
-                    const bool need = lo > 0 || hi < BN - 1 || (h_lo < h_hi && h_hi > 0 && h_lo < BN);
+                    const bool need = lo > 0 || hi < KC - 1 || (h_lo < h_hi && h_hi > 0 && h_lo < KC);
                     const bool any_mask = __any_sync(0xffffffffu, need);
                     ptx::tmem_wait_ld();
                     if (any_mask) {
 #pragma unroll
-                        for (int c = 0; c < BN; ++c)
+                        for (int c = 0; c < KC; ++c)
                             s[c] = (c >= lo && c <= hi && (c < h_lo || c >= h_hi)) ? s[c] : sent;
                     }
                     float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
                     if (!neg_scale) {
 #pragma unroll
-                        for (int c = 0; c < BN; c += 8) {
+                        for (int c = 0; c < KC; c += 8) {
                             r0 = ptx::fmax3(r0, s[c + 0], s[c + 1]);
                             r1 = ptx::fmax3(r1, s[c + 2], s[c + 3]);
                             r2 = ptx::fmax3(r2, s[c + 4], s[c + 5]);
@@ -559,7 +561,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                         }
                     } else {
 #pragma unroll
-                        for (int c = 0; c < BN; c += 8) {
+                        for (int c = 0; c < KC; c += 8) {
                             r0 = ptx::fmin3(r0, s[c + 0], s[c + 1]);
                             r1 = ptx::fmin3(r1, s[c + 2], s[c + 3]);
                             r2 = ptx::fmin3(r2, s[c + 4], s[c + 5]);
