@@ -582,44 +582,38 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                         l *= alpha;
                     }
                     if (__any_sync(0xffffffffu, rescale)) {
+                        // rare: rescale this row's accumulator, 8 columns at a time (few live registers)
                         const float a = rescale ? alpha : 1.f;
 #pragma unroll 1
-                        for (int c = 0; c < D / 32; ++c) {
-                            float o[32];
-                            ptx::tmem_ld32(t_lane + o_col + c * 32, o);
+                        for (int c = 0; c < D / 8; ++c) {
+                            uint32_t o[8];
+                            ptx::tmem_ld8(t_lane + o_col + c * 8, o);
                             ptx::tmem_wait_ld();
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) o[e] *= a;
-                            ptx::tmem_st32(t_lane + o_col + c * 32, o);
+                            for (int e = 0; e < 8; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
+                            ptx::tmem_st8u(t_lane + o_col + c * 8, o);
                         }
                     }
-                    // ---- pass 2, one 32-key chunk at a time (S re-read from TMEM): p = 2^(s *
-                    // scale * log2(e) - m), row sum, 16-bit pairs written over the chunk's own
-                    // S columns (hi pairs, then lo pairs for bf16)
+                    // ---- pass 2, from the registers of pass 1, one 32-key chunk at a time:
+                    // p = 2^(s * scale * log2(e) - m) (masked scores are already `sent`, which
+                    // maps to 0), row sum, 16-bit pairs written over the chunk's own S columns
+                    // (hi pairs, then lo pairs for bf16).  Chunks masked for the whole warp skip
+                    // the exponentials.
                     const float neg_m = (m == -INFINITY) ? 0.f : -m;
                     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 1
-                    for (int c = 0; c < nchunks; ++c) {
+#pragma unroll
+                    for (int c = 0; c < KC / 32; ++c) {
+                        if (c >= nchunks) break;
                         const int c0 = c * 32;
                         const bool in_none = hi < c0 || lo > c0 + 31 || (h_lo <= c0 && h_hi > c0 + 31);
-                        const bool in_full = lo <= c0 && hi >= c0 + 31 && (h_hi <= c0 || h_lo > c0 + 31);
-                        uint32_t w[16];
-                        uint32_t wl[16];
                         if (__all_sync(0xffffffffu, in_none)) {
+                            uint32_t z[16];
 #pragma unroll
-                            for (int e = 0; e < 16; ++e) w[e] = wl[e] = 0u;
+                            for (int e = 0; e < 16; ++e) z[e] = 0u;
+                            ptx::tmem_st16u(t_lane + s_col + c0, z);
+                            if (BF16) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
                         } else {
-                            float v[32];
-                            ptx::tmem_ld32(t_lane + s_col + c0, v);
-                            const bool part = !__all_sync(0xffffffffu, in_full);
-                            ptx::tmem_wait_ld();
-                            if (part) {
-#pragma unroll
-                                for (int e = 0; e < 32; ++e) {
-                                    const int col = c0 + e;
-                                    v[e] = (col >= lo && col <= hi && (col < h_lo || col >= h_hi)) ? v[e] : sent;
-                                }
-                            }
+                            float* v = s + c0;
 #pragma unroll
                             for (int e = 0; e < 32; e += 4) {
                                 v[e + 0] = ptx::ex2(fmaf(v[e + 0], sl2, neg_m));
@@ -632,18 +626,24 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                                 a3 += v[e + 3];
                             }
 #pragma unroll
-                            for (int e = 0; e < 16; ++e) {
-                                if (BF16) {
-                                    w[e] = ptx::pack_bf16x2(v[2 * e], v[2 * e + 1]);
-                                    wl[e] = ptx::pack_bf16x2(v[2 * e] - __uint_as_float(w[e] << 16),
-                                                             v[2 * e + 1] - __uint_as_float(w[e] & 0xFFFF0000u));
-                                } else {
-                                    w[e] = ptx::pack_f16x2(v[2 * e], v[2 * e + 1]);
+                            for (int g8 = 0; g8 < 2; ++g8) {  // 8 pairs (16 keys) per store
+                                uint32_t w[8];
+                                uint32_t wl[8];
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) {
+                                    const float x0 = v[g8 * 16 + 2 * e], x1 = v[g8 * 16 + 2 * e + 1];
+                                    if (BF16) {
+                                        w[e] = ptx::pack_bf16x2(x0, x1);
+                                        wl[e] = ptx::pack_bf16x2(x0 - __uint_as_float(w[e] << 16),
+                                                                 x1 - __uint_as_float(w[e] & 0xFFFF0000u));
+                                    } else {
+                                        w[e] = ptx::pack_f16x2(x0, x1);
+                                    }
                                 }
+                                ptx::tmem_st8u(t_lane + s_col + c0 + g8 * 8, w);
+                                if (BF16) ptx::tmem_st8u(t_lane + s_col + c0 + 16 + g8 * 8, wl);
                             }
                         }
-                        ptx::tmem_st16u(t_lane + s_col + c0, w);
-                        if (BF16) ptx::tmem_st16u(t_lane + s_col + c0 + 16, wl);
                     }
                     l += (a0 + a1) + (a2 + a3);
                     ptx::tmem_wait_st();
