@@ -771,8 +771,10 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
 
 template <int D>
 __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp) {
-    // one warp per (bh, global row); partial 2*s + x covers the key tiles of split s
-    // with parity x, and exists only if that split has more than x tiles
+    // One warp per (bh, global row).  Partial 2*s + x covers the key tiles of split s with
+    // parity x and exists only if that split has more than x tiles.  Lanes take partials
+    // in parallel for the max and the weights; the weighted sum then walks the partials
+    // with independent loads (lane = output column).
     const long long w = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= (long long)cp.num_global * cp.bh) return;
@@ -787,21 +789,31 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
         if (tiles > cp.split_tiles) tiles = cp.split_tiles;
         return tiles > (part & 1);
     };
+    auto lse_of = [&](int part) {
+        return valid(part) ? __ldg(cp.part_lse + ((size_t)part * cp.bh + bh) * cp.gpad + g) : -INFINITY;
+    };
     float mx = -INFINITY;
-    for (int s = 0; s < n_parts; ++s)
-        if (valid(s)) mx = fmaxf(mx, cp.part_lse[((size_t)s * cp.bh + bh) * cp.gpad + g]);
+    for (int s = lane; s < n_parts; s += 32) mx = fmaxf(mx, lse_of(s));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float wsum = 0.f;
+    for (int s = lane; s < n_parts; s += 32) {
+        const float ls = lse_of(s);
+        wsum += (ls == -INFINITY) ? 0.f : __expf(ls - mx);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
     float acc[kPer];
 #pragma unroll
     for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
-    float wsum = 0.f;
+#pragma unroll 4
     for (int s = 0; s < n_parts; ++s) {
-        if (!valid(s)) continue;
-        const size_t prow = (size_t)s * cp.bh + bh;
-        const float wt = __expf(cp.part_lse[prow * cp.gpad + g] - mx);
-        wsum += wt;
-        const float* po = cp.part_o + (prow * cp.gpad + g) * D;
+        const float ls = lse_of(s);
+        if (ls == -INFINITY) continue;
+        const float wt = __expf(ls - mx);
+        const float* po = cp.part_o + (((size_t)s * cp.bh + bh) * cp.gpad + g) * D;
 #pragma unroll
-        for (int e = 0; e < kPer; ++e) acc[e] += wt * po[lane + 32 * e];
+        for (int e = 0; e < kPer; ++e) acc[e] += wt * __ldg(po + lane + 32 * e);
     }
     const int row = cp.gidx[g];
     float* out = cp.o + ((size_t)bh * cp.n + row) * D;
