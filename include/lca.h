@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define LCA_ABI_VERSION 1
+#define LCA_ABI_VERSION 2
 
 #if defined(LCA_BUILDING_LIBRARY) && defined(__GNUC__)
 #define LCA_API __attribute__((visibility("default")))
@@ -117,6 +117,78 @@ LCA_API int lca_swa_forward_noalloc(const void* q, const void* k, const void* v,
                                     int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
                                     int64_t window_size, float scale, const int64_t* global_tokens,
                                     int64_t num_global_tokens, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Sequence shards.  A sequence too long for one GPU is cut into contiguous token shards,
+ * one per rank: rank r holds rows [shard_offset, shard_offset + shard_len) of Q, K and V
+ * for every (batch, head), and produces the same rows of the output.  The reference runs
+ * one sequence on one device only; these calls split its forward
+ * (csrc/bindings.cpp:31-73) into the compute steps around three exchanges that the
+ * caller performs with its own collectives library (NCCL):
+ *
+ *   1. lca_swa_shard_prepare   -- on every rank
+ *   2. exchange A (sum all-reduce): the `globals` region of every rank's workspace,
+ *      elementwise in the input dtype (each rank contributes the global rows it owns and
+ *      zeros elsewhere)
+ *      exchange B (point-to-point): send side 0 of `halo_send` to rank r-1 and side 1 to
+ *      rank r+1; receive from rank r-1 into side 0 of `halo_recv` and from rank r+1 into
+ *      side 1 (ranks without that neighbour skip the transfer)
+ *   3. lca_swa_shard_forward   -- on every rank
+ *   4. exchange C (all-gather): every rank's `rowpart` region into `rowpart_all`, rank
+ *      order, rowpart_bytes per rank
+ *   5. lca_swa_shard_finish    -- on every rank; writes the global rows this shard owns
+ *
+ * Exchanges A and C are skipped when there are no global tokens, B when halo_rows is 0.
+ * Every step takes the same descriptor and global-token list; the workspace carries
+ * state from one step to the next and must not be reused until step 5 has run.
+ * Limits: every shard but the last holds a multiple of 128 tokens, and
+ * min(window_size, seq_len) <= shard_len when world_size > 1 (halos come from the
+ * adjacent shards only).
+ */
+typedef struct lca_shard_desc {
+    int64_t batch, heads, seq_len, head_dim, window_size;
+    int64_t shard_offset; /* absolute index of this shard's first token */
+    int64_t shard_len;    /* tokens in this shard (rows of q / k / v / out / lse) */
+    int64_t world_size;   /* number of shards */
+    int dtype;            /* LCA_DTYPE_* */
+    float scale;
+} lca_shard_desc;
+
+/* Byte offsets of the exchanged regions inside the workspace, and sizes. */
+typedef struct lca_shard_layout {
+    size_t total_bytes;        /* workspace size */
+    int64_t halo_rows;         /* K / V rows per halo side (0: no halo exchange) */
+    size_t globals_offset;     /* exchange A region */
+    size_t globals_bytes;
+    size_t halo_send_offset;   /* [2 sides][2 (k, v)][batch*heads][halo_rows][head_dim], input dtype */
+    size_t halo_recv_offset;   /* same layout */
+    size_t halo_side_bytes;    /* bytes of one side of halo_send / halo_recv */
+    size_t rowpart_offset;     /* exchange C source */
+    size_t rowpart_bytes;
+    size_t rowpart_all_offset; /* exchange C target: world_size * rowpart_bytes */
+} lca_shard_layout;
+
+/* Workspace layout of one shard's problem (`num_unique_global` after normalisation).
+ * Host-only. */
+LCA_API int lca_swa_shard_layout(const lca_shard_desc* desc, int64_t num_unique_global, lca_shard_layout* out);
+
+/* Step 1: compact global rows owned by this shard, the sorted global index list and the
+ * halo blocks for the neighbours.  q, k, v: [batch, heads, shard_len, head_dim]. */
+LCA_API int lca_swa_shard_prepare(const lca_shard_desc* desc, const void* q, const void* k, const void* v,
+                                  const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* Step 3: every row of this shard (global rows are finished in step 5) and this shard's
+ * partial result for the global rows over its own keys.  out: [batch, heads, shard_len,
+ * head_dim] fp32; lse: [batch, heads, shard_len] fp32 or NULL. */
+LCA_API int lca_swa_shard_forward(const lca_shard_desc* desc, const void* q, const void* k, const void* v,
+                                  float* out, float* lse, const int64_t* global_tokens, int64_t num_global_tokens,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Step 5: log-sum-exp merge of the shards' global-row partials; writes the global rows
+ * that fall in this shard to out / lse. */
+LCA_API int lca_swa_shard_finish(const lca_shard_desc* desc, float* out, float* lse, const int64_t* global_tokens,
+                                 int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Measurement hook (no counterpart in the reference): when both events are non-NULL,

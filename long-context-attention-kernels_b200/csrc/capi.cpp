@@ -107,7 +107,97 @@ int check_device(int* dev_out, int** err_word) {
     return LCA_OK;
 }
 
-// ------------------------------------------------------------------ problem layout
+// ------------------------------------------------------------------ problem description
+
+// One forward problem: the whole sequence (q_off = 0, n = n_total), or one contiguous
+// shard of it.
+struct Problem {
+    int64_t bh = 0;
+    int64_t n_total = 0;   // sequence length
+    int64_t n = 0;         // local rows of Q / K / V / O
+    int64_t q_off = 0;     // absolute index of local row 0
+    int64_t d = 0;
+    int64_t window = 0;    // clamped to n_total
+    int64_t G = 0;         // unique global tokens
+    int64_t world = 1;     // shards
+    bool sharded = false;
+    int dtype = LCA_DTYPE_BF16;
+    float scale = 1.f;
+    std::vector<int32_t> gl;  // sorted unique global indices (absolute)
+    int64_t halo() const { return sharded && world > 1 ? window : 0; }
+    int64_t lead() const {
+        return sharded ? (window + lca::kTileRows - 1) / lca::kTileRows * lca::kTileRows : window;
+    }
+};
+
+int check_dtype_dim(int dtype, int64_t head_dim) {
+    if (dtype != LCA_DTYPE_F16 && dtype != LCA_DTYPE_BF16)
+        return fail(LCA_ERR_UNSUPPORTED, "dtype %d is not supported (fp16 or bf16 inputs)", dtype);
+    if (head_dim != 64 && head_dim != 128)
+        return fail(LCA_ERR_UNSUPPORTED, "head_dim %lld is not supported (64 or 128)", (long long)head_dim);
+    return LCA_OK;
+}
+
+// Shape checks shared by every entry point (csrc/bindings.cpp:25-42 restated for a C
+// caller), then the global-token list, normalised as the reference's mask builds it.
+int parse_common(Problem& P, int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                 int64_t window_size, float scale, const int64_t* global_tokens, int64_t num_global_tokens) {
+    int st = check_dtype_dim(dtype, head_dim);
+    if (st != LCA_OK) return st;
+    if (batch < 0 || heads < 0 || seq_len < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "negative shape");
+    if (window_size < 0)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "window_size must be >= 0 (got %lld)", (long long)window_size);
+    if (seq_len > ((int64_t)1 << 29))
+        return fail(LCA_ERR_UNSUPPORTED, "seq_len %lld too large (max 2^29)", (long long)seq_len);
+    const int64_t bh = batch * heads;
+    if (bh > INT_MAX / 64) return fail(LCA_ERR_UNSUPPORTED, "batch*heads %lld too large", (long long)bh);
+    if (num_global_tokens < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "negative global token count");
+    if (num_global_tokens > 0 && global_tokens == nullptr)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "global_tokens is NULL");
+    // Global tokens are validated even for empty problems, as the reference's mask
+    // construction would raise on them.
+    P.gl.assign((size_t)num_global_tokens + 1, 0);
+    int64_t G = 0;
+    st = lca_normalize_global_tokens(global_tokens, num_global_tokens, seq_len, P.gl.data(), &G);
+    if (st != LCA_OK) return st;
+    P.gl.resize((size_t)G);
+    P.bh = bh;
+    P.n_total = seq_len;
+    P.n = seq_len;
+    P.q_off = 0;
+    P.d = head_dim;
+    P.window = std::min(window_size, seq_len);
+    P.G = G;
+    P.dtype = dtype;
+    P.scale = scale;
+    return LCA_OK;
+}
+
+int parse_shard(Problem& P, const lca_shard_desc* sd, const int64_t* global_tokens, int64_t num_global_tokens) {
+    if (sd == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "shard descriptor is NULL");
+    int st = parse_common(P, sd->dtype, sd->batch, sd->heads, sd->seq_len, sd->head_dim, sd->window_size, sd->scale,
+                          global_tokens, num_global_tokens);
+    if (st != LCA_OK) return st;
+    if (sd->world_size < 1) return fail(LCA_ERR_INVALID_ARGUMENT, "world_size must be >= 1");
+    if (sd->shard_offset < 0 || sd->shard_len < 1 || sd->shard_offset + sd->shard_len > sd->seq_len)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "shard [%lld, %lld) is not inside the sequence of %lld tokens",
+                    (long long)sd->shard_offset, (long long)(sd->shard_offset + sd->shard_len), (long long)sd->seq_len);
+    const bool last = sd->shard_offset + sd->shard_len == sd->seq_len;
+    if (!last && sd->shard_len % lca::kTileRows != 0)
+        return fail(LCA_ERR_UNSUPPORTED, "a shard other than the last must hold a multiple of %d tokens (got %lld)",
+                    lca::kTileRows, (long long)sd->shard_len);
+    if (sd->world_size > 1 && P.window > sd->shard_len)
+        return fail(LCA_ERR_UNSUPPORTED,
+                    "window %lld exceeds the shard length %lld: halos come from the adjacent shards only",
+                    (long long)P.window, (long long)sd->shard_len);
+    P.sharded = true;
+    P.world = sd->world_size;
+    P.n = sd->shard_len;
+    P.q_off = sd->shard_offset;
+    return LCA_OK;
+}
+
+// ------------------------------------------------------------------ workspace layout
 
 constexpr int kMinGrowUnits = 148;  // at least one global-row unit per SM when possible
 constexpr size_t kAlign = 1024;
@@ -115,48 +205,58 @@ constexpr size_t kAlign = 1024;
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct Layout {
-    int64_t bh = 0, n = 0, d = 0, G = 0;
-    int g_tiles = 0, gpad = 0, key_tiles = 0, n_splits = 0, split_tiles = 0;
-    size_t off_gidx = 0, off_qg = 0, off_kg = 0, off_vg = 0, off_po = 0, off_plse = 0, total = 0;
+    int g_tiles = 0, key_tiles = 0, n_splits = 0, split_tiles = 0;
+    size_t gbytes = 0;  // one compact [bh][G][d] buffer
+    size_t off_gidx = 0, off_globals = 0, off_po = 0, off_plse = 0;
+    size_t off_send = 0, off_recv = 0, halo_block = 0;  // halo_block: one side, [2][bh][halo][d]
+    size_t off_rowpart = 0, rowpart_bytes = 0, off_rowpart_all = 0;
+    size_t total = 0;
 };
 
-// Split of the n keys for the global-row units.  A unit covers `split_tiles` key tiles
-// (its two query-tile warpgroups take alternate tiles), sized at about twice a band
-// unit's work so units stay similar in length, but shrunk until there are enough units
-// to occupy every SM.  Each split yields two partial results (even / odd tiles).
-Layout make_layout(int64_t bh, int64_t n, int64_t d, int64_t G, int64_t window) {
+// Split of the keys of the global-row units (all n keys, or the shard's own).  A unit
+// covers `split_tiles` key tiles (its two query-tile warpgroups take alternate tiles),
+// sized at about twice a band unit's work so units stay similar in length, but shrunk
+// until there are enough units to occupy every SM.  Each split yields two partial
+// results (even / odd tiles).
+Layout make_layout(const Problem& P) {
     Layout L;
-    L.bh = bh;
-    L.n = n;
-    L.d = d;
-    L.G = G;
-    if (G <= 0 || bh <= 0 || n <= 0) return L;
-    L.g_tiles = (int)((G + lca::kTileRows - 1) / lca::kTileRows);
-    L.gpad = L.g_tiles * lca::kTileRows;
-    L.key_tiles = (int)((n + lca::kTileRows - 1) / lca::kTileRows);
-    const int64_t w = std::min(window, n);
-    const int64_t band_tiles = (2 * w + 2 * lca::kTileRows - 1) / lca::kTileRows + L.g_tiles;
-    int64_t split = std::max<int64_t>(4, std::min<int64_t>(64, 4 * band_tiles));
-    const int64_t units_per_split_count = bh * L.g_tiles;
-    while (split > 2 && units_per_split_count * ((L.key_tiles + split - 1) / split) < kMinGrowUnits) split -= 2;
-    split += split & 1;
-    L.split_tiles = (int)split;
-    L.n_splits = (L.key_tiles + L.split_tiles - 1) / L.split_tiles;
-    const int64_t parts = 2 * (int64_t)L.n_splits;
+    const int64_t bh = P.bh, G = P.G, d = P.d;
     size_t off = 0;
-    L.off_gidx = off;
-    off = align_up(off + sizeof(int) * L.gpad, kAlign);
-    const size_t gbytes = (size_t)bh * L.gpad * d * 2;
-    L.off_qg = off;
-    off = align_up(off + gbytes, kAlign);
-    L.off_kg = off;
-    off = align_up(off + gbytes, kAlign);
-    L.off_vg = off;
-    off = align_up(off + gbytes, kAlign);
-    L.off_po = off;
-    off = align_up(off + (size_t)parts * bh * L.gpad * d * 4, kAlign);
-    L.off_plse = off;
-    off = align_up(off + (size_t)parts * bh * L.gpad * 4, kAlign);
+    if (G > 0 && bh > 0 && P.n > 0) {
+        L.g_tiles = (int)((G + lca::kTileRows - 1) / lca::kTileRows);
+        L.key_tiles = (int)((P.n + lca::kTileRows - 1) / lca::kTileRows);
+        const int64_t band_tiles = (P.lead() + P.window + 2 * lca::kTileRows - 1) / lca::kTileRows + L.g_tiles;
+        int64_t split = std::max<int64_t>(4, std::min<int64_t>(64, 4 * band_tiles));
+        const int64_t units_per_split_count = bh * L.g_tiles;
+        while (split > 2 && units_per_split_count * ((L.key_tiles + split - 1) / split) < kMinGrowUnits) split -= 2;
+        split += split & 1;
+        L.split_tiles = (int)split;
+        L.n_splits = (L.key_tiles + L.split_tiles - 1) / L.split_tiles;
+        const int64_t parts = 2 * (int64_t)L.n_splits;
+        L.off_gidx = off;
+        off = align_up(off + sizeof(int) * G, kAlign);
+        L.gbytes = (size_t)bh * G * d * 2;
+        L.off_globals = off;  // q, k, v compact rows back to back
+        off = align_up(off + 3 * L.gbytes, kAlign);
+        L.off_po = off;
+        off = align_up(off + (size_t)parts * bh * G * d * 4, kAlign);
+        L.off_plse = off;
+        off = align_up(off + (size_t)parts * bh * G * 4, kAlign);
+        if (P.sharded) {
+            L.rowpart_bytes = (size_t)bh * G * (d + 1) * 4;  // O [bh][G][d], then LSE [bh][G]
+            L.off_rowpart = off;
+            off = align_up(off + L.rowpart_bytes, kAlign);
+            L.off_rowpart_all = off;
+            off = align_up(off + L.rowpart_bytes * (size_t)P.world, kAlign);
+        }
+    }
+    if (P.halo() > 0 && bh > 0) {
+        L.halo_block = (size_t)2 * bh * P.halo() * d * 2;
+        L.off_send = off;
+        off = align_up(off + 2 * L.halo_block, kAlign);
+        L.off_recv = off;
+        off = align_up(off + 2 * L.halo_block, kAlign);
+    }
     L.total = off;
     return L;
 }
@@ -189,6 +289,177 @@ unsigned long long wait_timeout_ns() {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_workspace(const Layout& L, void* workspace, size_t workspace_bytes) {
+    if (workspace_bytes < L.total)
+        return fail(LCA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+    if (L.total > 0 && (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) % 256) != 0))
+        return fail(LCA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
+    return LCA_OK;
+}
+
+int check_io(const void* q, const void* k, const void* v, const void* out, const float* lse) {
+    if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "q, k, v and out must be non-NULL");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(LCA_ERR_INVALID_ARGUMENT, "q, k, v and out must be 16-byte aligned");
+    if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u))
+        return fail(LCA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
+    return LCA_OK;
+}
+
+// ------------------------------------------------------------------ launch steps
+
+// Compact copies of the global rows this problem's Q / K / V hold (zeros for global rows
+// owned by other shards) and the sorted index list.
+int enqueue_gather(const Problem& P, const Layout& L, const void* q, const void* k, const void* v, uint8_t* ws,
+                   cudaStream_t stream) {
+    if (P.G == 0) return LCA_OK;
+    static thread_local lca::GatherParams gp;
+    uint8_t* qg = ws + L.off_globals;
+    for (int first = 0; first < (int)P.G; first += lca::kGatherChunk) {
+        gp.n = (int)P.n;
+        gp.q_off = (int)P.q_off;
+        gp.num_global = (int)P.G;
+        gp.bh = (int)P.bh;
+        gp.first = first;
+        gp.count = std::min<int>(lca::kGatherChunk, (int)P.G - first);
+        gp.gidx_out = reinterpret_cast<int*>(ws + L.off_gidx);
+        gp.qg = reinterpret_cast<uint16_t*>(qg);
+        gp.kg = reinterpret_cast<uint16_t*>(qg + L.gbytes);
+        gp.vg = reinterpret_cast<uint16_t*>(qg + 2 * L.gbytes);
+        for (int i = 0; i < gp.count; ++i) gp.idx[i] = P.gl[(size_t)first + i];
+        cudaError_t e = lca::launch_gather((int)P.d, q, k, v, gp, (int)P.bh, stream);
+        if (e != cudaSuccess) return fail_cuda(e, "gather launch");
+    }
+    return LCA_OK;
+}
+
+// The main kernel over band and global-row units.
+int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, const void* q, const void* k,
+                 const void* v, float* out, float* lse, uint8_t* ws, cudaStream_t stream) {
+    const bool bf16 = P.dtype == LCA_DTYPE_BF16;
+    const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int n = (int)P.n;
+    const int d = (int)P.d;
+    const uint64_t bh = (uint64_t)P.bh;
+    int st;
+    lca::TensorMaps tm;
+    memset(&tm, 0, sizeof(tm));
+    if ((st = encode_3d(&tm.q, tdt, 2, q, d, n, bh, 64, "q")) != LCA_OK) return st;
+    if ((st = encode_3d(&tm.k, tdt, 2, k, d, n, bh, 64, "k")) != LCA_OK) return st;
+    if ((st = encode_3d(&tm.v, tdt, 2, v, d, n, bh, 64, "v")) != LCA_OK) return st;
+    if ((st = encode_3d(&tm.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, d, n, bh, 32, "out")) != LCA_OK) return st;
+
+    lca::MainParams p;
+    memset(&p, 0, sizeof(p));
+    p.n = n;
+    p.q_off = (int)P.q_off;
+    p.n_total = (int)P.n_total;
+    p.sharded = P.sharded ? 1 : 0;
+    p.halo = (int)P.halo();
+    p.bh = (int)P.bh;
+    p.window = (int)P.window;
+    p.lead = (int)P.lead();
+    p.key_lo = (int)std::max<int64_t>(0, P.q_off - P.window);
+    p.key_hi = (int)std::min<int64_t>(P.n_total, P.q_off + P.n + P.window);
+    if (!P.sharded) {
+        p.key_lo = 0;
+        p.key_hi = n;
+    }
+    p.gk_lo = (int)P.q_off;
+    p.gk_n = n;
+    p.q_tiles = (n + lca::kTileRows - 1) / lca::kTileRows;
+    p.num_global = (int)P.G;
+    p.scale_log2 = P.scale * 1.4426950408889634f;
+    // scale == 0 gives every visible key the same weight; a tiny positive factor keeps
+    // that (scores * 1e-30 round to 0 in the exponent) while masked scores stay -inf.
+    if (p.scale_log2 == 0.f) p.scale_log2 = 1e-30f;
+    p.lse = lse;
+    p.err = err_word;
+    p.timeout_ns = wait_timeout_ns();
+
+    if (p.halo > 0) {
+        // recv block [2 sides][2 (k, v)][bh][halo][d]: K planes at z = side * 2bh + b from
+        // the block start, V planes the same from bh planes further on
+        uint8_t* recv = ws + L.off_recv;
+        const size_t plane = (size_t)p.halo * d * 2;
+        if ((st = encode_3d(&tm.kh, tdt, 2, recv, d, p.halo, 4 * bh, 64, "k_halo")) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.vh, tdt, 2, recv + bh * plane, d, p.halo, 3 * bh, 64, "v_halo")) != LCA_OK)
+            return st;
+    } else {
+        tm.kh = tm.k;
+        tm.vh = tm.v;
+    }
+    if (P.G > 0) {
+        p.g_tiles = L.g_tiles;
+        p.n_splits = L.n_splits;
+        p.split_tiles = L.split_tiles;
+        p.n_grow_units = (int)(P.bh * L.g_tiles * L.n_splits);
+        p.gidx = reinterpret_cast<const int*>(ws + L.off_gidx);
+        p.part_lse = reinterpret_cast<float*>(ws + L.off_plse);
+        uint8_t* qg = ws + L.off_globals;
+        const uint64_t G = (uint64_t)P.G;
+        if ((st = encode_3d(&tm.qg, tdt, 2, qg, d, G, bh, 64, "q_global")) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.kg, tdt, 2, qg + L.gbytes, d, G, bh, 64, "k_global")) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.vg, tdt, 2, qg + 2 * L.gbytes, d, G, bh, 64, "v_global")) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.po, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.off_po, d, G,
+                            (uint64_t)2 * L.n_splits * bh, 32, "partial_out")) != LCA_OK)
+            return st;
+    } else {
+        // unused maps still need valid encodings for the kernel parameter block
+        tm.qg = tm.q;
+        tm.kg = tm.k;
+        tm.vg = tm.v;
+        tm.po = tm.o;
+    }
+
+    p.q_pairs = (p.q_tiles + 1) / 2;
+    const long long units = (long long)p.n_grow_units + (long long)P.bh * p.q_pairs;
+    if (units > INT_MAX) return fail(LCA_ERR_UNSUPPORTED, "problem too large (%lld work units)", units);
+    p.n_band_units = (int)(P.bh * p.q_pairs);
+    const int grid = (int)std::min<long long>(units, g_dev_sms[dev]);
+    const bool timed = g_ev_before_main != nullptr && g_ev_after_main != nullptr;
+    cudaError_t e;
+    if (timed && (e = cudaEventRecord(g_ev_before_main, stream)) != cudaSuccess)
+        return fail_cuda(e, "timing event record");
+    e = lca::launch_main(d, bf16, tm, p, grid, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "main kernel launch");
+    if (timed && (e = cudaEventRecord(g_ev_after_main, stream)) != cudaSuccess)
+        return fail_cuda(e, "timing event record");
+    return LCA_OK;
+}
+
+// Merge of the main kernel's global-row partials: over the rows of out / lse, or (for a
+// shard) into this shard's packed row partial.
+int enqueue_combine_splits(const Problem& P, const Layout& L, float* out, float* lse, uint8_t* ws,
+                           cudaStream_t stream) {
+    if (P.G == 0) return LCA_OK;
+    lca::CombineParams cp;
+    memset(&cp, 0, sizeof(cp));
+    cp.bh = (int)P.bh;
+    cp.num_global = (int)P.G;
+    cp.n_parts = 2 * L.n_splits;
+    cp.split_tiles = L.split_tiles;
+    cp.split_keys = (int)P.n;
+    cp.part_stride_o = (size_t)P.bh * P.G * P.d;
+    cp.part_stride_lse = (size_t)P.bh * P.G;
+    cp.part_o = reinterpret_cast<const float*>(ws + L.off_po);
+    cp.part_lse = reinterpret_cast<const float*>(ws + L.off_plse);
+    cp.gidx = reinterpret_cast<const int*>(ws + L.off_gidx);
+    if (P.sharded) {
+        cp.out_o = reinterpret_cast<float*>(ws + L.off_rowpart);
+        cp.out_lse = cp.out_o + (size_t)P.bh * P.G * P.d;
+    } else {
+        cp.o = out;
+        cp.lse = lse;
+        cp.n_rows = (int)P.n;
+        cp.row_off = 0;
+    }
+    cudaError_t e = lca::launch_combine((int)P.d, cp, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "combine launch");
+    return LCA_OK;
+}
 
 }  // namespace
 
@@ -242,11 +513,17 @@ int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_
     if (out_bytes == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "out_bytes is NULL");
     if (batch < 0 || heads < 0 || seq_len < 0 || num_unique_global < 0)
         return fail(LCA_ERR_INVALID_ARGUMENT, "negative size");
-    if (dtype != LCA_DTYPE_F16 && dtype != LCA_DTYPE_BF16) return fail(LCA_ERR_UNSUPPORTED, "dtype %d", dtype);
-    if (head_dim != 64 && head_dim != 128)
-        return fail(LCA_ERR_UNSUPPORTED, "head_dim %lld (supported: 64, 128)", (long long)head_dim);
+    int st = check_dtype_dim(dtype, head_dim);
+    if (st != LCA_OK) return st;
     if (window_size < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "window_size must be >= 0");
-    *out_bytes = make_layout(batch * heads, seq_len, head_dim, std::min(num_unique_global, seq_len), window_size).total;
+    Problem P;
+    P.bh = batch * heads;
+    P.n_total = P.n = seq_len;
+    P.d = head_dim;
+    P.window = std::min(window_size, seq_len);
+    P.G = std::min(num_unique_global, seq_len);
+    P.dtype = dtype;
+    *out_bytes = make_layout(P).total;
     return LCA_OK;
 }
 
@@ -255,150 +532,135 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
                     float scale, const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
                     size_t workspace_bytes, void* stream_ptr) {
     g_last_error.clear();
-    // ---- argument checks (csrc/bindings.cpp:25-42 restated for a C caller)
-    if (dtype != LCA_DTYPE_F16 && dtype != LCA_DTYPE_BF16)
-        return fail(LCA_ERR_UNSUPPORTED, "dtype %d is not supported (fp16 or bf16 inputs)", dtype);
-    if (head_dim != 64 && head_dim != 128)
-        return fail(LCA_ERR_UNSUPPORTED, "head_dim %lld is not supported (64 or 128)", (long long)head_dim);
-    if (batch < 0 || heads < 0 || seq_len < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "negative shape");
-    if (window_size < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "window_size must be >= 0 (got %lld)", (long long)window_size);
-    if (seq_len > ((int64_t)1 << 29))
-        return fail(LCA_ERR_UNSUPPORTED, "seq_len %lld too large (max 2^29)", (long long)seq_len);
-    const int64_t bh = batch * heads;
-    if (bh > INT_MAX / 64) return fail(LCA_ERR_UNSUPPORTED, "batch*heads %lld too large", (long long)bh);
-    if (num_global_tokens < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "negative global token count");
-    if (num_global_tokens > 0 && global_tokens == nullptr)
-        return fail(LCA_ERR_INVALID_ARGUMENT, "global_tokens is NULL");
-
-    // Global tokens are validated even for empty problems, as the reference's mask
-    // construction would raise on them.
-    std::vector<int32_t> gl((size_t)num_global_tokens + 1);
-    int64_t G = 0;
-    int st = lca_normalize_global_tokens(global_tokens, num_global_tokens, seq_len, gl.data(), &G);
+    Problem P;
+    int st = parse_common(P, dtype, batch, heads, seq_len, head_dim, window_size, scale, global_tokens,
+                          num_global_tokens);
     if (st != LCA_OK) return st;
-    if (bh == 0 || seq_len == 0) return LCA_OK;  // nothing to compute
-
-    if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
-        return fail(LCA_ERR_INVALID_ARGUMENT, "q, k, v and out must be non-NULL");
-    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
-        return fail(LCA_ERR_INVALID_ARGUMENT, "q, k, v and out must be 16-byte aligned");
-    if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u))
-        return fail(LCA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
-
+    if (P.bh == 0 || P.n == 0) return LCA_OK;  // nothing to compute
+    if ((st = check_io(q, k, v, out, lse)) != LCA_OK) return st;
     int dev = 0;
     int* err_word = nullptr;
-    st = check_device(&dev, &err_word);
-    if (st != LCA_OK) return st;
-
-    const Layout L = make_layout(bh, seq_len, head_dim, G, window_size);
-    if (workspace_bytes < L.total) return fail(LCA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
-    if (L.total > 0 && (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) % 256) != 0))
-        return fail(LCA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
-
+    if ((st = check_device(&dev, &err_word)) != LCA_OK) return st;
+    const Layout L = make_layout(P);
+    if ((st = check_workspace(L, workspace, workspace_bytes)) != LCA_OK) return st;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    const bool bf16 = dtype == LCA_DTYPE_BF16;
-    const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const int n = (int)seq_len;
-    const int d = (int)head_dim;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
+    // 1. gather the global rows, 2. band + global-row units, 3. merge the global-row splits
+    if ((st = enqueue_gather(P, L, q, k, v, ws, stream)) != LCA_OK) return st;
+    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream)) != LCA_OK) return st;
+    return enqueue_combine_splits(P, L, out, lse, ws, stream);
+}
 
-    lca::TensorMaps tm;
-    memset(&tm, 0, sizeof(tm));
-    if ((st = encode_3d(&tm.q, tdt, 2, q, d, n, bh, 64, "q")) != LCA_OK) return st;
-    if ((st = encode_3d(&tm.k, tdt, 2, k, d, n, bh, 64, "k")) != LCA_OK) return st;
-    if ((st = encode_3d(&tm.v, tdt, 2, v, d, n, bh, 64, "v")) != LCA_OK) return st;
-    if ((st = encode_3d(&tm.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, d, n, bh, 32, "out")) != LCA_OK) return st;
+// ------------------------------------------------------------------ sequence shards
 
-    lca::MainParams p;
-    memset(&p, 0, sizeof(p));
-    p.n = n;
-    p.bh = (int)bh;
-    p.window = (int)std::min<int64_t>(window_size, seq_len);
-    p.q_tiles = (n + lca::kTileRows - 1) / lca::kTileRows;
-    p.num_global = (int)G;
-    p.scale_log2 = scale * 1.4426950408889634f;
-    // scale == 0 gives every visible key the same weight; a tiny positive factor keeps
-    // that (scores * 1e-30 round to 0 in the exponent) while masked scores stay -inf.
-    if (p.scale_log2 == 0.f) p.scale_log2 = 1e-30f;
-    p.lse = lse;
-    p.err = err_word;
-    p.timeout_ns = wait_timeout_ns();
+int lca_swa_shard_layout(const lca_shard_desc* desc, int64_t num_unique_global, lca_shard_layout* out) {
+    if (out == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "out is NULL");
+    if (num_unique_global < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "negative global count");
+    Problem P;
+    int st = parse_shard(P, desc, nullptr, 0);
+    if (st != LCA_OK) return st;
+    P.G = std::min(num_unique_global, P.n_total);
+    const Layout L = make_layout(P);
+    memset(out, 0, sizeof(*out));
+    out->total_bytes = L.total;
+    out->halo_rows = P.halo();
+    out->globals_offset = L.off_globals;
+    out->globals_bytes = 3 * L.gbytes;
+    out->halo_send_offset = L.off_send;
+    out->halo_recv_offset = L.off_recv;
+    out->halo_side_bytes = L.halo_block;
+    out->rowpart_offset = L.off_rowpart;
+    out->rowpart_bytes = L.rowpart_bytes;
+    out->rowpart_all_offset = L.off_rowpart_all;
+    return LCA_OK;
+}
 
-    if (G > 0) {
-        p.g_tiles = L.g_tiles;
-        p.gpad = L.gpad;
-        p.n_splits = L.n_splits;
-        p.split_tiles = L.split_tiles;
-        p.n_grow_units = (int)(bh * L.g_tiles * L.n_splits);
-        p.gidx = reinterpret_cast<const int*>(ws + L.off_gidx);
-        p.part_lse = reinterpret_cast<float*>(ws + L.off_plse);
-        void* qg = ws + L.off_qg;
-        void* kg = ws + L.off_kg;
-        void* vg = ws + L.off_vg;
-        if ((st = encode_3d(&tm.qg, tdt, 2, qg, d, L.gpad, bh, 64, "q_global")) != LCA_OK) return st;
-        if ((st = encode_3d(&tm.kg, tdt, 2, kg, d, L.gpad, bh, 64, "k_global")) != LCA_OK) return st;
-        if ((st = encode_3d(&tm.vg, tdt, 2, vg, d, L.gpad, bh, 64, "v_global")) != LCA_OK) return st;
-        if ((st = encode_3d(&tm.po, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.off_po, d, L.gpad,
-                            (uint64_t)2 * L.n_splits * bh, 32, "partial_out")) != LCA_OK)
-            return st;
-
-        // 1. gather the global rows (chunks of kGatherChunk indices per launch)
-        static thread_local lca::GatherParams gp;
-        for (int first = 0; first < L.gpad; first += lca::kGatherChunk) {
-            gp.n = n;
-            gp.gpad = L.gpad;
-            gp.num_global = (int)G;
-            gp.bh = (int)bh;
-            gp.first = first;
-            gp.count = std::min(lca::kGatherChunk, L.gpad - first);
-            gp.gidx_out = reinterpret_cast<int*>(ws + L.off_gidx);
-            gp.qg = static_cast<uint16_t*>(qg);
-            gp.kg = static_cast<uint16_t*>(kg);
-            gp.vg = static_cast<uint16_t*>(vg);
-            for (int i = 0; i < gp.count; ++i) gp.idx[i] = (first + i < G) ? gl[first + i] : 0;
-            cudaError_t e = lca::launch_gather(d, q, k, v, gp, (int)bh, stream);
-            if (e != cudaSuccess) return fail_cuda(e, "gather launch");
-        }
-    } else {
-        // unused maps still need valid encodings for the kernel parameter block
-        tm.qg = tm.q;
-        tm.kg = tm.k;
-        tm.vg = tm.v;
-        tm.po = tm.o;
+int lca_swa_shard_prepare(const lca_shard_desc* desc, const void* q, const void* k, const void* v,
+                          const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
+                          size_t workspace_bytes, void* stream_ptr) {
+    g_last_error.clear();
+    Problem P;
+    int st = parse_shard(P, desc, global_tokens, num_global_tokens);
+    if (st != LCA_OK) return st;
+    if (P.bh == 0) return LCA_OK;
+    if (q == nullptr || k == nullptr || v == nullptr || !aligned16(q) || !aligned16(k) || !aligned16(v))
+        return fail(LCA_ERR_INVALID_ARGUMENT, "q, k and v must be non-NULL and 16-byte aligned");
+    int dev = 0;
+    int* err_word = nullptr;
+    if ((st = check_device(&dev, &err_word)) != LCA_OK) return st;
+    const Layout L = make_layout(P);
+    if ((st = check_workspace(L, workspace, workspace_bytes)) != LCA_OK) return st;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if ((st = enqueue_gather(P, L, q, k, v, ws, stream)) != LCA_OK) return st;
+    if (P.halo() > 0) {
+        lca::HaloPackParams hp;
+        hp.n = (int)P.n;
+        hp.halo = (int)P.halo();
+        hp.bh = (int)P.bh;
+        hp.d = (int)P.d;
+        hp.k = static_cast<const uint16_t*>(k);
+        hp.v = static_cast<const uint16_t*>(v);
+        hp.send = reinterpret_cast<uint16_t*>(ws + L.off_send);
+        cudaError_t e = lca::launch_halo_pack(hp, stream);
+        if (e != cudaSuccess) return fail_cuda(e, "halo pack launch");
     }
+    return LCA_OK;
+}
 
-    // 2. band + global-row units
-    p.q_pairs = (p.q_tiles + 1) / 2;
-    const long long units = (long long)p.n_grow_units + (long long)bh * p.q_pairs;
-    if (units > INT_MAX) return fail(LCA_ERR_UNSUPPORTED, "problem too large (%lld work units)", units);
-    p.n_band_units = (int)(bh * p.q_pairs);
-    const int grid = (int)std::min<long long>(units, g_dev_sms[dev]);
-    const bool timed = g_ev_before_main != nullptr && g_ev_after_main != nullptr;
-    cudaError_t e;
-    if (timed && (e = cudaEventRecord(g_ev_before_main, stream)) != cudaSuccess)
-        return fail_cuda(e, "timing event record");
-    e = lca::launch_main(d, bf16, tm, p, grid, stream);
-    if (e != cudaSuccess) return fail_cuda(e, "main kernel launch");
-    if (timed && (e = cudaEventRecord(g_ev_after_main, stream)) != cudaSuccess)
-        return fail_cuda(e, "timing event record");
+int lca_swa_shard_forward(const lca_shard_desc* desc, const void* q, const void* k, const void* v, float* out,
+                          float* lse, const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
+                          size_t workspace_bytes, void* stream_ptr) {
+    g_last_error.clear();
+    Problem P;
+    int st = parse_shard(P, desc, global_tokens, num_global_tokens);
+    if (st != LCA_OK) return st;
+    if (P.bh == 0) return LCA_OK;
+    if ((st = check_io(q, k, v, out, lse)) != LCA_OK) return st;
+    int dev = 0;
+    int* err_word = nullptr;
+    if ((st = check_device(&dev, &err_word)) != LCA_OK) return st;
+    const Layout L = make_layout(P);
+    if ((st = check_workspace(L, workspace, workspace_bytes)) != LCA_OK) return st;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream)) != LCA_OK) return st;
+    return enqueue_combine_splits(P, L, out, lse, ws, stream);
+}
 
-    // 3. merge the global-row splits over the global rows of out / lse
-    if (G > 0) {
-        lca::CombineParams cp;
-        cp.n = n;
-        cp.bh = (int)bh;
-        cp.gpad = L.gpad;
-        cp.num_global = (int)G;
-        cp.n_splits = L.n_splits;
-        cp.split_tiles = L.split_tiles;
-        cp.gidx = p.gidx;
-        cp.part_o = reinterpret_cast<const float*>(ws + L.off_po);
-        cp.part_lse = p.part_lse;
-        cp.o = out;
-        cp.lse = lse;
-        e = lca::launch_combine(d, cp, stream);
-        if (e != cudaSuccess) return fail_cuda(e, "combine launch");
-    }
+int lca_swa_shard_finish(const lca_shard_desc* desc, float* out, float* lse, const int64_t* global_tokens,
+                         int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+    g_last_error.clear();
+    Problem P;
+    int st = parse_shard(P, desc, global_tokens, num_global_tokens);
+    if (st != LCA_OK) return st;
+    if (P.bh == 0 || P.G == 0) return LCA_OK;
+    if (out == nullptr || !aligned16(out)) return fail(LCA_ERR_INVALID_ARGUMENT, "out must be non-NULL and 16-byte aligned");
+    if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u))
+        return fail(LCA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
+    int dev = 0;
+    int* err_word = nullptr;
+    if ((st = check_device(&dev, &err_word)) != LCA_OK) return st;
+    const Layout L = make_layout(P);
+    if ((st = check_workspace(L, workspace, workspace_bytes)) != LCA_OK) return st;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    lca::CombineParams cp;
+    memset(&cp, 0, sizeof(cp));
+    cp.bh = (int)P.bh;
+    cp.num_global = (int)P.G;
+    cp.n_parts = (int)P.world;
+    cp.split_tiles = 0;  // every shard's partial is present
+    cp.part_stride_o = L.rowpart_bytes / 4;
+    cp.part_stride_lse = L.rowpart_bytes / 4;
+    cp.part_o = reinterpret_cast<const float*>(ws + L.off_rowpart_all);
+    cp.part_lse = cp.part_o + (size_t)P.bh * P.G * P.d;
+    cp.gidx = reinterpret_cast<const int*>(ws + L.off_gidx);
+    cp.o = out;
+    cp.lse = lse;
+    cp.n_rows = (int)P.n;
+    cp.row_off = (int)P.q_off;
+    cudaError_t e = lca::launch_combine((int)P.d, cp, static_cast<cudaStream_t>(stream_ptr));
+    if (e != cudaSuccess) return fail_cuda(e, "shard combine launch");
     return LCA_OK;
 }
 

@@ -5,13 +5,14 @@
 // i is a global token.  Output is fp32 softmax(scale * Q K^T restricted to that mask) V.
 //
 // Three launches per forward:
-//   1. lca_gather_globals : copies the G global rows of Q, K, V into compact,
-//                           zero-padded [bh][gpad][d] buffers (gpad = 128 * ceil(G/128))
-//                           and writes the sorted index list.
+//   1. lca_gather_globals : copies the G global rows of Q, K, V into compact [bh][G][d]
+//                           buffers (TMA reads rows >= G as zeros) and writes the sorted
+//                           index list.
 //   2. lca_swa_main       : persistent, one CTA per SM, looping over work units:
 //        band unit      : two adjacent 128-row query tiles A, B of one (batch, head).
 //                         Key tiles: the band [q0 - w, q0 + 255 + w] in 128-key tiles
-//                         starting at q0 - w (A uses the first ceil((2w+128)/128) of
+//                         starting at q0 - lead (lead = w, or w rounded up to 128 for a
+//                         sequence shard; A uses the first ceil((lead+w+128)/128) of
 //                         them, B the same count shifted by one; each tile is loaded
 //                         once for both), out-of-band and out-of-range tiles are never
 //                         issued; then the compact global-key tiles, masked so a global
@@ -20,12 +21,14 @@
 //                         query-to-global-keys + combine kernels (csrc/global_attention.cu:
 //                         104-152, csrc/combine.cu:18-56), merged in the online softmax.
 //        global-row unit: the compact global queries (one 128-row tile, loaded as both A
-//                         and B) against one contiguous split of all n keys, A taking the
-//                         even key tiles and B the odd ones; each writes a normalised
-//                         partial O and its log-sum-exp.  Replaces
-//                         csrc/global_attention.cu:29-96.
+//                         and B) against one contiguous split of the keys (all n, or the
+//                         shard's own), A taking the even key tiles and B the odd ones;
+//                         each writes a normalised partial O and its log-sum-exp.
+//                         Replaces csrc/global_attention.cu:29-96.
 //   3. lca_combine_global_rows : log-sum-exp merge of the partials, written over the
-//                           global rows of O (and LSE).
+//                           global rows of O (and LSE), or, for a sequence shard, into a
+//                           per-shard partial that a second merge across shards finishes.
+// Sequence shards add lca_pack_halo (the K / V rows the neighbours need as their halo).
 //
 // Main-kernel CTA layout.  Each query tile X (A or B) is served by H softmax warpgroups
 // (H = 2 for d = 64, 1 for d = 128); warpgroup (X, h) owns key columns
@@ -51,6 +54,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <algorithm>
 #include <climits>
 
 #include "sm100_ptx.cuh"
@@ -125,9 +129,9 @@ struct Unit {
     bool grow;        // global-row unit
     bool active[2];   // query tile A / B has work
     int bh;           // (batch * heads) index
-    int qrow[2];      // first query row of A / B (band: absolute; grow: compact)
+    int qrow[2];      // first query row of A / B (band: local; grow: compact)
     int ntiles;       // issued key tiles
-    int kstart;       // band: key index of pair tile 0 (= q0 - w)
+    int kstart;       // band: absolute key index of pair tile 0 (= q_off + q0 - lead)
     int p_lo;         // band: first issued pair tile
     int nA;           // band: pair tiles used by each query tile
     int num_band;     // band: issued band tiles
@@ -151,8 +155,8 @@ __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
         const int gt = rest % p.g_tiles;
         un.bh = rest / p.g_tiles;
         un.qrow[0] = un.qrow[1] = gt * BM;
-        un.k0 = un.split * p.split_tiles * BN;
-        const int rem = (p.n - un.k0 + BN - 1) / BN;
+        un.k0 = p.gk_lo + un.split * p.split_tiles * BN;
+        const int rem = (p.gk_lo + p.gk_n - un.k0 + BN - 1) / BN;
         un.ntiles = rem < p.split_tiles ? rem : p.split_tiles;
         un.active[0] = true;
         un.active[1] = un.ntiles >= 2;
@@ -168,11 +172,11 @@ __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
         un.qrow[1] = q0 + BM;
         un.active[0] = true;
         un.active[1] = q0 + BM < p.n;
-        un.kstart = q0 - p.window;
-        un.nA = (2 * p.window + BM + BN - 1) / BN;
-        const int p_first = un.kstart < 0 ? (-un.kstart) / BN : 0;
+        un.kstart = p.q_off + q0 - p.lead;
+        un.nA = (p.lead + p.window + BM + BN - 1) / BN;
+        const int p_first = un.kstart < p.key_lo ? (p.key_lo - un.kstart) / BN : 0;
         int p_last = un.active[1] ? un.nA : un.nA - 1;
-        const int p_overlap_last = (p.n - 1 - un.kstart) / BN;
+        const int p_overlap_last = (p.key_hi - 1 - un.kstart) / BN;
         if (p_overlap_last < p_last) p_last = p_overlap_last;
         un.p_lo = p_first;
         un.num_band = p_last - p_first + 1;
@@ -225,7 +229,8 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk16) {
 template <int D, bool BF16>
 __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
     lca_swa_main(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qg,
+                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kh,
+                 const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_qg,
                  const __grid_constant__ CUtensorMap tm_kg, const __grid_constant__ CUtensorMap tm_vg,
                  const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_po,
                  const MainParams p) {
@@ -279,6 +284,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                 ptx::prefetch_tmap(&tm_q);
                 ptx::prefetch_tmap(&tm_k);
                 ptx::prefetch_tmap(&tm_v);
+                if (p.sharded) {
+                    ptx::prefetch_tmap(&tm_kh);
+                    ptx::prefetch_tmap(&tm_vh);
+                }
                 int L = 0;   // K/V loads issued
                 int qn = 0;  // Q loads issued per tile buffer
                 bool ok = true;
@@ -310,12 +319,25 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                                 break;
                             }
                             const CUtensorMap* m = t.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
+                            int y = t.row0, z = un.bh;
+                            if (!t.global_key && p.sharded) {
+                                // the tile lies wholly in the left halo, the shard or the right halo
+                                if (y < p.q_off) {
+                                    m = kv ? &tm_vh : &tm_kh;
+                                    y -= p.q_off - p.halo;
+                                } else if (y >= p.q_off + p.n) {
+                                    m = kv ? &tm_vh : &tm_kh;
+                                    y -= p.q_off + p.n;
+                                    z += 2 * p.bh;
+                                } else {
+                                    y -= p.q_off;
+                                }
+                            }
                             uint8_t* dst = sSlots + slot * C::kTileBytes;
                             ptx::mbar_arrive_expect_tx(&ctl->kv_full[slot], C::kTileBytes);
 #pragma unroll
                             for (int pn = 0; pn < C::kPanels; ++pn)
-                                ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64, t.row0,
-                                                 un.bh);
+                                ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64, y, z);
                             ++L;
                         }
                     }
@@ -478,27 +500,28 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
             const bool active_x = X ? un.active[1] : un.active[0];
             if (!active_x) continue;
             const int qrow_x = X ? un.qrow[1] : un.qrow[0];
-            const int qi = qrow_x + r;
+            const int qi = qrow_x + r;         // local (band) or compact (global-row unit) row
+            const int qa = p.q_off + qi;       // band: absolute query index
             const bool live = un.grow ? (qi < p.num_global) : (qi < p.n);
             const bool warp_live = __any_sync(0xffffffffu, live);
             // row's visible keys in band / split tiles: [jlo, jhi] (absolute key index)
-            int jlo = 0, jhi = p.n - 1;
+            int jlo = p.gk_lo, jhi = p.gk_lo + p.gk_n - 1;
             // run [g_lo, g_hi) of sorted global indices inside the row's band (band units)
             int g_lo = 0, g_hi = 0;
             if (!un.grow) {
-                jlo = qi - p.window > 0 ? qi - p.window : 0;
-                jhi = (qi + p.window < p.n - 1) ? qi + p.window : p.n - 1;
+                jlo = qa - p.window > 0 ? qa - p.window : 0;
+                jhi = (qa + p.window < p.n_total - 1) ? qa + p.window : p.n_total - 1;
                 if (p.g_tiles > 0) {
                     int a = 0, b = p.num_global;
                     while (a < b) {
                         const int mid = (a + b) >> 1;
-                        if (__ldg(p.gidx + mid) < qi - p.window) a = mid + 1; else b = mid;
+                        if (__ldg(p.gidx + mid) < qa - p.window) a = mid + 1; else b = mid;
                     }
                     g_lo = a;
                     b = p.num_global;
                     while (a < b) {
                         const int mid = (a + b) >> 1;
-                        if (__ldg(p.gidx + mid) <= qi + p.window) a = mid + 1; else b = mid;
+                        if (__ldg(p.gidx + mid) <= qa + p.window) a = mid + 1; else b = mid;
                     }
                     g_hi = a;
                 }
@@ -722,7 +745,8 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
             if (ok && hh == 0) {
                 const float lse = (((M == -INFINITY) ? 0.f : M) + __log2f(Lsum)) * kLn2;
                 if (un.grow) {
-                    p.part_lse[((size_t)(2 * un.split + X) * p.bh + un.bh) * p.gpad + qi] = lse;
+                    if (qi < p.num_global)
+                        p.part_lse[((size_t)(2 * un.split + X) * p.bh + un.bh) * p.num_global + qi] = lse;
                 } else if (p.lse != nullptr && qi < p.n) {
                     p.lse[(size_t)un.bh * p.n + qi] = lse;
                 }
@@ -751,19 +775,42 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
     const int row = (int)(w % gp.count);
     const int bh = (int)(w / gp.count);
     const int g = gp.first + row;  // compact row index
-    const bool live = g < gp.num_global;
-    const int src_row = live ? gp.idx[row] : 0;
-    if (bh == 0 && lane == 0) gp.gidx_out[g] = live ? src_row : INT_MAX;
-    const size_t src_off = ((size_t)bh * gp.n + src_row) * D;
-    const size_t dst_off = ((size_t)bh * gp.gpad + g) * D;
+    const int src_abs = gp.idx[row];
+    const int src_row = src_abs - gp.q_off;
+    const bool owned = src_row >= 0 && src_row < gp.n;
+    if (bh == 0 && lane == 0) gp.gidx_out[g] = src_abs;
+    const size_t src_off = ((size_t)bh * gp.n + (owned ? src_row : 0)) * D;
+    const size_t dst_off = ((size_t)bh * gp.num_global + g) * D;
     for (int c = lane; c < 3 * kChunks; c += 32) {
         const int which = c / kChunks;
         const int cc = c % kChunks;
         const uint16_t* src = which == 0 ? q : (which == 1 ? k : v);
         uint16_t* dst = which == 0 ? gp.qg : (which == 1 ? gp.kg : gp.vg);
         uint4 val = make_uint4(0, 0, 0, 0);
-        if (live) val = *reinterpret_cast<const uint4*>(src + src_off + cc * 8);
+        if (owned) val = *reinterpret_cast<const uint4*>(src + src_off + cc * 8);
         *reinterpret_cast<uint4*>(dst + dst_off + cc * 8) = val;
+    }
+}
+
+// ------------------------------------------------------------------------ halo pack
+
+__global__ void __launch_bounds__(256) lca_pack_halo(HaloPackParams hp) {
+    // one thread per 16-byte chunk of send[2][2][bh][halo][d]
+    const int per_row = hp.d * 2 / 16;
+    const long long total = 4ll * hp.bh * hp.halo * per_row;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(i % per_row);
+        long long rest = i / per_row;
+        const int r = (int)(rest % hp.halo);
+        rest /= hp.halo;
+        const int b = (int)(rest % hp.bh);
+        rest /= hp.bh;
+        const int kv = (int)(rest & 1);
+        const int side = (int)(rest >> 1);
+        const int row = side == 0 ? r : hp.n - hp.halo + r;
+        const uint16_t* src = (kv ? hp.v : hp.k) + ((size_t)b * hp.n + row) * hp.d + c * 8;
+        *reinterpret_cast<uint4*>(hp.send + (size_t)i * 8) = *reinterpret_cast<const uint4*>(src);
     }
 }
 
@@ -771,33 +818,33 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
 
 template <int D>
 __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp) {
-    // One warp per (bh, global row).  Partial 2*s + x covers the key tiles of split s with
-    // parity x and exists only if that split has more than x tiles.  Lanes take partials
-    // in parallel for the max and the weights; the weighted sum then walks the partials
-    // with independent loads (lane = output column).
+    // One warp per (bh, global row).  Lanes take partials in parallel for the max and the
+    // weights; the weighted sum then walks the partials with independent loads (lane =
+    // output column).
     const long long w = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= (long long)cp.num_global * cp.bh) return;
     const int g = (int)(w % cp.num_global);
     const int bh = (int)(w / cp.num_global);
     constexpr int kPer = D / 32;
-    const int n_parts = 2 * cp.n_splits;
+    const size_t row = (size_t)bh * cp.num_global + g;
     auto valid = [&](int part) {
+        if (cp.split_tiles == 0) return true;
         const int s = part >> 1;
         const int first_key = s * cp.split_tiles * 128;
-        int tiles = (cp.n - first_key + 127) / 128;
+        int tiles = (cp.split_keys - first_key + 127) / 128;
         if (tiles > cp.split_tiles) tiles = cp.split_tiles;
         return tiles > (part & 1);
     };
     auto lse_of = [&](int part) {
-        return valid(part) ? __ldg(cp.part_lse + ((size_t)part * cp.bh + bh) * cp.gpad + g) : -INFINITY;
+        return valid(part) ? __ldg(cp.part_lse + (size_t)part * cp.part_stride_lse + row) : -INFINITY;
     };
     float mx = -INFINITY;
-    for (int s = lane; s < n_parts; s += 32) mx = fmaxf(mx, lse_of(s));
+    for (int s = lane; s < cp.n_parts; s += 32) mx = fmaxf(mx, lse_of(s));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float wsum = 0.f;
-    for (int s = lane; s < n_parts; s += 32) {
+    for (int s = lane; s < cp.n_parts; s += 32) {
         const float ls = lse_of(s);
         wsum += (ls == -INFINITY) ? 0.f : __expf(ls - mx);
     }
@@ -807,20 +854,29 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
 #pragma unroll
     for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
 #pragma unroll 4
-    for (int s = 0; s < n_parts; ++s) {
+    for (int s = 0; s < cp.n_parts; ++s) {
         const float ls = lse_of(s);
         if (ls == -INFINITY) continue;
         const float wt = __expf(ls - mx);
-        const float* po = cp.part_o + (((size_t)s * cp.bh + bh) * cp.gpad + g) * D;
+        const float* po = cp.part_o + (size_t)s * cp.part_stride_o + row * D;
 #pragma unroll
         for (int e = 0; e < kPer; ++e) acc[e] += wt * __ldg(po + lane + 32 * e);
     }
-    const int row = cp.gidx[g];
-    float* out = cp.o + ((size_t)bh * cp.n + row) * D;
     const float inv = 1.f / wsum;
+    const float lse = mx + __logf(wsum);
+    if (cp.out_o != nullptr) {
+        float* out = cp.out_o + row * D;
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) out[lane + 32 * e] = acc[e] * inv;
+        if (lane == 0) cp.out_lse[row] = lse;
+        return;
+    }
+    const int orow = cp.gidx[g] - cp.row_off;
+    if (orow < 0 || orow >= cp.n_rows) return;  // owned by another shard
+    float* out = cp.o + ((size_t)bh * cp.n_rows + orow) * D;
 #pragma unroll
     for (int e = 0; e < kPer; ++e) out[lane + 32 * e] = acc[e] * inv;
-    if (cp.lse != nullptr && lane == 0) cp.lse[(size_t)bh * cp.n + row] = mx + __logf(wsum);
+    if (cp.lse != nullptr && lane == 0) cp.lse[(size_t)bh * cp.n_rows + orow] = lse;
 }
 
 }  // namespace
@@ -833,7 +889,8 @@ static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int 
     const int smem = Cfg<D, BF16>::kSmemBytes;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, Cfg<D, BF16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.qg, tm.kg, tm.vg, tm.o, tm.po, p);
+    kern<<<grid, Cfg<D, BF16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kh, tm.vh, tm.qg, tm.kg, tm.vg, tm.o,
+                                                         tm.po, p);
     return cudaGetLastError();
 }
 
@@ -871,6 +928,14 @@ cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t s
         lca_combine_global_rows<128><<<grid, 128, 0, stream>>>(cp);
     else
         return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_halo_pack(const HaloPackParams& hp, cudaStream_t stream) {
+    const long long chunks = 4ll * hp.bh * hp.halo * (hp.d * 2 / 16);
+    if (chunks <= 0) return cudaSuccess;
+    const long long blocks = std::min<long long>((chunks + 255) / 256, 148ll * 16);
+    lca_pack_halo<<<(unsigned)blocks, 256, 0, stream>>>(hp);
     return cudaGetLastError();
 }
 

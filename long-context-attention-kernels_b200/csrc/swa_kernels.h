@@ -23,47 +23,84 @@ constexpr int kGatherChunk = 1024;    // global indices passed per gather launch
 
 struct TensorMaps {
     CUtensorMap q, k, v;     // inputs [bh][n][d] (bf16 / f16), box 64 x 128 rows, 128B swizzle
-    CUtensorMap qg, kg, vg;  // compact global rows [bh][gpad][d]
+    CUtensorMap kh, vh;      // sequence shards: K / V halo blocks (z = bh + b left, 2*bh + b right)
+    CUtensorMap qg, kg, vg;  // compact global rows [bh][G][d] (rows >= G read as zeros)
     CUtensorMap o;           // output [bh][n][d] fp32, box 32 x 128 rows, 128B swizzle
-    CUtensorMap po;          // global-row partial outputs [2*splits*bh][gpad][d] fp32
+    CUtensorMap po;          // global-row partial outputs [2*splits*bh][G][d] fp32
 };
 
+// Key and query indices below are absolute positions in the full sequence unless named
+// local.  Without sequence sharding q_off = 0, n = n_total and the K / V maps cover all
+// keys.  With it, the K / V maps cover the local shard [q_off, q_off + n) and the halo
+// maps the `halo` keys on either side; band key tiles are then aligned to the shard
+// start (lead is a multiple of 128 and n of the non-last shards too), so every key tile
+// lies in exactly one of left halo, shard or right halo.
 struct MainParams {
-    int n;            // sequence length
+    int n;            // local query rows (rows of Q, O and LSE)
+    int q_off;        // absolute index of local query row 0
+    int n_total;      // sequence length
+    int sharded;      // K / V maps cover the shard only; keys outside it come from the halo maps
+    int halo;         // rows per halo block
     int bh;           // batch * heads
-    int window;       // band radius, clamped to n
+    int window;       // band radius, clamped to n_total
+    int lead;         // band: pair tile 0 starts `lead` keys before the pair's first query
+    int key_lo, key_hi;  // band keys that exist in the maps: [key_lo, key_hi)
+    int gk_lo, gk_n;  // global-row units: keys [gk_lo, gk_lo + gk_n)
     int q_tiles;      // ceil(n / 128)
     int num_global;   // G: unique global tokens
     int g_tiles;      // ceil(G / 128)
-    int gpad;         // g_tiles * 128
     int n_splits;     // key splits per (bh, global tile)
     int split_tiles;  // key tiles per split
     int n_grow_units; // bh * g_tiles * n_splits global-row units (scheduled first)
     int n_band_units; // bh * q_pairs band units
     int q_pairs;      // ceil(q_tiles / 2): band units per (batch, head)
     float scale_log2; // scale * log2(e)
-    const int* gidx;  // [gpad] sorted global indices (padding = INT_MAX)
+    const int* gidx;  // [G] sorted absolute global indices
     float* lse;       // [bh][n] natural-log LSE, or nullptr
-    float* part_lse;  // [2 * n_splits][bh][gpad]
+    float* part_lse;  // [2 * n_splits][bh][G]
     int* err;         // device error word (first error wins)
     unsigned long long timeout_ns;  // per-wait budget
 };
 
+// Copies the global rows owned by this shard into the compact buffers; rows owned by
+// other shards are written as zeros (a sum over the shards then yields every row).
 struct GatherParams {
-    int n, gpad, num_global, bh;
+    int n, q_off;      // local rows of q / k / v and the absolute index of row 0
+    int num_global, bh;
     int first, count;  // compact rows [first, first + count) handled by this launch
     int* gidx_out;
     uint16_t *qg, *kg, *vg;
     int idx[kGatherChunk];
 };
 
+// Halo blocks sent to the neighbours: send[s][kv][b][r][:] = (kv ? v : k)[b][row][:] with
+// row = r (s = 0, towards the left neighbour) or n - halo + r (s = 1, towards the right).
+struct HaloPackParams {
+    int n, halo, bh, d;
+    const uint16_t* k;
+    const uint16_t* v;
+    uint16_t* send;
+};
+
+// Log-sum-exp merge of `n_parts` normalised partial results per (bh, global row).
+// Partial s of row (b, g): O at part_o + s * part_stride_o + (b * G + g) * d, LSE at
+// part_lse + s * part_stride_lse + b * G + g.  With split_tiles > 0 the partials are the
+// main kernel's (part 2s + x covers the x-parity key tiles of split s of `split_keys`
+// keys and exists only if that split has more than x tiles); with split_tiles == 0 all
+// are present.  The result goes to the rows gidx[g] - row_off of o / lse that fall in
+// [0, n_rows), or, when out_o is set, to out_o [bh][G][d] and out_lse [bh][G].
 struct CombineParams {
-    int n, bh, gpad, num_global, n_splits, split_tiles;
-    const int* gidx;
+    int bh, num_global, n_parts;
+    int split_tiles, split_keys;
+    size_t part_stride_o, part_stride_lse;
     const float* part_o;
     const float* part_lse;
+    const int* gidx;
     float* o;
     float* lse;
+    int n_rows, row_off;
+    float* out_o;
+    float* out_lse;
 };
 
 cudaError_t launch_main(int head_dim, bool bf16, const TensorMaps& tm, const MainParams& p, int grid,
@@ -71,6 +108,7 @@ cudaError_t launch_main(int head_dim, bool bf16, const TensorMaps& tm, const Mai
 cudaError_t launch_gather(int head_dim, const void* q, const void* k, const void* v, const GatherParams& gp,
                           int bh, cudaStream_t stream);
 cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t stream);
+cudaError_t launch_halo_pack(const HaloPackParams& hp, cudaStream_t stream);
 int main_smem_bytes(int head_dim, bool bf16);
 // Record `status` and a printf-style detail message as this thread's last C-ABI error
 // (what lca_last_error() returns); returns `status`.

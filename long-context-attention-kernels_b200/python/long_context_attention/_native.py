@@ -39,6 +39,25 @@ def native_error() -> int:
     return extension().device_error()
 
 
+class ShardDesc(ctypes.Structure):
+    """``lca_shard_desc`` of include/lca.h."""
+
+    _fields_ = [("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("seq_len", ctypes.c_int64),
+                ("head_dim", ctypes.c_int64), ("window_size", ctypes.c_int64), ("shard_offset", ctypes.c_int64),
+                ("shard_len", ctypes.c_int64), ("world_size", ctypes.c_int64), ("dtype", ctypes.c_int),
+                ("scale", ctypes.c_float)]
+
+
+class ShardLayout(ctypes.Structure):
+    """``lca_shard_layout`` of include/lca.h."""
+
+    _fields_ = [("total_bytes", ctypes.c_size_t), ("halo_rows", ctypes.c_int64),
+                ("globals_offset", ctypes.c_size_t), ("globals_bytes", ctypes.c_size_t),
+                ("halo_send_offset", ctypes.c_size_t), ("halo_recv_offset", ctypes.c_size_t),
+                ("halo_side_bytes", ctypes.c_size_t), ("rowpart_offset", ctypes.c_size_t),
+                ("rowpart_bytes", ctypes.c_size_t), ("rowpart_all_offset", ctypes.c_size_t)]
+
+
 class CABI:
     """ctypes binding of include/lca.h (the same stub a non-Python caller would write)."""
 
@@ -74,6 +93,15 @@ class CABI:
         lib.lca_swa_forward_noalloc.restype = ctypes.c_int
         lib.lca_swa_forward_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64,
                                                 ctypes.c_float, ctypes.POINTER(i64), i64, vp]
+        dp, lp = ctypes.POINTER(ShardDesc), ctypes.POINTER(ShardLayout)
+        lib.lca_swa_shard_layout.restype = ctypes.c_int
+        lib.lca_swa_shard_layout.argtypes = [dp, i64, lp]
+        lib.lca_swa_shard_prepare.restype = ctypes.c_int
+        lib.lca_swa_shard_prepare.argtypes = [dp, vp, vp, vp, ctypes.POINTER(i64), i64, vp, sz, vp]
+        lib.lca_swa_shard_forward.restype = ctypes.c_int
+        lib.lca_swa_shard_forward.argtypes = [dp, vp, vp, vp, vp, vp, ctypes.POINTER(i64), i64, vp, sz, vp]
+        lib.lca_swa_shard_finish.restype = ctypes.c_int
+        lib.lca_swa_shard_finish.argtypes = [dp, vp, vp, ctypes.POINTER(i64), i64, vp, sz, vp]
         lib.lca_set_timing_events.restype = ctypes.c_int
         lib.lca_set_timing_events.argtypes = [vp, vp]
         lib.lca_device_error.restype = ctypes.c_int
@@ -104,13 +132,37 @@ class CABI:
         return self.lib.lca_swa_forward(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim,
                                         window, ctypes.c_float(scale), arr, n, ws_ptr, ws_bytes, stream_ptr)
 
-
     def forward_noalloc(self, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim, window,
                         scale, tokens, stream_ptr) -> int:
         n = len(tokens)
         arr = (ctypes.c_int64 * max(n, 1))(*tokens)
         return self.lib.lca_swa_forward_noalloc(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len,
                                                 head_dim, window, ctypes.c_float(scale), arr, n, stream_ptr)
+
+    @staticmethod
+    def _tokens(tokens):
+        n = len(tokens)
+        return (ctypes.c_int64 * max(n, 1))(*tokens), n
+
+    def shard_layout(self, desc: ShardDesc, num_unique_global: int) -> tuple[int, ShardLayout]:
+        out = ShardLayout()
+        st = self.lib.lca_swa_shard_layout(ctypes.byref(desc), num_unique_global, ctypes.byref(out))
+        return st, out
+
+    def shard_prepare(self, desc: ShardDesc, q_ptr, k_ptr, v_ptr, tokens, ws_ptr, ws_bytes, stream_ptr) -> int:
+        arr, n = self._tokens(tokens)
+        return self.lib.lca_swa_shard_prepare(ctypes.byref(desc), q_ptr, k_ptr, v_ptr, arr, n, ws_ptr, ws_bytes,
+                                              stream_ptr)
+
+    def shard_forward(self, desc: ShardDesc, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, tokens, ws_ptr, ws_bytes,
+                      stream_ptr) -> int:
+        arr, n = self._tokens(tokens)
+        return self.lib.lca_swa_shard_forward(ctypes.byref(desc), q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, arr, n, ws_ptr,
+                                              ws_bytes, stream_ptr)
+
+    def shard_finish(self, desc: ShardDesc, o_ptr, lse_ptr, tokens, ws_ptr, ws_bytes, stream_ptr) -> int:
+        arr, n = self._tokens(tokens)
+        return self.lib.lca_swa_shard_finish(ctypes.byref(desc), o_ptr, lse_ptr, arr, n, ws_ptr, ws_bytes, stream_ptr)
 
 
 def cabi() -> CABI:

@@ -26,7 +26,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     c = _native.cabi()
-    assert c.lib.lca_abi_version() == 1
+    assert c.lib.lca_abi_version() == 2
     for code in range(7):
         assert c.lib.lca_status_string(code)
     assert c.lib.lca_status_string(99) == b"unknown status"
