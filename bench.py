@@ -47,6 +47,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=None,
                     help="override heads per GPU (smaller cases for profiling; not the headline config)")
+    ap.add_argument("--parallel", choices=["heads", "sequence"], default=None,
+                    help="multi-GPU split: independent head shards (default) or contiguous sequence shards "
+                         "(default for context_128k_d128)")
     return ap.parse_args(argv)
 
 
@@ -323,10 +326,146 @@ def run_ours(args):
     return 0
 
 
+def run_sequence(args):
+    """One sequence cut into contiguous shards, one per rank (strong scaling: the whole
+    job is fixed).  A step is the full sharded forward on every rank -- prepare, the
+    point-to-point exchange (global rows, halos), the shard kernels, the global-row
+    partial all-gather and the merge -- replayed from one CUDA graph per rank; the step
+    time is the max over ranks."""
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import datetime
+
+    import torch.distributed as dist
+
+    import long_context_attention as lca
+    from long_context_attention import _native
+    from long_context_attention.distributed import ShardedAttention, shard_bounds
+    from long_context_attention.workloads import useful_scores_shard
+
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    w = WORKLOADS[args.workload]
+    if args.heads is not None:
+        import dataclasses
+        w = dataclasses.replace(w, heads=args.heads)
+    g = w.global_tokens()
+    off, ln = shard_bounds(w.seq_len, world)[rank]
+    qf, kf, vf = w.inputs()
+    q, k, v = (t[:, :, off:off + ln].contiguous().to(dev) for t in (qf, kf, vf))
+    cpu_inputs = (qf, kf, vf) if (rank == 0 and world == 1) else None
+    del qf, kf, vf
+    cabi = _native.cabi()
+    plan = ShardedAttention(w.batch, w.heads, w.seq_len, w.head_dim, w.window, g, w.scale, w.torch_dtype, device=dev)
+    plan.capture(q, k, v, warmup=max(args.warmup, 3))
+    for _ in range(max(args.warmup, 3)):
+        plan.replay()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start.record()
+    for _ in range(args.steps):
+        plan.replay()
+    stop.record()
+    torch.cuda.synchronize()
+    clocks.stop()
+    ms = start.elapsed_time(stop) / args.steps
+
+    # main-kernel time from eager calls of the same plan (events recorded around the launch)
+    k_steps = min(args.steps, 20)
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(k_steps)]
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(k_steps)]
+    for e in ev_b + ev_a:  # torch's events count as recorded only after one record()
+        e.record()
+    for i in range(k_steps):
+        cabi.lib.lca_set_timing_events(ev_b[i].cuda_event, ev_a[i].cuda_event)
+        plan(q, k, v)
+    cabi.lib.lca_set_timing_events(None, None)
+    torch.cuda.synchronize()
+    main_ms = statistics.mean(ev_b[i].elapsed_time(ev_a[i]) for i in range(k_steps))
+    assert lca.device_error() == 0
+
+    # end to end: pinned H2D of this rank's shard into the plan's inputs, the graph, D2H
+    # of its rows
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty(plan.out.shape, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        q.copy_(qh, non_blocking=True)
+        k.copy_(kh, non_blocking=True)
+        v.copy_(vh, non_blocking=True)
+        oh.copy_(plan.replay(), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+
+    flops_rank = 4 * w.head_dim * w.batch * w.heads * useful_scores_shard(w.seq_len, w.window, g, off, ln)
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, main_ms, float(flops_rank)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, main_ms, flops_max = (float(x) for x in t.tolist())
+    else:
+        flops_max = flops_rank
+    tokens = w.tokens()
+    peak_tf, peak_gbs, peak_src = load_peaks()
+    achieved_tf = flops_max / (main_ms * 1e-3) / 1e12
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(w, *cpu_inputs, args.cpu_budget_s)
+        shard_io = w.io_bytes() / world
+        line = {
+            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+            "useful_tflops": w.useful_flops() / (ms * 1e-3) / 1e12,
+            "config": {"workload": w.name, "batch": w.batch, "heads": w.heads, "seq_len": w.seq_len,
+                       "head_dim": w.head_dim, "window": w.window, "num_global": len(g),
+                       "tokens_per_gpu_step": ln * w.batch * w.heads,
+                       "parallelism": f"sequence-sharded x{world}", "cuda_graph": True,
+                       "l2": "inputs larger than L2 (shard Q/K/V/O resident: %.0f MB)" % (shard_io / 1e6)},
+            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved_tf / peak_tf, "traffic": None, "kernel": "lca_swa_main",
+                         "kernel_ms": main_ms, "peak_source": peak_src,
+                         "note": "largest shard's useful FLOPs / max-over-ranks main-kernel time"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)) * world,
+                    "d2h_bytes_per_step": oh.numel() * 4 * world, "ms_per_step": e2e_ms},
+            # halo pack (2+ shards) and main; with global tokens also gather and two merges
+            "gpu_launches": args.steps * ((2 if world > 1 else 1) + (3 if g else 0)),
+            "clocks": clocks.report(),
+        }
+        print(json.dumps(line), flush=True)
+    plan.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    parallel = args.parallel or ("sequence" if args.workload == "context_128k_d128" else "heads")
+    if parallel == "sequence":
+        return run_sequence(args)
     return run_ours(args)
 
 

@@ -127,12 +127,15 @@ LCA_API int lca_swa_forward_noalloc(const void* q, const void* k, const void* v,
  * caller performs with its own collectives library (NCCL):
  *
  *   1. lca_swa_shard_prepare   -- on every rank
- *   2. exchange A (sum all-reduce): the `globals` region of every rank's workspace,
- *      elementwise in the input dtype (each rank contributes the global rows it owns and
- *      zeros elsewhere)
- *      exchange B (point-to-point): send side 0 of `halo_send` to rank r-1 and side 1 to
- *      rank r+1; receive from rank r-1 into side 0 of `halo_recv` and from rank r+1 into
- *      side 1 (ranks without that neighbour skip the transfer)
+ *   2. exchange A+B (point-to-point, one group):
+ *      A: the global rows.  The `globals` region holds one globals_row_bytes row per
+ *         unique global token, in sorted token order; the rows of the tokens inside
+ *         rank r's shard form one contiguous run, which rank r has filled.  Rank r sends
+ *         its run to every other rank, and receives every other rank's run into the same
+ *         offsets of its own region (ranks whose shard holds no global token send nothing).
+ *      B: the halos.  Send side 0 of `halo_send` to rank r-1 and side 1 to rank r+1;
+ *         receive from rank r-1 into side 0 of `halo_recv` and from rank r+1 into side 1
+ *         (ranks without that neighbour skip the transfer)
  *   3. lca_swa_shard_forward   -- on every rank
  *   4. exchange C (all-gather): every rank's `rowpart` region into `rowpart_all`, rank
  *      order, rowpart_bytes per rank
@@ -158,8 +161,9 @@ typedef struct lca_shard_desc {
 typedef struct lca_shard_layout {
     size_t total_bytes;        /* workspace size */
     int64_t halo_rows;         /* K / V rows per halo side (0: no halo exchange) */
-    size_t globals_offset;     /* exchange A region */
+    size_t globals_offset;     /* exchange A region: [G][3 (q, k, v)][batch*heads][head_dim], input dtype */
     size_t globals_bytes;
+    size_t globals_row_bytes;  /* one global row of that region */
     size_t halo_send_offset;   /* [2 sides][2 (k, v)][batch*heads][halo_rows][head_dim], input dtype */
     size_t halo_recv_offset;   /* same layout */
     size_t halo_side_bytes;    /* bytes of one side of halo_send / halo_recv */

@@ -206,7 +206,7 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct Layout {
     int g_tiles = 0, key_tiles = 0, n_splits = 0, split_tiles = 0;
-    size_t gbytes = 0;  // one compact [bh][G][d] buffer
+    size_t grow_bytes = 0;  // one compact global row: [3][bh][d]
     size_t off_gidx = 0, off_globals = 0, off_po = 0, off_plse = 0;
     size_t off_send = 0, off_recv = 0, halo_block = 0;  // halo_block: one side, [2][bh][halo][d]
     size_t off_rowpart = 0, rowpart_bytes = 0, off_rowpart_all = 0;
@@ -235,9 +235,9 @@ Layout make_layout(const Problem& P) {
         const int64_t parts = 2 * (int64_t)L.n_splits;
         L.off_gidx = off;
         off = align_up(off + sizeof(int) * G, kAlign);
-        L.gbytes = (size_t)bh * G * d * 2;
-        L.off_globals = off;  // q, k, v compact rows back to back
-        off = align_up(off + 3 * L.gbytes, kAlign);
+        L.grow_bytes = (size_t)3 * bh * d * 2;
+        L.off_globals = off;  // compact rows [G][3 (q, k, v)][bh][d]
+        off = align_up(off + (size_t)G * L.grow_bytes, kAlign);
         L.off_po = off;
         off = align_up(off + (size_t)parts * bh * G * d * 4, kAlign);
         L.off_plse = off;
@@ -270,6 +270,24 @@ int encode_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* bas
     cuuint64_t dims[3] = {d, rows, planes};
     cuuint64_t strides[2] = {d * (uint64_t)esize, d * rows * (uint64_t)esize};
     cuuint32_t box[3] = {box_x, (cuuint32_t)lca::kTileRows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
+    return LCA_OK;
+}
+
+// Compact global rows [G][3][bh][d] (16-bit): dims {d, bh, G} with the row stride of a
+// whole compact row, box 64 columns x 1 head x 128 rows (lands in shared memory exactly
+// like a 64 x 128 box of a [bh][n][d] tensor).
+int encode_compact(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d, uint64_t bh, uint64_t G,
+                   const char* name) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (enc == nullptr) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+    cuuint64_t dims[3] = {d, bh, G};
+    cuuint64_t strides[2] = {d * 2, 3 * bh * d * 2};
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)lca::kTileRows};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -325,9 +343,7 @@ int enqueue_gather(const Problem& P, const Layout& L, const void* q, const void*
         gp.first = first;
         gp.count = std::min<int>(lca::kGatherChunk, (int)P.G - first);
         gp.gidx_out = reinterpret_cast<int*>(ws + L.off_gidx);
-        gp.qg = reinterpret_cast<uint16_t*>(qg);
-        gp.kg = reinterpret_cast<uint16_t*>(qg + L.gbytes);
-        gp.vg = reinterpret_cast<uint16_t*>(qg + 2 * L.gbytes);
+        gp.compact = reinterpret_cast<uint16_t*>(qg);
         for (int i = 0; i < gp.count; ++i) gp.idx[i] = P.gl[(size_t)first + i];
         cudaError_t e = lca::launch_gather((int)P.d, q, k, v, gp, (int)P.bh, stream);
         if (e != cudaSuccess) return fail_cuda(e, "gather launch");
@@ -400,9 +416,10 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
         p.part_lse = reinterpret_cast<float*>(ws + L.off_plse);
         uint8_t* qg = ws + L.off_globals;
         const uint64_t G = (uint64_t)P.G;
-        if ((st = encode_3d(&tm.qg, tdt, 2, qg, d, G, bh, 64, "q_global")) != LCA_OK) return st;
-        if ((st = encode_3d(&tm.kg, tdt, 2, qg + L.gbytes, d, G, bh, 64, "k_global")) != LCA_OK) return st;
-        if ((st = encode_3d(&tm.vg, tdt, 2, qg + 2 * L.gbytes, d, G, bh, 64, "v_global")) != LCA_OK) return st;
+        const size_t plane = (size_t)bh * d * 2;  // one of q / k / v within a compact row
+        if ((st = encode_compact(&tm.qg, tdt, qg, d, bh, G, "q_global")) != LCA_OK) return st;
+        if ((st = encode_compact(&tm.kg, tdt, qg + plane, d, bh, G, "k_global")) != LCA_OK) return st;
+        if ((st = encode_compact(&tm.vg, tdt, qg + 2 * plane, d, bh, G, "v_global")) != LCA_OK) return st;
         if ((st = encode_3d(&tm.po, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.off_po, d, G,
                             (uint64_t)2 * L.n_splits * bh, 32, "partial_out")) != LCA_OK)
             return st;
@@ -565,7 +582,8 @@ int lca_swa_shard_layout(const lca_shard_desc* desc, int64_t num_unique_global, 
     out->total_bytes = L.total;
     out->halo_rows = P.halo();
     out->globals_offset = L.off_globals;
-    out->globals_bytes = 3 * L.gbytes;
+    out->globals_bytes = (size_t)P.G * L.grow_bytes;
+    out->globals_row_bytes = L.grow_bytes;
     out->halo_send_offset = L.off_send;
     out->halo_recv_offset = L.off_recv;
     out->halo_side_bytes = L.halo_block;

@@ -5,9 +5,9 @@
 // i is a global token.  Output is fp32 softmax(scale * Q K^T restricted to that mask) V.
 //
 // Three launches per forward:
-//   1. lca_gather_globals : copies the G global rows of Q, K, V into compact [bh][G][d]
-//                           buffers (TMA reads rows >= G as zeros) and writes the sorted
-//                           index list.
+//   1. lca_gather_globals : copies the G global rows of Q, K, V into one compact
+//                           [G][3][bh][d] buffer (TMA reads rows >= G as zeros) and
+//                           writes the sorted index list.
 //   2. lca_swa_main       : persistent, one CTA per SM, looping over work units:
 //        band unit      : two adjacent 128-row query tiles A, B of one (batch, head).
 //                         Key tiles: the band [q0 - w, q0 + 255 + w] in 128-key tiles
@@ -295,6 +295,9 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     const Unit un = decode_unit(p, u);
                     const CUtensorMap* mq = un.grow ? &tm_qg : &tm_q;
                     for (int x = 0; x < 2 && ok; ++x) {
+                        // the compact global rows are [G][3][bh][d]: their maps index (col, bh, row)
+                        const int qy = un.grow ? un.bh : (x ? un.qrow[1] : un.qrow[0]);
+                        const int qz = un.grow ? un.qrow[x] : un.bh;
                         if (qn > 0 && !ptx::mbar_wait(&ctl->q_empty[x], (qn - 1) & 1, abort_flag, p.err,
                                                       LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
                             ok = false;
@@ -304,7 +307,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
 #pragma unroll
                         for (int pn = 0; pn < C::kPanels; ++pn)
                             ptx::tma_load_3d(sQ + x * C::kTileBytes + pn * kPanelBytes, mq, &ctl->q_full[x],
-                                             pn * 64, x ? un.qrow[1] : un.qrow[0], un.bh);
+                                             pn * 64, qy, qz);
                     }
                     if (!ok) break;
                     ++qn;
@@ -320,7 +323,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                             }
                             const CUtensorMap* m = t.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
                             int y = t.row0, z = un.bh;
-                            if (!t.global_key && p.sharded) {
+                            if (t.global_key) {
+                                y = un.bh;
+                                z = t.row0;
+                            } else if (p.sharded) {
                                 // the tile lies wholly in the left halo, the shard or the right halo
                                 if (y < p.q_off) {
                                     m = kv ? &tm_vh : &tm_kh;
@@ -777,18 +783,16 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
     const int g = gp.first + row;  // compact row index
     const int src_abs = gp.idx[row];
     const int src_row = src_abs - gp.q_off;
-    const bool owned = src_row >= 0 && src_row < gp.n;
     if (bh == 0 && lane == 0) gp.gidx_out[g] = src_abs;
-    const size_t src_off = ((size_t)bh * gp.n + (owned ? src_row : 0)) * D;
-    const size_t dst_off = ((size_t)bh * gp.num_global + g) * D;
+    if (src_row < 0 || src_row >= gp.n) return;  // owned by another shard
+    const size_t src_off = ((size_t)bh * gp.n + src_row) * D;
     for (int c = lane; c < 3 * kChunks; c += 32) {
         const int which = c / kChunks;
         const int cc = c % kChunks;
         const uint16_t* src = which == 0 ? q : (which == 1 ? k : v);
-        uint16_t* dst = which == 0 ? gp.qg : (which == 1 ? gp.kg : gp.vg);
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (owned) val = *reinterpret_cast<const uint4*>(src + src_off + cc * 8);
-        *reinterpret_cast<uint4*>(dst + dst_off + cc * 8) = val;
+        const size_t dst_off = (((size_t)g * 3 + which) * gp.bh + bh) * D;
+        *reinterpret_cast<uint4*>(gp.compact + dst_off + cc * 8) =
+            *reinterpret_cast<const uint4*>(src + src_off + cc * 8);
     }
 }
 

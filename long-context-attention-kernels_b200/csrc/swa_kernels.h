@@ -24,7 +24,8 @@ constexpr int kGatherChunk = 1024;    // global indices passed per gather launch
 struct TensorMaps {
     CUtensorMap q, k, v;     // inputs [bh][n][d] (bf16 / f16), box 64 x 128 rows, 128B swizzle
     CUtensorMap kh, vh;      // sequence shards: K / V halo blocks (z = bh + b left, 2*bh + b right)
-    CUtensorMap qg, kg, vg;  // compact global rows [bh][G][d] (rows >= G read as zeros)
+    CUtensorMap qg, kg, vg;  // compact global rows [G][3 (q, k, v)][bh][d]; maps {d, bh, G}, box 64 x 1 x 128
+                             // (rows >= G read as zeros)
     CUtensorMap o;           // output [bh][n][d] fp32, box 32 x 128 rows, 128B swizzle
     CUtensorMap po;          // global-row partial outputs [2*splits*bh][G][d] fp32
 };
@@ -62,14 +63,15 @@ struct MainParams {
     unsigned long long timeout_ns;  // per-wait budget
 };
 
-// Copies the global rows owned by this shard into the compact buffers; rows owned by
-// other shards are written as zeros (a sum over the shards then yields every row).
+// Copies the global rows owned by this shard into the compact buffer [G][3][bh][d] and
+// writes the sorted index list; rows owned by other shards are left untouched (their
+// owners send them).
 struct GatherParams {
     int n, q_off;      // local rows of q / k / v and the absolute index of row 0
     int num_global, bh;
     int first, count;  // compact rows [first, first + count) handled by this launch
     int* gidx_out;
-    uint16_t *qg, *kg, *vg;
+    uint16_t* compact;
     int idx[kGatherChunk];
 };
 

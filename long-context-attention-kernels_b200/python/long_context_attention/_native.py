@@ -53,6 +53,7 @@ class ShardLayout(ctypes.Structure):
 
     _fields_ = [("total_bytes", ctypes.c_size_t), ("halo_rows", ctypes.c_int64),
                 ("globals_offset", ctypes.c_size_t), ("globals_bytes", ctypes.c_size_t),
+                ("globals_row_bytes", ctypes.c_size_t),
                 ("halo_send_offset", ctypes.c_size_t), ("halo_recv_offset", ctypes.c_size_t),
                 ("halo_side_bytes", ctypes.c_size_t), ("rowpart_offset", ctypes.c_size_t),
                 ("rowpart_bytes", ctypes.c_size_t), ("rowpart_all_offset", ctypes.c_size_t)]

@@ -10,10 +10,10 @@ Two ways to spread one forward over several GPUs, one process per GPU:
   `window` keys from each neighbouring shard (the halo) and the global tokens' K / V
   rows, and a global row needs every shard's keys.  The forward runs as
 
-    1. ``lca_swa_shard_prepare``: compact global rows this shard owns (zeros for the
-       others) and the halo blocks for the neighbours;
-    2. exchange: sum all-reduce of the compact global rows (every rank then holds all
-       of them) and point-to-point send / receive of the halos with ranks r-1 and r+1;
+    1. ``lca_swa_shard_prepare``: compact copies of the global rows this shard holds and
+       the halo blocks for the neighbours;
+    2. exchange, one point-to-point group: each rank sends its global rows to all others
+       (every rank then holds all of them) and its halo blocks to ranks r-1 and r+1;
     3. ``lca_swa_shard_forward``: every local row, plus this shard's partial result
        (normalised O and log-sum-exp) for each global row over its own keys;
     4. exchange: all-gather of the per-shard global-row partials;
@@ -26,7 +26,8 @@ Two ways to spread one forward over several GPUs, one process per GPU:
 
 The compute steps come from the native library; the ``steps`` argument exists so that
 the exchange logic can be driven by another implementation of the same three steps
-(the CPU tests run it on ``gloo`` ranks that way).
+(the CPU tests run it on ``gloo`` ranks that way).  :class:`ShardedAttention` sets a
+problem up once and can capture the whole step, exchanges included, in a CUDA graph.
 """
 from __future__ import annotations
 
@@ -39,7 +40,8 @@ import torch.distributed as dist
 
 from ._native import CABI, ShardDesc, ShardLayout, cabi
 
-__all__ = ["shard_bounds", "head_shard", "ShardSpec", "NativeShardSteps", "sliding_window_attention_sharded"]
+__all__ = ["shard_bounds", "head_shard", "global_row_runs", "ShardSpec", "NativeShardSteps", "ShardedAttention",
+           "sliding_window_attention_sharded"]
 
 _TILE = 128
 
@@ -155,34 +157,49 @@ def _normalize(tokens: Sequence[int], seq_len: int) -> list[int]:
     return sorted(out)
 
 
-def exchange_globals(ws: torch.Tensor, lay: ShardLayout, dtype: torch.dtype, group=None) -> None:
-    """Sum all-reduce of the compact global rows (each rank holds its own, zeros elsewhere)."""
-    if lay.globals_bytes == 0:
-        return
-    buf = ws[lay.globals_offset:lay.globals_offset + lay.globals_bytes].view(dtype)
-    dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+def global_row_runs(tokens: Sequence[int], bounds: Sequence[tuple[int, int]]) -> list[tuple[int, int]]:
+    """Per rank, the run [lo, hi) of compact global rows (sorted unique tokens) that fall
+    in its shard."""
+    import bisect
+
+    return [(bisect.bisect_left(tokens, off), bisect.bisect_left(tokens, off + ln)) for off, ln in bounds]
 
 
-def exchange_halos(ws: torch.Tensor, lay: ShardLayout, rank: int, world_size: int, group=None) -> None:
-    """Halo blocks: side 0 of the send region goes to rank - 1 and side 1 to rank + 1; side
-    0 of the receive region comes from rank - 1 and side 1 from rank + 1."""
-    side = lay.halo_side_bytes
-    if lay.halo_rows == 0 or side == 0 or world_size == 1:
+def exchange_p2p(ws: torch.Tensor, lay: ShardLayout, runs, rank: int, world_size: int, group=None) -> None:
+    """One point-to-point group: every rank sends the global rows its shard holds to all
+    other ranks (into the same offsets of their compact region), and the halo blocks go
+    to the neighbours (side 0 of the send region to rank - 1, side 1 to rank + 1; side 0
+    of the receive region comes from rank - 1, side 1 from rank + 1)."""
+    if world_size == 1:
         return
-    send, recv = lay.halo_send_offset, lay.halo_recv_offset
     ops = []
 
     def peer(r):
         return r if group is None else dist.get_global_rank(group, r)
 
-    if rank > 0:
-        ops.append(dist.P2POp(dist.isend, ws[send:send + side], peer(rank - 1), group))
-        ops.append(dist.P2POp(dist.irecv, ws[recv:recv + side], peer(rank - 1), group))
-    if rank < world_size - 1:
-        ops.append(dist.P2POp(dist.isend, ws[send + side:send + 2 * side], peer(rank + 1), group))
-        ops.append(dist.P2POp(dist.irecv, ws[recv + side:recv + 2 * side], peer(rank + 1), group))
-    for req in dist.batch_isend_irecv(ops):
-        req.wait()
+    rb, g0 = lay.globals_row_bytes, lay.globals_offset
+    if lay.globals_bytes:
+        lo, hi = runs[rank]
+        for r in range(world_size):
+            if r == rank:
+                continue
+            if hi > lo:
+                ops.append(dist.P2POp(dist.isend, ws[g0 + lo * rb:g0 + hi * rb], peer(r), group))
+            rlo, rhi = runs[r]
+            if rhi > rlo:
+                ops.append(dist.P2POp(dist.irecv, ws[g0 + rlo * rb:g0 + rhi * rb], peer(r), group))
+    side = lay.halo_side_bytes
+    if lay.halo_rows and side:
+        send, recv = lay.halo_send_offset, lay.halo_recv_offset
+        if rank > 0:
+            ops.append(dist.P2POp(dist.isend, ws[send:send + side], peer(rank - 1), group))
+            ops.append(dist.P2POp(dist.irecv, ws[recv:recv + side], peer(rank - 1), group))
+        if rank < world_size - 1:
+            ops.append(dist.P2POp(dist.isend, ws[send + side:send + 2 * side], peer(rank + 1), group))
+            ops.append(dist.P2POp(dist.irecv, ws[recv + side:recv + 2 * side], peer(rank + 1), group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
 
 
 def exchange_rowparts(ws: torch.Tensor, lay: ShardLayout, world_size: int, group=None) -> None:
@@ -191,7 +208,121 @@ def exchange_rowparts(ws: torch.Tensor, lay: ShardLayout, world_size: int, group
         return
     src = ws[lay.rowpart_offset:lay.rowpart_offset + lay.rowpart_bytes]
     dst = ws[lay.rowpart_all_offset:lay.rowpart_all_offset + world_size * lay.rowpart_bytes]
-    dist.all_gather_into_tensor(dst, src, group=group)
+    if world_size == 1:
+        dst.copy_(src)
+    else:
+        dist.all_gather_into_tensor(dst, src, group=group)
+
+
+class ShardedAttention:
+    """A sequence-sharded forward of one problem shape on this rank, set up once.
+
+    Holds the shard geometry, the workspace and the output buffers, so a call does only
+    the compute steps and the exchanges.  :meth:`capture` records one whole forward
+    (kernels and NCCL exchanges) into a CUDA graph over fixed input tensors, and
+    :meth:`replay` re-runs it with a single launch: the way to run a shard whose step is
+    short enough for host-side launch work to matter.  Outputs live in :attr:`out` (and
+    :attr:`lse`) and are overwritten by every call.  All ranks of `group` must build the
+    same plan and call it in the same order.
+    """
+
+    def __init__(self, batch: int, heads: int, seq_len: int, head_dim: int, window_size: int,
+                 global_tokens: Sequence[int] = (), scale: float | None = None, dtype=torch.bfloat16, *,
+                 group=None, device=None, return_lse: bool = False, steps=None):
+        if dist.is_available() and dist.is_initialized():
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        else:
+            if group is not None:
+                raise RuntimeError("long_context_attention: a process group was given but torch.distributed "
+                                   "is not initialised")
+            self.rank, self.world = 0, 1
+        if window_size < 0:
+            raise RuntimeError("long_context_attention: window_size must be >= 0")
+        self.group = group
+        self.bounds = shard_bounds(seq_len, self.world)
+        off, ln = self.bounds[self.rank]
+        w = min(window_size, seq_len)
+        if self.world > 1 and w > min(b for _, b in self.bounds):
+            raise RuntimeError(f"long_context_attention: window {w} exceeds the shortest shard "
+                               f"({min(b for _, b in self.bounds)} tokens); halos come from adjacent shards only")
+        if scale is None:
+            scale = 1.0 / math.sqrt(head_dim)
+        self.tokens = _normalize(global_tokens, seq_len)
+        self.runs = global_row_runs(self.tokens, self.bounds)
+        self.dtype = dtype
+        self.spec = ShardSpec(batch, heads, seq_len, head_dim, int(window_size), self.rank, self.world, off, ln,
+                              _dtype_code(dtype), float(scale))
+        self.steps = steps if steps is not None else NativeShardSteps()
+        self.layout = self.steps.layout(self.spec, len(self.tokens))
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device)
+        self.ws = self.steps.workspace(self.layout.total_bytes, self.device)
+        self.out = torch.empty(batch, heads, ln, head_dim, dtype=torch.float32, device=self.device)
+        self.lse = torch.empty(batch, heads, ln, dtype=torch.float32, device=self.device) if return_lse else None
+        self.graph = None
+        self._graph_inputs = None
+
+    @property
+    def shard(self) -> tuple[int, int]:
+        """(offset, length) of this rank's tokens."""
+        return self.spec.offset, self.spec.length
+
+    def _check(self, Q, K, V):
+        shape = (self.spec.batch, self.spec.heads, self.spec.length, self.spec.head_dim)
+        for name, t in (("Q", Q), ("K", K), ("V", V)):
+            if tuple(t.shape) != shape:
+                raise RuntimeError(f"long_context_attention: {name} has shape {tuple(t.shape)}; this rank's shard "
+                                   f"is {shape}")
+            if t.dtype != self.dtype or not t.is_contiguous():
+                raise RuntimeError(f"long_context_attention: {name} must be a contiguous {self.dtype} tensor")
+
+    def _run(self, Q, K, V):
+        spec, lay, ws = self.spec, self.layout, self.ws
+        self.steps.prepare(spec, Q, K, V, self.tokens, ws)
+        exchange_p2p(ws, lay, self.runs, self.rank, self.world, self.group)
+        self.steps.forward(spec, Q, K, V, self.out, self.lse, self.tokens, ws)
+        exchange_rowparts(ws, lay, self.world, self.group)
+        self.steps.finish(spec, self.out, self.lse, self.tokens, ws)
+
+    def __call__(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor):
+        """One forward on the current stream; returns :attr:`out` (and :attr:`lse`)."""
+        self._check(Q, K, V)
+        self._run(Q, K, V)
+        return (self.out, self.lse) if self.lse is not None else self.out
+
+    def capture(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, warmup: int = 2) -> None:
+        """Record one forward over these input tensors into a CUDA graph (after `warmup`
+        eager runs on the capture stream, which also set up the NCCL communicators).
+        Later :meth:`replay` calls read whatever Q, K, V then hold."""
+        self._check(Q, K, V)
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._run(Q, K, V)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._run(Q, K, V)
+        self.graph = g
+        self._graph_inputs = (Q, K, V)
+
+    def replay(self):
+        """Run the captured forward; returns :attr:`out` (and :attr:`lse`)."""
+        if self.graph is None:
+            raise RuntimeError("long_context_attention: capture() has not been called")
+        self.graph.replay()
+        return (self.out, self.lse) if self.lse is not None else self.out
+
+    def release(self) -> None:
+        """Drop the captured graph (it holds NCCL work: release it before destroying the
+        process group)."""
+        self.graph = None
+        self._graph_inputs = None
 
 
 def sliding_window_attention_sharded(
@@ -215,45 +346,16 @@ def sliding_window_attention_sharded(
     `global_tokens` (indices into the whole sequence) and `scale` mean what they mean for
     :func:`long_context_attention.sliding_window_attention`, and are the same on every
     rank.  Returns this shard's fp32 output rows (and their log-sum-exp with
-    ``return_lse``).  Limit: ``min(window_size, seq_len)`` must not exceed a shard.
+    ``return_lse``) in new tensors.  Limit: ``min(window_size, seq_len)`` must not exceed
+    a shard.  For repeated calls of one shape, :class:`ShardedAttention` avoids the setup.
     """
-    rank = dist.get_rank(group)
-    world = dist.get_world_size(group)
     B, H, n_loc, d = Q.shape
-    if K.shape != Q.shape or V.shape != Q.shape:
-        raise RuntimeError("long_context_attention: Q, K and V must have the same shape")
-    if not (Q.is_contiguous() and K.is_contiguous() and V.is_contiguous()):
-        raise RuntimeError("long_context_attention: Q, K and V must be contiguous")
-    if Q.dtype != K.dtype or Q.dtype != V.dtype:
-        raise RuntimeError("long_context_attention: Q, K and V must share one dtype")
-    if window_size < 0:
-        raise RuntimeError("long_context_attention: window_size must be >= 0")
+    world = dist.get_world_size(group)
     if seq_len is None:
         seq_len = n_loc * world
-    bounds = shard_bounds(seq_len, world)
-    offset, length = bounds[rank]
-    if length != n_loc:
-        raise RuntimeError(f"long_context_attention: rank {rank} holds {n_loc} tokens; shard_bounds({seq_len}, {world}) "
-                           f"gives it {length}")
-    w = min(window_size, seq_len)
-    if world > 1 and w > min(ln for _, ln in bounds):
-        raise RuntimeError(f"long_context_attention: window {w} exceeds the shortest shard "
-                           f"({min(ln for _, ln in bounds)} tokens); halos come from adjacent shards only")
-    if scale is None:
-        scale = 1.0 / math.sqrt(d)
-    tokens = _normalize(global_tokens, seq_len)
-    spec = ShardSpec(B, H, seq_len, d, int(window_size), rank, world, offset, length, _dtype_code(Q.dtype),
-                     float(scale))
-    steps = steps if steps is not None else NativeShardSteps()
-    lay = steps.layout(spec, len(tokens))
-    ws = steps.workspace(lay.total_bytes, Q.device)
-    out = torch.empty(B, H, n_loc, d, dtype=torch.float32, device=Q.device)
-    lse = torch.empty(B, H, n_loc, dtype=torch.float32, device=Q.device) if return_lse else None
-
-    steps.prepare(spec, Q, K, V, tokens, ws)
-    exchange_globals(ws, lay, Q.dtype, group)
-    exchange_halos(ws, lay, rank, world, group)
-    steps.forward(spec, Q, K, V, out, lse, tokens, ws)
-    exchange_rowparts(ws, lay, world, group)
-    steps.finish(spec, out, lse, tokens, ws)
-    return (out, lse) if return_lse else out
+    plan = ShardedAttention(B, H, seq_len, d, window_size, global_tokens, scale, Q.dtype, group=group,
+                            device=Q.device, return_lse=return_lse, steps=steps)
+    if plan.spec.length != n_loc:
+        raise RuntimeError(f"long_context_attention: rank {plan.rank} holds {n_loc} tokens; "
+                           f"shard_bounds({seq_len}, {world}) gives it {plan.spec.length}")
+    return plan(Q, K, V)

@@ -136,3 +136,21 @@ def useful_scores(seq_len: int, window: int, global_tokens: Sequence[int]) -> in
     is_g[g] = True
     per_row = np.where(is_g, n, per_row)
     return int(per_row.sum())
+
+
+def useful_scores_shard(seq_len: int, window: int, global_tokens: Sequence[int], offset: int, length: int) -> int:
+    """True mask entries one sequence shard computes: its non-global rows' entries, plus
+    the global rows' entries against its own keys (G * length).  Summed over all shards
+    this is :func:`useful_scores`."""
+    n, w = seq_len, window
+    g = np.asarray(normalize_global_tokens(global_tokens, n), dtype=np.int64)
+    i = np.arange(offset, offset + length, dtype=np.int64)
+    lo = np.maximum(0, i - w)
+    hi = np.minimum(n - 1, i + w)
+    per_row = hi - lo + 1
+    if g.size:
+        inside = np.searchsorted(g, hi, side="right") - np.searchsorted(g, lo, side="left")
+        per_row = per_row + (g.size - inside)
+        is_g = np.isin(i, g)
+        per_row = np.where(is_g, 0, per_row)
+    return int(per_row.sum()) + int(g.size) * length

@@ -6,7 +6,7 @@ It reads and writes the same workspace regions as the native steps
 library's own layout function returns, so that the exchange logic of
 ``long_context_attention.distributed`` can be run on ``gloo`` ranks without a GPU.  The
 arithmetic is float64 numpy over the dense Longformer mask restricted to what a shard
-holds: its own rows, the received halos and the all-reduced compact global rows.
+holds: its own rows, the received halos and the exchanged compact global rows.
 """
 from __future__ import annotations
 
@@ -36,7 +36,7 @@ class CpuShardSteps:
 
     def _globals(self, spec, lay, ws, dtype, G):
         bh, d = self._dims(spec)
-        return _region(ws, lay.globals_offset, lay.globals_bytes, dtype).view(3, bh, G, d)
+        return _region(ws, lay.globals_offset, lay.globals_bytes, dtype).view(G, 3, bh, d)
 
     def _halo(self, spec, lay, ws, off, dtype):
         bh, d = self._dims(spec)
@@ -51,12 +51,11 @@ class CpuShardSteps:
         n = spec.length
         if G:
             g = self._globals(spec, lay, ws, q.dtype, G)
-            g.zero_()
             for j, t in enumerate(tokens):
                 if spec.offset <= t < spec.offset + n:
                     r = t - spec.offset
                     for which, src in enumerate((q, k, v)):
-                        g[which, :, j] = src.reshape(bh, n, d)[:, r]
+                        g[j, which] = src.reshape(bh, n, d)[:, r]
         if lay.halo_rows:
             h = lay.halo_rows
             send = self._halo(spec, lay, ws, lay.halo_send_offset, q.dtype)
@@ -91,8 +90,8 @@ class CpuShardSteps:
                 vv[:, off + n - lo_abs:] = recv[1, 1][:, :m]
         gset = np.asarray(tokens, dtype=np.int64)
         if G:
-            g = self._globals(spec, lay, ws, q.dtype, G).double().numpy()
-            qg, kg, vg = g[0], g[1], g[2]
+            g = self._globals(spec, lay, ws, q.dtype, G).double().numpy()  # [G][3][bh][d]
+            qg, kg, vg = (g[:, i].transpose(1, 0, 2) for i in range(3))
         o = np.zeros((bh, n, d))
         ls = np.zeros((bh, n))
         for i in range(n):

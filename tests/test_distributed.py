@@ -52,7 +52,7 @@ def test_shard_layout_sizes():
     assert st == c.OK, c.last_error()
     bh, d, G, w = 8, 128, 16, 512
     assert lay.halo_rows == w
-    assert lay.globals_bytes == 3 * bh * G * d * 2
+    assert lay.globals_bytes == 3 * bh * G * d * 2 and lay.globals_row_bytes == 3 * bh * d * 2
     assert lay.halo_side_bytes == 2 * bh * w * d * 2
     assert lay.rowpart_bytes == bh * G * (d + 1) * 4
     regions = sorted([(lay.globals_offset, lay.globals_bytes), (lay.halo_send_offset, 2 * lay.halo_side_bytes),

@@ -1,7 +1,7 @@
 """Sequence shards on the GPU.
 
 * Emulated ranks on one GPU: every shard's native steps run on cuda:0 and the test
-  performs the three exchanges itself (sum of the compact global rows, halo copies,
+  performs the exchanges itself (each shard's global rows to all others, halo copies,
   gather of the per-shard partials) between the shards' workspaces.  This checks the
   shard kernels (halo tensor maps, shard offsets, per-shard global-row partials and
   their merge) against the oracle and against the unsharded forward.
@@ -17,7 +17,8 @@ import pytest
 import torch
 
 import long_context_attention as lca
-from long_context_attention.distributed import NativeShardSteps, ShardSpec, shard_bounds, _dtype_code, _normalize
+from long_context_attention.distributed import (NativeShardSteps, ShardSpec, _dtype_code, _normalize,
+                                                global_row_runs, shard_bounds)
 from long_context_attention.workloads import WORKLOADS, make_inputs
 from lca_testutil import LSE_ABS_TOL, MAX_ABS_TOL, REL_L2_TOL, max_abs, rel_l2
 from oracle import swa_oracle
@@ -49,10 +50,13 @@ def run_emulated(q, k, v, window, tokens, scale, world, with_lse=True):
         steps.prepare(specs[r], *parts[r], toks, wss[r])
     lay0 = lays[0]
     if lay0.globals_bytes:
-        total = sum(w[l.globals_offset:l.globals_offset + l.globals_bytes].view(q.dtype).float()
-                    for w, l in zip(wss, lays))
-        for w, l in zip(wss, lays):
-            w[l.globals_offset:l.globals_offset + l.globals_bytes].view(q.dtype).copy_(total.to(q.dtype))
+        # each shard's run of global rows goes to every other shard, same offsets
+        rb = lay0.globals_row_bytes
+        for r, (lo, hi) in enumerate(global_row_runs(toks, bounds)):
+            for t in range(world):
+                if t != r and hi > lo:
+                    a, b = lays[r].globals_offset, lays[t].globals_offset
+                    wss[t][b + lo * rb:b + hi * rb].copy_(wss[r][a + lo * rb:a + hi * rb])
     for r in range(world):
         lay, side = lays[r], lays[r].halo_side_bytes
         if lay.halo_rows == 0:
