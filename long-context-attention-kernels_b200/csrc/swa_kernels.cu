@@ -575,9 +575,17 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     const bool any_mask = __any_sync(0xffffffffu, need);
                     ptx::tmem_wait_ld();
                     if (any_mask) {
+                        // column c is visible iff c in [lo, hi] and c outside [h_lo, h_hi)
+                        // (one unsigned range test each; an empty [lo, hi] passes no column)
+                        const int lo_m = hi < lo ? -1 : lo;
+                        const unsigned vis_len = hi < lo ? 0u : (unsigned)(hi - lo);
+                        const int hl = h_lo < h_hi ? h_lo : -KC - 1;
+                        const unsigned hole_len = h_lo < h_hi ? (unsigned)(h_hi - h_lo) : 0u;
 #pragma unroll
-                        for (int c = 0; c < KC; ++c)
-                            s[c] = (c >= lo && c <= hi && (c < h_lo || c >= h_hi)) ? s[c] : sent;
+                        for (int c = 0; c < KC; ++c) {
+                            const bool vis = (unsigned)(c - lo_m) <= vis_len && (unsigned)(c - hl) >= hole_len;
+                            s[c] = vis ? s[c] : sent;
+                        }
                     }
                     float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
                     if (!neg_scale) {
