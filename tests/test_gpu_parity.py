@@ -89,6 +89,29 @@ def test_shapes_and_windows(dtype, d, n, w, g):
     assert max_abs(to_np(lse), want_lse) <= LSE_ABS_TOL
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_bf16_values_beyond_fp16_range(d):
+    """bf16 inputs with V values far outside the fp16 range (2^17, 7e4, -1e30) in a few
+    key tiles, a band tile and a global-key tile among them: P*V stays in bf16 (P split as
+    hi + lo), so every finite bf16 value is handled.  (The fp32 accumulator holds
+    sum p*v with p <= 2^8, so |v| far beyond 1e30 can overflow it; that range is not
+    covered.)"""
+    n, w, g = 1024, 200, [5, 900]
+    q, k, v = make_inputs(77 + d, 1, 2, n, d, torch.bfloat16)
+    v = v.clone()
+    v[0, 0, 130] = 131072.0            # key tile 1 of head 0 (band tiles start at q0 - w)
+    v[0, 1, 700, :8] = -1.0e30         # head 1
+    v[0, 0, 900] = 70000.0             # a global key row
+    out, lse = lca.sliding_window_attention_with_lse(q.cuda(), k.cuda(), v.cuda(), w, g, 0.1)
+    want, want_lse = swa_oracle.sliding_window_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                                         w, g, 0.1)
+    got = to_np(out)
+    scale = np.abs(want).max(axis=-1, keepdims=True).clip(min=1.0)  # per-row magnitude of O
+    assert np.isfinite(got).all()
+    assert (np.abs(got - want) / scale).max() <= 2e-3
+    assert max_abs(to_np(lse), want_lse) <= LSE_ABS_TOL
+
+
 @pytest.mark.parametrize("scale", [-0.2, 0.0, 1e-3])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_scale_edge_cases(scale, dtype):
