@@ -116,8 +116,8 @@ struct Ctl {
     uint64_t q_empty[2];
     uint64_t kv_full[4];
     uint64_t kv_empty[4];
-    uint64_t s_full[2];
-    uint64_t p_full[2];
+    uint64_t s_full[2][2];   // [query tile][half]: S columns of the half ready
+    uint64_t p_full[2][2];   // [query tile][half]: P of the half written
     uint64_t o_full[2];
     uint64_t o_free[2];
     uint64_t mma_drained[2];
@@ -253,8 +253,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
         for (int x = 0; x < 2; ++x) {
             ptx::mbar_init(&ctl->q_full[x], 1);
             ptx::mbar_init(&ctl->q_empty[x], 1);
-            ptx::mbar_init(&ctl->s_full[x], 1);
-            ptx::mbar_init(&ctl->p_full[x], 4 * H);
+            for (int h = 0; h < 2; ++h) {
+                ptx::mbar_init(&ctl->s_full[x][h], 1);
+                ptx::mbar_init(&ctl->p_full[x][h], 4);
+            }
             ptx::mbar_init(&ctl->o_full[x], 1);
             ptx::mbar_init(&ctl->o_free[x], 4 * H);
         }
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                 // groups); a k-step only advances the low word's start address
                 const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
                 const uint32_t qlo = ptx::smem_desc_sw128_lo(ptx::smem_u32(sQ) + X * C::kTileBytes, 0);
-                const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, BN, false);
+                const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, KC, false);
                 const uint32_t idesc_pv = ptx::idesc_f16(BF16, BM, D, true);
                 const uint32_t sx = tmem + X * 128;
                 int L = 0, qn = 0, pc = 0, oc = 0;
@@ -383,25 +385,31 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     if (ok) ptx::tc_fence_after();
                     return ok;
                 };
-                // S_X = Q_X K^T
-                auto issue_s = [&](int slot, int ncols) {
-                    const uint32_t idesc = (ncols == BN) ? idesc_s_full : ptx::idesc_f16(BF16, BM, ncols, false);
-                    const uint32_t klo = ptx::smem_desc_sw128_lo(sslots + slot * C::kTileBytes, 0);
+                // S_X[:, half h] = Q_X K[keys of half h]^T: keys [KC*h, KC*h + n) of the tile
+                // (n = ncols - KC*h, at most KC) into TMEM columns [KC*h, KC*h + n).  The K
+                // rows of half h start KC*h rows (KC*h*128 bytes, whole 8-row swizzle atoms)
+                // into each panel.
+                auto issue_s = [&](int slot, int ncols, int h) {
+                    int n = ncols - KC * h;
+                    if (n <= 0) return;
+                    if (n > KC) n = KC;
+                    const uint32_t idesc = (n == KC) ? idesc_s_full : ptx::idesc_f16(BF16, BM, n, false);
+                    const uint32_t klo =
+                        ptx::smem_desc_sw128_lo(sslots + slot * C::kTileBytes + KC * h * 128, 0);
 #pragma unroll
                     for (int ks = 0; ks < D / 16; ++ks) {
                         const uint32_t off = ((ks >> 2) * kPanelBytes + (ks & 3) * 32) >> 4;
-                        ptx::mma_f16_ss(sx, ptx::desc_join(qlo + off, dhi), ptx::desc_join(klo + off, dhi), idesc,
-                                        ks > 0 ? 1u : 0u);
+                        ptx::mma_f16_ss(sx + KC * h, ptx::desc_join(qlo + off, dhi), ptx::desc_join(klo + off, dhi),
+                                        idesc, ks > 0 ? 1u : 0u);
                     }
                 };
                 // O_{X,h} += P_{X,h} V[keys of half h].  P lives in S_X's TMEM columns: keys
                 // [32c, 32c + 32) of the tile occupy columns [32c, 32c + 32), hi pairs in the
                 // first 16 and, for bf16, lo pairs in the next 16 (two 16-bit elements per
                 // 32-bit column).  Half h owns keys [KC*h, KC*(h+1)) and accumulates into O_{X,h}.
-                auto issue_pv = [&](int slot, int ncols, bool first) {
+                auto issue_pv = [&](int slot, int ncols, bool first, int h) {
                     const uint32_t vlo = ptx::smem_desc_sw128_lo(sslots + slot * C::kTileBytes, kPanelBytes);
-#pragma unroll
-                    for (int h = 0; h < H; ++h) {
+                    {
                         const uint32_t dcol = tmem + C::kOCol + (X * H + h) * D;
 #pragma unroll
                         for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
@@ -423,36 +431,67 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     const bool act = X ? un.active[1] : un.active[0];
                     if (!W(&ctl->q_full[X], qn)) break;
                     ++qn;
-                    bool first = true;       // next P*V starts the accumulator
+                    bool first = true;       // next P*V starts the accumulators
                     int pend_lv = -1;        // slot use of V for the member tile whose P*V is pending
                     int pend_cols = 0;
-                    // P*V of the pending member tile; it precedes the next S MMA, which
-                    // overwrites the TMEM columns holding that tile's P
-                    auto pv_step = [&]() -> bool {
-                        if (!W(&ctl->p_full[X], pc)) return false;
+                    // P*V of the pending member tile for half h, after that half's P is written;
+                    // it precedes the half's next S MMA, which overwrites the TMEM columns
+                    // holding that P.  The first half also waits for the accumulators to be free
+                    // and for the V tile.
+                    auto pv_half = [&](int h) -> bool {
+                        if (!W(&ctl->p_full[X][h], pc)) return false;
+                        if (h == 0) {
+                            if (first && oc > 0 && !W(&ctl->o_free[X], oc - 1)) return false;
+                            if (!W(&ctl->kv_full[pend_lv % C::kSlots], pend_lv / C::kSlots)) return false;
+                        }
+                        issue_pv(pend_lv % C::kSlots, pend_cols, first, h);
+                        return true;
+                    };
+                    auto pv_done = [&]() {
                         ++pc;
-                        if (first && oc > 0 && !W(&ctl->o_free[X], oc - 1)) return false;
-                        if (!W(&ctl->kv_full[pend_lv % C::kSlots], pend_lv / C::kSlots)) return false;
-                        issue_pv(pend_lv % C::kSlots, pend_cols, first);
                         first = false;
                         ptx::mma_commit(&ctl->kv_empty[pend_lv % C::kSlots]);
-                        return true;
+                        pend_lv = -1;
                     };
                     for (int j = 0; j < un.ntiles && ok; ++j) {
                         const Tile t = tile_of(p, un, j);
                         const bool mem = act && (X ? t.mem[1] : t.mem[0]);
                         const int lk = L + 2 * j, lv = lk + 1;
-                        // The pending P*V goes first: it releases its V slot, which the producer
-                        // may need before it can load this tile (a 3-slot ring holds one tile
-                        // plus one V), and it must precede the next S MMA in any case.
-                        if (pend_lv >= 0) {
-                            if (!pv_step()) break;
-                            pend_lv = -1;
+                        if (H == 1 || !mem) {
+                            // The pending P*V goes first: it releases its V slot, which the
+                            // producer may need before it can load this tile (a 3-slot ring
+                            // holds one tile plus one V), and it must precede the next S MMA.
+                            if (pend_lv >= 0) {
+                                bool pv_ok = true;
+#pragma unroll
+                                for (int h = 0; h < H; ++h) pv_ok = pv_ok && pv_half(h);
+                                if (!pv_ok) break;
+                                pv_done();
+                            }
+                            if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
+                            if (mem) {
+                                issue_s(lk % C::kSlots, t.ncols, 0);
+                                ptx::mma_commit(&ctl->s_full[X][0]);
+                            }
+                        } else {
+                            // Two halves (4-slot ring): K of this tile can land while the
+                            // pending V is held, so each half runs its own chain, P*V of the
+                            // pending tile then S of this one, as soon as its P is written.
+                            if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
+                            bool s_ok = true;
+#pragma unroll
+                            for (int h = 0; h < H; ++h) {
+                                if (pend_lv >= 0 && !pv_half(h)) {
+                                    s_ok = false;
+                                    break;
+                                }
+                                issue_s(lk % C::kSlots, t.ncols, h);
+                                ptx::mma_commit(&ctl->s_full[X][h]);
+                            }
+                            if (!s_ok) break;
+                            if (pend_lv >= 0) pv_done();
                         }
-                        if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
                         if (mem) {
-                            issue_s(lk % C::kSlots, t.ncols);
-                            ptx::mma_commit(&ctl->s_full[X]);
                             ptx::mma_commit(&ctl->kv_empty[lk % C::kSlots]);
                             pend_lv = lv;
                             pend_cols = t.ncols;
@@ -465,7 +504,13 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     if (!ok) break;
                     // every S MMA of this unit has been issued: Q_X may be refilled once they complete
                     ptx::mma_commit(&ctl->q_empty[X]);
-                    if (pend_lv >= 0 && !pv_step()) break;
+                    if (pend_lv >= 0) {
+                        bool pv_ok = true;
+#pragma unroll
+                        for (int h = 0; h < H; ++h) pv_ok = pv_ok && pv_half(h);
+                        if (!pv_ok) break;
+                        pv_done();
+                    }
                     if (!first) {
                         ptx::mma_commit(&ctl->o_full[X]);
                         ++oc;
@@ -538,7 +583,8 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
             for (int j = 0; j < un.ntiles; ++j) {
                 const Tile t = tile_of(p, un, j);
                 if (!(X ? t.mem[1] : t.mem[0])) continue;
-                if (ok) ok = warp_wait(&ctl->s_full[X], sc & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+                if (ok) ok = warp_wait(&ctl->s_full[X][H == 1 ? 0 : hh], sc & 1, abort_flag, p.err,
+                                       LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
                 ++sc;
                 const int col0 = t.row0 + KC * hh;  // key (band) or compact global row of column 0
                 const int ncols_h = t.ncols - KC * hh;
@@ -688,7 +734,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                 seen = true;
                 ptx::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(&ctl->p_full[X]);
+                if (lane == 0) ptx::mbar_arrive(&ctl->p_full[X][H == 1 ? 0 : hh]);
             }
 
             // ---- epilogue: merge the halves, O / l -> fp32 rows via staging + TMA store
