@@ -167,7 +167,8 @@ typedef struct lca_shard_layout {
     size_t halo_send_offset;   /* [2 sides][2 (k, v)][batch*heads][halo_rows][head_dim], input dtype */
     size_t halo_recv_offset;   /* same layout */
     size_t halo_side_bytes;    /* bytes of one side of halo_send / halo_recv */
-    size_t rowpart_offset;     /* exchange C source */
+    size_t rowpart_offset;     /* exchange C source: fp32 O [batch*heads][G][head_dim], then fp32 LSE
+                                  [batch*heads][G], padded to a multiple of 16 bytes */
     size_t rowpart_bytes;
     size_t rowpart_all_offset; /* exchange C target: world_size * rowpart_bytes */
 } lca_shard_layout;

@@ -243,7 +243,9 @@ Layout make_layout(const Problem& P) {
         L.off_plse = off;
         off = align_up(off + (size_t)parts * bh * G * 4, kAlign);
         if (P.sharded) {
-            L.rowpart_bytes = (size_t)bh * G * (d + 1) * 4;  // O [bh][G][d], then LSE [bh][G]
+            // O [bh][G][d], then LSE [bh][G] padded to 16 bytes (each rank's block in the
+            // gathered region stays 16-byte aligned for the merge's float4 loads)
+            L.rowpart_bytes = (size_t)bh * G * d * 4 + align_up((size_t)bh * G * 4, 16);
             L.off_rowpart = off;
             off = align_up(off + L.rowpart_bytes, kAlign);
             L.off_rowpart_all = off;

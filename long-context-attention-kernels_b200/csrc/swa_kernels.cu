@@ -876,16 +876,19 @@ __global__ void __launch_bounds__(256) lca_pack_halo(HaloPackParams hp) {
 
 template <int D>
 __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp) {
-    // One warp per (bh, global row).  Lanes take partials in parallel for the max and the
-    // weights; the weighted sum then walks the partials with independent loads (lane =
-    // output column).
-    const long long w = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (w >= (long long)cp.num_global * cp.bh) return;
-    const int g = (int)(w % cp.num_global);
-    const int bh = (int)(w / cp.num_global);
+    // One block per (bh, global row).  Each warp finds the largest log-sum-exp with its
+    // lanes spread over the partials, then sums a quarter of the partials (lane = kPer
+    // adjacent output columns, independent loads); the four warps' sums meet in shared
+    // memory.
+    constexpr int kWarps = 4;
     constexpr int kPer = D / 32;
-    const size_t row = (size_t)bh * cp.num_global + g;
+    __shared__ float s_acc[kWarps][D];
+    __shared__ float s_w[kWarps];
+    const long long row = blockIdx.x;  // b * G + g
+    const int g = (int)(row % cp.num_global);
+    const int bh = (int)(row / cp.num_global);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
     auto valid = [&](int part) {
         if (cp.split_tiles == 0) return true;
         const int s = part >> 1;
@@ -901,40 +904,50 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
     for (int s = lane; s < cp.n_parts; s += 32) mx = fmaxf(mx, lse_of(s));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float wsum = 0.f;
-    for (int s = lane; s < cp.n_parts; s += 32) {
-        const float ls = lse_of(s);
-        wsum += (ls == -INFINITY) ? 0.f : __expf(ls - mx);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
     float acc[kPer];
 #pragma unroll
     for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
+    float wsum = 0.f;
 #pragma unroll 4
-    for (int s = 0; s < cp.n_parts; ++s) {
+    for (int s = warp; s < cp.n_parts; s += kWarps) {
         const float ls = lse_of(s);
         if (ls == -INFINITY) continue;
         const float wt = __expf(ls - mx);
-        const float* po = cp.part_o + (size_t)s * cp.part_stride_o + row * D;
-#pragma unroll
-        for (int e = 0; e < kPer; ++e) acc[e] += wt * __ldg(po + lane + 32 * e);
+        const float* po = cp.part_o + (size_t)s * cp.part_stride_o + row * D + lane * kPer;
+        wsum += wt;
+        if constexpr (kPer == 2) {
+            const float2 v = __ldg(reinterpret_cast<const float2*>(po));
+            acc[0] += wt * v.x;
+            acc[1] += wt * v.y;
+        } else {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(po));
+            acc[0] += wt * v.x;
+            acc[1] += wt * v.y;
+            acc[2] += wt * v.z;
+            acc[3] += wt * v.w;
+        }
     }
-    const float inv = 1.f / wsum;
-    const float lse = mx + __logf(wsum);
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) s_acc[warp][lane * kPer + e] = acc[e];
+    if (lane == 0) s_w[warp] = wsum;
+    __syncthreads();
+    const float wtot = (s_w[0] + s_w[1]) + (s_w[2] + s_w[3]);
+    const float inv = 1.f / wtot;
+    const float lse = mx + __logf(wtot);
+    float* out_row;
+    float* lse_out;
     if (cp.out_o != nullptr) {
-        float* out = cp.out_o + row * D;
-#pragma unroll
-        for (int e = 0; e < kPer; ++e) out[lane + 32 * e] = acc[e] * inv;
-        if (lane == 0) cp.out_lse[row] = lse;
-        return;
+        out_row = cp.out_o + row * D;
+        lse_out = cp.out_lse + row;
+    } else {
+        const int orow = cp.gidx[g] - cp.row_off;
+        if (orow < 0 || orow >= cp.n_rows) return;  // owned by another shard
+        out_row = cp.o + ((size_t)bh * cp.n_rows + orow) * D;
+        lse_out = cp.lse != nullptr ? cp.lse + (size_t)bh * cp.n_rows + orow : nullptr;
     }
-    const int orow = cp.gidx[g] - cp.row_off;
-    if (orow < 0 || orow >= cp.n_rows) return;  // owned by another shard
-    float* out = cp.o + ((size_t)bh * cp.n_rows + orow) * D;
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) out[lane + 32 * e] = acc[e] * inv;
-    if (cp.lse != nullptr && lane == 0) cp.lse[(size_t)bh * cp.n_rows + orow] = lse;
+    for (int c = threadIdx.x; c < D; c += blockDim.x)
+        out_row[c] = ((s_acc[0][c] + s_acc[1][c]) + (s_acc[2][c] + s_acc[3][c])) * inv;
+    if (threadIdx.x == 0 && lse_out != nullptr) *lse_out = lse;
 }
 
 }  // namespace
@@ -979,7 +992,8 @@ cudaError_t launch_gather(int head_dim, const void* q, const void* k, const void
 cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t stream) {
     const long long rows = (long long)cp.num_global * cp.bh;
     if (rows <= 0) return cudaSuccess;
-    const unsigned grid = (unsigned)((rows + 3) / 4);
+    if (rows > INT_MAX) return cudaErrorInvalidValue;
+    const unsigned grid = (unsigned)rows;
     if (head_dim == 64)
         lca_combine_global_rows<64><<<grid, 128, 0, stream>>>(cp);
     else if (head_dim == 128)

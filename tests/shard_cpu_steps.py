@@ -122,7 +122,7 @@ class CpuShardSteps:
             pl = mx[..., 0] + np.log(l)
             rp = _region(ws, lay.rowpart_offset, lay.rowpart_bytes, torch.float32)
             rp[:bh * G * d] = torch.from_numpy(po.reshape(-1)).float()
-            rp[bh * G * d:] = torch.from_numpy(pl.reshape(-1)).float()
+            rp[bh * G * d:bh * G * (d + 1)] = torch.from_numpy(pl.reshape(-1)).float()
 
     def finish(self, spec, out, lse, tokens, ws):
         lay = self.layout(spec, len(tokens))
@@ -134,7 +134,7 @@ class CpuShardSteps:
         allp = _region(ws, lay.rowpart_all_offset, world * lay.rowpart_bytes, torch.float32).double().numpy()
         allp = allp.reshape(world, -1)
         po = allp[:, :bh * G * d].reshape(world, bh, G, d)
-        pl = allp[:, bh * G * d:].reshape(world, bh, G)
+        pl = allp[:, bh * G * d:bh * G * (d + 1)].reshape(world, bh, G)
         mx = pl.max(axis=0)
         wts = np.exp(pl - mx[None])
         o = (wts[..., None] * po).sum(axis=0) / wts.sum(axis=0)[..., None]

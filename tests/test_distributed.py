@@ -54,7 +54,9 @@ def test_shard_layout_sizes():
     assert lay.halo_rows == w
     assert lay.globals_bytes == 3 * bh * G * d * 2 and lay.globals_row_bytes == 3 * bh * d * 2
     assert lay.halo_side_bytes == 2 * bh * w * d * 2
-    assert lay.rowpart_bytes == bh * G * (d + 1) * 4
+    assert lay.rowpart_bytes == bh * G * d * 4 + -(-bh * G * 4 // 16) * 16 and lay.rowpart_bytes % 16 == 0
+    st, lay_odd = c.shard_layout(_spec(heads=1).desc(), 5)  # 5 LSE floats pad to 8
+    assert st == c.OK and lay_odd.rowpart_bytes == 5 * d * 4 + 32
     regions = sorted([(lay.globals_offset, lay.globals_bytes), (lay.halo_send_offset, 2 * lay.halo_side_bytes),
                       (lay.halo_recv_offset, 2 * lay.halo_side_bytes), (lay.rowpart_offset, lay.rowpart_bytes),
                       (lay.rowpart_all_offset, 8 * lay.rowpart_bytes)])
