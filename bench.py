@@ -47,6 +47,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=None,
                     help="override heads per GPU (smaller cases for profiling; not the headline config)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="sequence shards: halos / global rows / row partials by the library's NVLink peer "
+                         "stores (default) or through NCCL")
     ap.add_argument("--parallel", choices=["heads", "sequence"], default=None,
                     help="multi-GPU split: independent head shards (default) or contiguous sequence shards "
                          "(default for context_128k_d128)")
@@ -357,7 +360,8 @@ def run_sequence(args):
     cpu_inputs = (qf, kf, vf) if (rank == 0 and world == 1) else None
     del qf, kf, vf
     cabi = _native.cabi()
-    plan = ShardedAttention(w.batch, w.heads, w.seq_len, w.head_dim, w.window, g, w.scale, w.torch_dtype, device=dev)
+    plan = ShardedAttention(w.batch, w.heads, w.seq_len, w.head_dim, w.window, g, w.scale, w.torch_dtype, device=dev,
+                            exchange=args.exchange)
     plan.capture(q, k, v, warmup=max(args.warmup, 3))
     for _ in range(max(args.warmup, 3)):
         plan.replay()
@@ -438,6 +442,7 @@ def run_sequence(args):
                        "head_dim": w.head_dim, "window": w.window, "num_global": len(g),
                        "tokens_per_gpu_step": ln * w.batch * w.heads,
                        "parallelism": f"sequence-sharded x{world}", "cuda_graph": True,
+                       "exchange": plan.exchange,
                        "l2": "inputs larger than L2 (shard Q/K/V/O resident: %.0f MB)" % (shard_io / 1e6)},
             "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved_tf / peak_tf, "traffic": None, "kernel": "lca_swa_main",
@@ -447,8 +452,10 @@ def run_sequence(args):
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)) * world,
                     "d2h_bytes_per_step": oh.numel() * 4 * world, "ms_per_step": e2e_ms},
-            # halo pack (2+ shards) and main; with global tokens also gather and two merges
-            "gpu_launches": args.steps * ((2 if world > 1 else 1) + (3 if g else 0)),
+            # main, halo pack (2+ shards), the two peer puts and the peer merge (peer exchange);
+            # with global tokens also gather, local merge (and the final merge over NCCL)
+            "gpu_launches": args.steps * (
+                (5 + (2 if g else 0)) if plan.exchange == "peer" else ((2 if world > 1 else 1) + (3 if g else 0))),
             "clocks": clocks.report(),
         }
         print(json.dumps(line), flush=True)

@@ -153,6 +153,7 @@ typedef struct lca_shard_desc {
     int64_t shard_offset; /* absolute index of this shard's first token */
     int64_t shard_len;    /* tokens in this shard (rows of q / k / v / out / lse) */
     int64_t world_size;   /* number of shards */
+    int64_t rank;         /* this shard's index; shard r-1 holds the tokens just before */
     int dtype;            /* LCA_DTYPE_* */
     float scale;
 } lca_shard_desc;
@@ -194,6 +195,41 @@ LCA_API int lca_swa_shard_forward(const lca_shard_desc* desc, const void* q, con
  * that fall in this shard to out / lse. */
 LCA_API int lca_swa_shard_finish(const lca_shard_desc* desc, float* out, float* lse, const int64_t* global_tokens,
                                  int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Peer-memory exchange for sequence shards: one process per GPU, all GPUs in one NVLink
+ * domain.  Instead of the caller's collectives, the library writes the halos, the global
+ * rows and the row partials straight into the other ranks' workspaces over NVLink and
+ * waits on counters there (bounded: a rank that stops leaves LCA_ERR_DEVICE to
+ * lca_device_error on the others).  Each rank allocates its workspace with
+ * lca_peer_alloc, sends the 64-byte handle to the others, and maps theirs with
+ * lca_peer_open; `peer_workspaces[r]` is rank r's workspace (this rank's own at
+ * [rank]).  A step is then: lca_swa_shard_prepare, lca_swa_shard_exchange_peer,
+ * lca_swa_shard_forward, lca_swa_shard_finish_peer -- no other exchange.  Every rank must
+ * run the same steps; never run two ranks on one GPU (their waits need both to run at
+ * once).  Ranks hold consecutive shards in rank order.
+ */
+
+/* cudaMalloc `bytes` (zero-filled) and its CUDA IPC handle (64 bytes) for other processes. */
+LCA_API int lca_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+/* Map another process's lca_peer_alloc buffer from its IPC handle. */
+LCA_API int lca_peer_open(const void* ipc_handle, void** dev_ptr);
+/* Unmap a buffer mapped by lca_peer_open. */
+LCA_API int lca_peer_close(void* dev_ptr);
+/* Free a buffer from lca_peer_alloc. */
+LCA_API int lca_peer_free(void* dev_ptr);
+
+/* Exchange A+B by peer stores: this rank's global rows to every rank, its halo blocks to
+ * its neighbours, then wait for every other rank's. */
+LCA_API int lca_swa_shard_exchange_peer(const lca_shard_desc* desc, const int64_t* global_tokens,
+                                        int64_t num_global_tokens, void* const* peer_workspaces,
+                                        size_t workspace_bytes, void* stream);
+
+/* Exchange C by peer stores, then step 5: this rank's global-row partial into every
+ * rank's gathered region, wait for all, merge into the global rows this shard owns. */
+LCA_API int lca_swa_shard_finish_peer(const lca_shard_desc* desc, float* out, float* lse,
+                                      const int64_t* global_tokens, int64_t num_global_tokens,
+                                      void* const* peer_workspaces, size_t workspace_bytes, void* stream);
 
 /*
  * Measurement hook (no counterpart in the reference): when both events are non-NULL,

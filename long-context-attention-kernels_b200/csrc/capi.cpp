@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -179,6 +180,9 @@ int parse_shard(Problem& P, const lca_shard_desc* sd, const int64_t* global_toke
                           global_tokens, num_global_tokens);
     if (st != LCA_OK) return st;
     if (sd->world_size < 1) return fail(LCA_ERR_INVALID_ARGUMENT, "world_size must be >= 1");
+    if (sd->rank < 0 || sd->rank >= sd->world_size)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "rank %lld outside [0, %lld)", (long long)sd->rank,
+                    (long long)sd->world_size);
     if (sd->shard_offset < 0 || sd->shard_len < 1 || sd->shard_offset + sd->shard_len > sd->seq_len)
         return fail(LCA_ERR_INVALID_ARGUMENT, "shard [%lld, %lld) is not inside the sequence of %lld tokens",
                     (long long)sd->shard_offset, (long long)(sd->shard_offset + sd->shard_len), (long long)sd->seq_len);
@@ -207,9 +211,10 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 struct Layout {
     int g_tiles = 0, key_tiles = 0, n_splits = 0, split_tiles = 0;
     size_t grow_bytes = 0;  // one compact global row: [3][bh][d]
+    size_t off_sig = 0;     // sequence shards: peer-exchange counters (lca::PeerSignals)
     size_t off_gidx = 0, off_globals = 0, off_po = 0, off_plse = 0;
     size_t off_send = 0, off_recv = 0, halo_block = 0;  // halo_block: one side, [2][bh][halo][d]
-    size_t off_rowpart = 0, rowpart_bytes = 0, off_rowpart_all = 0;
+    size_t off_rowpart = 0, rowpart_bytes = 0, off_rowpart_all = 0;  // rowpart_all: two buffers
     size_t total = 0;
 };
 
@@ -218,11 +223,16 @@ struct Layout {
 // sized at about twice a band unit's work so units stay similar in length, but shrunk
 // until there are enough units to occupy every SM.  Each split yields two partial
 // results (even / odd tiles).
+//
+// For a sequence shard the regions other ranks write come first -- signal counters,
+// compact global rows, halo receive blocks, gathered row partials -- and their sizes
+// depend only on quantities every rank shares (heads, G, d, window, world), so they sit
+// at the same offsets on every rank.  The rank's own regions follow.
 Layout make_layout(const Problem& P) {
     Layout L;
     const int64_t bh = P.bh, G = P.G, d = P.d;
-    size_t off = 0;
-    if (G > 0 && bh > 0 && P.n > 0) {
+    const bool glob = G > 0 && bh > 0 && P.n > 0;
+    if (glob) {
         L.g_tiles = (int)((G + lca::kTileRows - 1) / lca::kTileRows);
         L.key_tiles = (int)((P.n + lca::kTileRows - 1) / lca::kTileRows);
         const int64_t band_tiles = (P.lead() + P.window + 2 * lca::kTileRows - 1) / lca::kTileRows + L.g_tiles;
@@ -232,32 +242,45 @@ Layout make_layout(const Problem& P) {
         split += split & 1;
         L.split_tiles = (int)split;
         L.n_splits = (L.key_tiles + L.split_tiles - 1) / L.split_tiles;
-        const int64_t parts = 2 * (int64_t)L.n_splits;
+        L.grow_bytes = (size_t)3 * bh * d * 2;
+        if (P.sharded) {
+            // O [bh][G][d], then LSE [bh][G] padded to 16 bytes (each rank's block in the
+            // gathered region stays 16-byte aligned for the merge's float4 loads)
+            L.rowpart_bytes = (size_t)bh * G * d * 4 + align_up((size_t)bh * G * 4, 16);
+        }
+    }
+    if (P.halo() > 0 && bh > 0) L.halo_block = (size_t)2 * bh * P.halo() * d * 2;
+    const int64_t parts = 2 * (int64_t)L.n_splits;
+    size_t off = 0;
+    if (P.sharded) {
+        L.off_sig = off;
+        off = align_up(off + sizeof(lca::PeerSignals), kAlign);
+        L.off_globals = off;  // compact rows [G][3 (q, k, v)][bh][d]
+        off = align_up(off + (size_t)G * L.grow_bytes, kAlign);
+        L.off_recv = off;
+        off = align_up(off + 2 * L.halo_block, kAlign);
+        L.off_rowpart_all = off;
+        off = align_up(off + 2 * L.rowpart_bytes * (size_t)P.world, kAlign);
+        // this rank's own regions
         L.off_gidx = off;
         off = align_up(off + sizeof(int) * G, kAlign);
-        L.grow_bytes = (size_t)3 * bh * d * 2;
-        L.off_globals = off;  // compact rows [G][3 (q, k, v)][bh][d]
+        L.off_po = off;
+        off = align_up(off + (size_t)parts * bh * G * d * 4, kAlign);
+        L.off_plse = off;
+        off = align_up(off + (size_t)parts * bh * G * 4, kAlign);
+        L.off_rowpart = off;
+        off = align_up(off + L.rowpart_bytes, kAlign);
+        L.off_send = off;
+        off = align_up(off + 2 * L.halo_block, kAlign);
+    } else if (glob) {
+        L.off_gidx = off;
+        off = align_up(off + sizeof(int) * G, kAlign);
+        L.off_globals = off;
         off = align_up(off + (size_t)G * L.grow_bytes, kAlign);
         L.off_po = off;
         off = align_up(off + (size_t)parts * bh * G * d * 4, kAlign);
         L.off_plse = off;
         off = align_up(off + (size_t)parts * bh * G * 4, kAlign);
-        if (P.sharded) {
-            // O [bh][G][d], then LSE [bh][G] padded to 16 bytes (each rank's block in the
-            // gathered region stays 16-byte aligned for the merge's float4 loads)
-            L.rowpart_bytes = (size_t)bh * G * d * 4 + align_up((size_t)bh * G * 4, 16);
-            L.off_rowpart = off;
-            off = align_up(off + L.rowpart_bytes, kAlign);
-            L.off_rowpart_all = off;
-            off = align_up(off + L.rowpart_bytes * (size_t)P.world, kAlign);
-        }
-    }
-    if (P.halo() > 0 && bh > 0) {
-        L.halo_block = (size_t)2 * bh * P.halo() * d * 2;
-        L.off_send = off;
-        off = align_up(off + 2 * L.halo_block, kAlign);
-        L.off_recv = off;
-        off = align_up(off + 2 * L.halo_block, kAlign);
     }
     L.total = off;
     return L;
@@ -681,6 +704,195 @@ int lca_swa_shard_finish(const lca_shard_desc* desc, float* out, float* lse, con
     cp.row_off = (int)P.q_off;
     cudaError_t e = lca::launch_combine((int)P.d, cp, static_cast<cudaStream_t>(stream_ptr));
     if (e != cudaSuccess) return fail_cuda(e, "shard combine launch");
+    return LCA_OK;
+}
+
+// ------------------------------------------------------------------ peer-memory exchange
+
+int lca_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {
+    if (dev_ptr == nullptr || ipc_handle == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "NULL output");
+    *dev_ptr = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes > 0 ? bytes : 1);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(peer workspace)");
+    e = cudaMemset(p, 0, bytes > 0 ? bytes : 1);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail_cuda(e, "peer workspace setup");
+    }
+    *dev_ptr = p;
+    return LCA_OK;
+}
+
+int lca_peer_open(const void* ipc_handle, void** dev_ptr) {
+    if (dev_ptr == nullptr || ipc_handle == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "NULL argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaIpcOpenMemHandle");
+    return LCA_OK;
+}
+
+int lca_peer_close(void* dev_ptr) {
+    cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    return e == cudaSuccess ? LCA_OK : fail_cuda(e, "cudaIpcCloseMemHandle");
+}
+
+int lca_peer_free(void* dev_ptr) {
+    cudaError_t e = cudaFree(dev_ptr);
+    return e == cudaSuccess ? LCA_OK : fail_cuda(e, "cudaFree(peer workspace)");
+}
+
+}  // extern "C"
+
+namespace {
+
+int check_peer_args(const Problem& P, void* const* peers, size_t workspace_bytes, const Layout& L) {
+    if (P.world > lca::kMaxPeers)
+        return fail(LCA_ERR_UNSUPPORTED, "peer exchange supports at most %d ranks (got %lld)", lca::kMaxPeers,
+                    (long long)P.world);
+    if (peers == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "peer workspace array is NULL");
+    for (int64_t r = 0; r < P.world; ++r)
+        if (peers[r] == nullptr || (reinterpret_cast<uintptr_t>(peers[r]) % 256) != 0)
+            return fail(LCA_ERR_WORKSPACE, "peer workspace %lld is NULL or not 256-byte aligned", (long long)r);
+    if (workspace_bytes < L.total)
+        return fail(LCA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+    return LCA_OK;
+}
+
+uint8_t* at(void* const* peers, int64_t r, size_t off) { return static_cast<uint8_t*>(peers[r]) + off; }
+
+}  // namespace
+
+extern "C" {
+
+int lca_swa_shard_exchange_peer(const lca_shard_desc* desc, const int64_t* global_tokens, int64_t num_global_tokens,
+                                void* const* peer_workspaces, size_t workspace_bytes, void* stream_ptr) {
+    g_last_error.clear();
+    Problem P;
+    int st = parse_shard(P, desc, global_tokens, num_global_tokens);
+    if (st != LCA_OK) return st;
+    int dev = 0;
+    int* err_word = nullptr;
+    if ((st = check_device(&dev, &err_word)) != LCA_OK) return st;
+    const Layout L = make_layout(P);
+    if ((st = check_peer_args(P, peer_workspaces, workspace_bytes, L)) != LCA_OK) return st;
+    const int64_t rank = desc->rank;
+    lca::PeerPutParams pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.world = (int)P.world;
+    // this rank's run of compact global rows, to every other rank
+    int64_t g_lo = 0, g_hi = 0;
+    for (size_t i = 0; i < P.gl.size(); ++i) {
+        if (P.gl[i] < P.q_off) g_lo = (int64_t)i + 1;
+        if (P.gl[i] < P.q_off + P.n) g_hi = (int64_t)i + 1;
+    }
+    if (g_hi > g_lo) {
+        const size_t off = L.off_globals + (size_t)g_lo * L.grow_bytes;
+        for (int64_t r = 0; r < P.world; ++r) {
+            if (r == rank) continue;
+            pp.src[pp.n_jobs] = at(peer_workspaces, rank, off);
+            pp.dst[pp.n_jobs] = at(peer_workspaces, r, off);
+            pp.bytes[pp.n_jobs] = (unsigned long long)(g_hi - g_lo) * L.grow_bytes;
+            ++pp.n_jobs;
+        }
+    }
+    // halo blocks: side 0 (first rows) to rank - 1's side 1, side 1 (last rows) to rank + 1's side 0
+    if (L.halo_block > 0) {
+        if (rank > 0) {
+            pp.src[pp.n_jobs] = at(peer_workspaces, rank, L.off_send);
+            pp.dst[pp.n_jobs] = at(peer_workspaces, rank - 1, L.off_recv + L.halo_block);
+            pp.bytes[pp.n_jobs++] = L.halo_block;
+        }
+        if (rank < P.world - 1) {
+            pp.src[pp.n_jobs] = at(peer_workspaces, rank, L.off_send + L.halo_block);
+            pp.dst[pp.n_jobs] = at(peer_workspaces, rank + 1, L.off_recv);
+            pp.bytes[pp.n_jobs++] = L.halo_block;
+        }
+    }
+    for (int64_t r = 0; r < P.world; ++r) {
+        if (r == rank) continue;
+        pp.signal[r] = reinterpret_cast<unsigned int*>(at(peer_workspaces, r, L.off_sig) +
+                                                       offsetof(lca::PeerSignals, prep) + rank * sizeof(unsigned int));
+        pp.wait[r] = reinterpret_cast<unsigned int*>(at(peer_workspaces, rank, L.off_sig) +
+                                                     offsetof(lca::PeerSignals, prep) + r * sizeof(unsigned int));
+    }
+    pp.epoch = reinterpret_cast<const unsigned int*>(at(peer_workspaces, rank, L.off_sig) +
+                                                     offsetof(lca::PeerSignals, epoch));
+    pp.err = err_word;
+    pp.timeout_ns = wait_timeout_ns();
+    cudaError_t e = lca::launch_peer_put(pp, lca::kPeerPrepBlocks, static_cast<cudaStream_t>(stream_ptr));
+    if (e != cudaSuccess) return fail_cuda(e, "peer exchange launch");
+    return LCA_OK;
+}
+
+int lca_swa_shard_finish_peer(const lca_shard_desc* desc, float* out, float* lse, const int64_t* global_tokens,
+                              int64_t num_global_tokens, void* const* peer_workspaces, size_t workspace_bytes,
+                              void* stream_ptr) {
+    g_last_error.clear();
+    Problem P;
+    int st = parse_shard(P, desc, global_tokens, num_global_tokens);
+    if (st != LCA_OK) return st;
+    if (P.G > 0 && (out == nullptr || !aligned16(out)))
+        return fail(LCA_ERR_INVALID_ARGUMENT, "out must be non-NULL and 16-byte aligned");
+    int dev = 0;
+    int* err_word = nullptr;
+    if ((st = check_device(&dev, &err_word)) != LCA_OK) return st;
+    const Layout L = make_layout(P);
+    if ((st = check_peer_args(P, peer_workspaces, workspace_bytes, L)) != LCA_OK) return st;
+    const int64_t rank = desc->rank;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    uint8_t* own_sig = at(peer_workspaces, rank, L.off_sig);
+    // 1. this rank's row partial into slot `rank` of every rank's gathered region (the
+    //    buffer of the step's parity), then signal and wait: also the end-of-step barrier
+    //    that keeps any rank from overwriting buffers another rank still reads
+    lca::PeerPutParams pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.world = (int)P.world;
+    if (L.rowpart_bytes > 0) {
+        for (int64_t r = 0; r < P.world; ++r) {
+            pp.src[pp.n_jobs] = at(peer_workspaces, rank, L.off_rowpart);
+            pp.dst[pp.n_jobs] = at(peer_workspaces, r, L.off_rowpart_all + (size_t)rank * L.rowpart_bytes);
+            pp.bytes[pp.n_jobs] = L.rowpart_bytes;
+            pp.parity_bytes[pp.n_jobs] = (unsigned long long)P.world * L.rowpart_bytes;
+            ++pp.n_jobs;
+        }
+    }
+    for (int64_t r = 0; r < P.world; ++r) {
+        if (r == rank) continue;
+        pp.signal[r] = reinterpret_cast<unsigned int*>(at(peer_workspaces, r, L.off_sig) +
+                                                       offsetof(lca::PeerSignals, fin) + rank * sizeof(unsigned int));
+        pp.wait[r] = reinterpret_cast<unsigned int*>(own_sig + offsetof(lca::PeerSignals, fin) +
+                                                     r * sizeof(unsigned int));
+    }
+    pp.epoch = reinterpret_cast<const unsigned int*>(own_sig + offsetof(lca::PeerSignals, epoch));
+    pp.err = err_word;
+    pp.timeout_ns = wait_timeout_ns();
+    cudaError_t e = lca::launch_peer_put(pp, lca::kPeerCopyBlocks, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "peer row-partial launch");
+    // 2. merge over the shards' partials into the global rows this shard owns; its last
+    //    block advances the epoch
+    lca::CombineParams cp;
+    memset(&cp, 0, sizeof(cp));
+    cp.bh = (int)P.bh;
+    cp.num_global = (int)P.G;
+    cp.n_parts = (int)P.world;
+    cp.split_tiles = 0;
+    cp.part_stride_o = L.rowpart_bytes / 4;
+    cp.part_stride_lse = L.rowpart_bytes / 4;
+    cp.part_o = reinterpret_cast<const float*>(at(peer_workspaces, rank, L.off_rowpart_all));
+    cp.part_lse = cp.part_o + (size_t)P.bh * P.G * P.d;
+    cp.gidx = reinterpret_cast<const int*>(at(peer_workspaces, rank, L.off_gidx));
+    cp.o = out;
+    cp.lse = lse;
+    cp.n_rows = (int)P.n;
+    cp.row_off = (int)P.q_off;
+    cp.epoch = reinterpret_cast<unsigned int*>(own_sig + offsetof(lca::PeerSignals, epoch));
+    cp.ticket = reinterpret_cast<unsigned int*>(own_sig + offsetof(lca::PeerSignals, ticket));
+    cp.parity_floats = (size_t)P.world * L.rowpart_bytes / 4;
+    e = lca::launch_combine((int)P.d, cp, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "peer merge launch");
     return LCA_OK;
 }
 

@@ -885,10 +885,24 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
     __shared__ float s_acc[kWarps][D];
     __shared__ float s_w[kWarps];
     const long long row = blockIdx.x;  // b * G + g
+    if (row >= (long long)cp.num_global * cp.bh) {  // no global rows: only the epoch step below
+        if (cp.epoch != nullptr && threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(cp.ticket, 1u) == gridDim.x - 1) {
+                *cp.ticket = 0u;
+                atomicAdd(cp.epoch, 1u);
+            }
+        }
+        return;
+    }
     const int g = (int)(row % cp.num_global);
     const int bh = (int)(row / cp.num_global);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    if (cp.epoch != nullptr && ((*reinterpret_cast<volatile unsigned int*>(cp.epoch) + 1u) & 1u)) {
+        cp.part_o += cp.parity_floats;
+        cp.part_lse += cp.parity_floats;
+    }
     auto valid = [&](int part) {
         if (cp.split_tiles == 0) return true;
         const int s = part >> 1;
@@ -934,20 +948,65 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
     const float wtot = (s_w[0] + s_w[1]) + (s_w[2] + s_w[3]);
     const float inv = 1.f / wtot;
     const float lse = mx + __logf(wtot);
-    float* out_row;
-    float* lse_out;
+    float* out_row = nullptr;
+    float* lse_out = nullptr;
     if (cp.out_o != nullptr) {
         out_row = cp.out_o + row * D;
         lse_out = cp.out_lse + row;
     } else {
         const int orow = cp.gidx[g] - cp.row_off;
-        if (orow < 0 || orow >= cp.n_rows) return;  // owned by another shard
-        out_row = cp.o + ((size_t)bh * cp.n_rows + orow) * D;
-        lse_out = cp.lse != nullptr ? cp.lse + (size_t)bh * cp.n_rows + orow : nullptr;
+        if (orow >= 0 && orow < cp.n_rows) {  // else owned by another shard
+            out_row = cp.o + ((size_t)bh * cp.n_rows + orow) * D;
+            lse_out = cp.lse != nullptr ? cp.lse + (size_t)bh * cp.n_rows + orow : nullptr;
+        }
     }
-    for (int c = threadIdx.x; c < D; c += blockDim.x)
-        out_row[c] = ((s_acc[0][c] + s_acc[1][c]) + (s_acc[2][c] + s_acc[3][c])) * inv;
-    if (threadIdx.x == 0 && lse_out != nullptr) *lse_out = lse;
+    if (out_row != nullptr) {
+        for (int c = threadIdx.x; c < D; c += blockDim.x)
+            out_row[c] = ((s_acc[0][c] + s_acc[1][c]) + (s_acc[2][c] + s_acc[3][c])) * inv;
+        if (threadIdx.x == 0 && lse_out != nullptr) *lse_out = lse;
+    }
+    if (cp.epoch != nullptr) {
+        // the last block of the merge ends the peer step: every block has read the epoch
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(cp.ticket, 1u) == gridDim.x - 1) {
+                *cp.ticket = 0u;
+                atomicAdd(cp.epoch, 1u);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------ peer put
+
+__global__ void __launch_bounds__(256) lca_peer_put(PeerPutParams pp) {
+    const unsigned int e = *reinterpret_cast<volatile const unsigned int*>(pp.epoch) + 1u;
+    const unsigned long long tid = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const unsigned long long nthr = (unsigned long long)gridDim.x * blockDim.x;
+    for (int j = 0; j < pp.n_jobs; ++j) {
+        const uint4* src = static_cast<const uint4*>(pp.src[j]);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(pp.dst[j]) + ((e & 1u) ? pp.parity_bytes[j] : 0ull));
+        const unsigned long long n = pp.bytes[j] / 16;
+        for (unsigned long long i = tid; i < n; i += nthr) dst[i] = src[i];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if ((int)threadIdx.x < pp.world && pp.signal[threadIdx.x] != nullptr)
+        atomicAdd_system(pp.signal[threadIdx.x], 1u);
+    if (blockIdx.x == 0 && (int)threadIdx.x < pp.world && pp.wait[threadIdx.x] != nullptr) {
+        // bounded wait for every other rank's blocks of this step
+        const unsigned int target = e * gridDim.x;
+        const unsigned int* c = pp.wait[threadIdx.x];
+        const uint64_t t0 = ptx::global_timer_ns();
+        while ((int)(ptx::ld_acquire_sys(c) - target) < 0) {
+            if (ptx::global_timer_ns() - t0 > pp.timeout_ns) {
+                atomicCAS(pp.err, 0, LCA_DEVERR_TIMEOUT_PEER);
+                break;
+            }
+            __nanosleep(200);
+        }
+    }
 }
 
 }  // namespace
@@ -991,9 +1050,9 @@ cudaError_t launch_gather(int head_dim, const void* q, const void* k, const void
 
 cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t stream) {
     const long long rows = (long long)cp.num_global * cp.bh;
-    if (rows <= 0) return cudaSuccess;
+    if (rows <= 0 && cp.epoch == nullptr) return cudaSuccess;
     if (rows > INT_MAX) return cudaErrorInvalidValue;
-    const unsigned grid = (unsigned)rows;
+    const unsigned grid = rows > 0 ? (unsigned)rows : 1u;  // one block for the epoch step alone
     if (head_dim == 64)
         lca_combine_global_rows<64><<<grid, 128, 0, stream>>>(cp);
     else if (head_dim == 128)
@@ -1008,6 +1067,11 @@ cudaError_t launch_halo_pack(const HaloPackParams& hp, cudaStream_t stream) {
     if (chunks <= 0) return cudaSuccess;
     const long long blocks = std::min<long long>((chunks + 255) / 256, 148ll * 16);
     lca_pack_halo<<<(unsigned)blocks, 256, 0, stream>>>(hp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_peer_put(const PeerPutParams& pp, int blocks, cudaStream_t stream) {
+    lca_peer_put<<<blocks, 256, 0, stream>>>(pp);
     return cudaGetLastError();
 }
 

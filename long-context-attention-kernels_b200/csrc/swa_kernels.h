@@ -16,9 +16,22 @@ enum : int {
     LCA_DEVERR_TIMEOUT_MMA = 2,
     LCA_DEVERR_TIMEOUT_SOFTMAX = 3,
     LCA_DEVERR_TIMEOUT_DRAIN = 4,
+    LCA_DEVERR_TIMEOUT_PEER = 5,
 };
 
 constexpr int kTileRows = 128;        // query rows / keys per tile
+constexpr int kMaxPeers = 16;         // ranks of a peer-memory shard exchange
+constexpr int kPeerPrepBlocks = 64;   // blocks of the peer prepare kernel (each signals every peer)
+constexpr int kPeerCopyBlocks = 8;    // blocks of the peer row-partial copy kernel
+
+// Counters at the start of a shard workspace.  Other ranks add to them over NVLink
+// (system-scope atomics); they only grow, so one step's target is epoch * blocks.
+struct PeerSignals {
+    unsigned int prep[kMaxPeers];   // prepare blocks of rank s that finished writing here
+    unsigned int fin[kMaxPeers];    // copy blocks of rank s that finished writing here
+    unsigned int epoch;             // completed peer steps of this rank
+    unsigned int ticket;            // merge blocks done in the current step
+};
 constexpr int kGatherChunk = 1024;    // global indices passed per gather launch
 
 struct TensorMaps {
@@ -103,7 +116,34 @@ struct CombineParams {
     int n_rows, row_off;
     float* out_o;
     float* out_lse;
+    // peer exchange: when `epoch` is set the partials are read from the buffer of parity
+    // (epoch + 1) & 1 (parity_floats further on for odd), and the last block to finish
+    // advances *epoch
+    unsigned int* epoch;
+    unsigned int* ticket;
+    size_t parity_floats;
 };
+
+// Copies contiguous 16-byte-aligned ranges into other ranks' workspaces (or this rank's),
+// then bumps one counter on every other rank and, in block 0, waits until this rank's
+// counters from every other rank reach (epoch + 1) * gridDim.x.  The destination of job
+// j moves by parity_bytes[j] when epoch + 1 is odd (double-buffered regions).
+constexpr int kMaxPutJobs = kMaxPeers + 2;
+struct PeerPutParams {
+    int n_jobs;
+    int world;
+    const void* src[kMaxPutJobs];
+    void* dst[kMaxPutJobs];
+    unsigned long long bytes[kMaxPutJobs];
+    unsigned long long parity_bytes[kMaxPutJobs];
+    unsigned int* signal[kMaxPeers];   // counter on rank r to bump (nullptr: none, e.g. self)
+    unsigned int* wait[kMaxPeers];     // this rank's counter for rank s (nullptr: none)
+    const unsigned int* epoch;         // this rank's completed-step count
+    int* err;
+    unsigned long long timeout_ns;
+};
+
+cudaError_t launch_peer_put(const PeerPutParams& pp, int blocks, cudaStream_t stream);
 
 cudaError_t launch_main(int head_dim, bool bf16, const TensorMaps& tm, const MainParams& p, int grid,
                         cudaStream_t stream);

@@ -44,7 +44,8 @@ class ShardDesc(ctypes.Structure):
 
     _fields_ = [("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("seq_len", ctypes.c_int64),
                 ("head_dim", ctypes.c_int64), ("window_size", ctypes.c_int64), ("shard_offset", ctypes.c_int64),
-                ("shard_len", ctypes.c_int64), ("world_size", ctypes.c_int64), ("dtype", ctypes.c_int),
+                ("shard_len", ctypes.c_int64), ("world_size", ctypes.c_int64), ("rank", ctypes.c_int64),
+                ("dtype", ctypes.c_int),
                 ("scale", ctypes.c_float)]
 
 
@@ -103,6 +104,19 @@ class CABI:
         lib.lca_swa_shard_forward.argtypes = [dp, vp, vp, vp, vp, vp, ctypes.POINTER(i64), i64, vp, sz, vp]
         lib.lca_swa_shard_finish.restype = ctypes.c_int
         lib.lca_swa_shard_finish.argtypes = [dp, vp, vp, ctypes.POINTER(i64), i64, vp, sz, vp]
+        lib.lca_peer_alloc.restype = ctypes.c_int
+        lib.lca_peer_alloc.argtypes = [sz, ctypes.POINTER(vp), vp]
+        lib.lca_peer_open.restype = ctypes.c_int
+        lib.lca_peer_open.argtypes = [vp, ctypes.POINTER(vp)]
+        lib.lca_peer_close.restype = ctypes.c_int
+        lib.lca_peer_close.argtypes = [vp]
+        lib.lca_peer_free.restype = ctypes.c_int
+        lib.lca_peer_free.argtypes = [vp]
+        pp = ctypes.POINTER(vp)
+        lib.lca_swa_shard_exchange_peer.restype = ctypes.c_int
+        lib.lca_swa_shard_exchange_peer.argtypes = [dp, ctypes.POINTER(i64), i64, pp, sz, vp]
+        lib.lca_swa_shard_finish_peer.restype = ctypes.c_int
+        lib.lca_swa_shard_finish_peer.argtypes = [dp, vp, vp, ctypes.POINTER(i64), i64, pp, sz, vp]
         lib.lca_set_timing_events.restype = ctypes.c_int
         lib.lca_set_timing_events.argtypes = [vp, vp]
         lib.lca_device_error.restype = ctypes.c_int

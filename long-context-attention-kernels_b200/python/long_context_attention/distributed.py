@@ -31,6 +31,7 @@ problem up once and can capture the whole step, exchanges included, in a CUDA gr
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 from typing import Sequence
@@ -91,7 +92,7 @@ class ShardSpec:
 
     def desc(self) -> ShardDesc:
         return ShardDesc(self.batch, self.heads, self.seq_len, self.head_dim, self.window, self.offset, self.length,
-                         self.world_size, self.dtype_code, self.scale)
+                         self.world_size, self.rank, self.dtype_code, self.scale)
 
 
 def _check(st: int, lib: CABI, what: str) -> None:
@@ -137,6 +138,61 @@ class NativeShardSteps:
         st = self.lib.shard_finish(spec.desc(), out.data_ptr(), lse.data_ptr() if lse is not None else None, tokens,
                                    ws.data_ptr(), ws.numel(), self._stream(out))
         _check(st, self.lib, "lca_swa_shard_finish")
+
+    # ---- peer-memory exchange (no collectives library in the step)
+    def exchange_peer(self, spec, tokens, peers, nbytes, stream) -> None:
+        arr, n = CABI._tokens(tokens)
+        st = self.lib.lib.lca_swa_shard_exchange_peer(ctypes.byref(spec.desc()), arr, n, peers, nbytes, stream)
+        _check(st, self.lib, "lca_swa_shard_exchange_peer")
+
+    def finish_peer(self, spec, out, lse, tokens, peers, nbytes, stream) -> None:
+        arr, n = CABI._tokens(tokens)
+        st = self.lib.lib.lca_swa_shard_finish_peer(ctypes.byref(spec.desc()), out.data_ptr(),
+                                                    lse.data_ptr() if lse is not None else None, arr, n, peers,
+                                                    nbytes, stream)
+        _check(st, self.lib, "lca_swa_shard_finish_peer")
+
+
+class _PeerBuffer:
+    """This rank's workspace from lca_peer_alloc, with the other ranks' mapped (the data
+    pointer and size are all the compute steps use)."""
+
+    def __init__(self, lib: CABI, nbytes: int, rank: int, world: int, group, device):
+        self.lib, self.nbytes, self.rank = lib, nbytes, rank
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        _check(lib.lib.lca_peer_alloc(nbytes, ctypes.byref(ptr), handle), lib, "lca_peer_alloc")
+        self.ptr = ptr.value
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        allh = torch.empty(world * 64, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        allh = allh.cpu().numpy().reshape(world, 64)
+        self.opened = []
+        ptrs = []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self.ptr)
+                continue
+            h = (ctypes.c_ubyte * 64)(*allh[r].tolist())
+            pr = ctypes.c_void_p()
+            _check(lib.lib.lca_peer_open(h, ctypes.byref(pr)), lib, "lca_peer_open")
+            self.opened.append(pr.value)
+            ptrs.append(pr.value)
+        self.peers = (ctypes.c_void_p * world)(*ptrs)
+
+    def data_ptr(self) -> int:
+        return self.ptr
+
+    def numel(self) -> int:
+        return self.nbytes
+
+    def free(self) -> None:
+        for pr in self.opened:
+            self.lib.lib.lca_peer_close(ctypes.c_void_p(pr))
+        self.opened = []
+        if self.ptr:
+            self.lib.lib.lca_peer_free(ctypes.c_void_p(self.ptr))
+            self.ptr = 0
 
 
 def _dtype_code(dtype: torch.dtype) -> int:
@@ -224,11 +280,16 @@ class ShardedAttention:
     short enough for host-side launch work to matter.  Outputs live in :attr:`out` (and
     :attr:`lse`) and are overwritten by every call.  All ranks of `group` must build the
     same plan and call it in the same order.
+
+    ``exchange="peer"`` moves the halos, global rows and row partials by NVLink stores
+    from the library's own kernels into the other ranks' workspaces (CUDA IPC mappings
+    made at construction; one GPU per rank), with bounded waits on counters there, so a
+    step runs no collective at all.  ``"nccl"`` (default) uses the process group.
     """
 
     def __init__(self, batch: int, heads: int, seq_len: int, head_dim: int, window_size: int,
                  global_tokens: Sequence[int] = (), scale: float | None = None, dtype=torch.bfloat16, *,
-                 group=None, device=None, return_lse: bool = False, steps=None):
+                 group=None, device=None, return_lse: bool = False, steps=None, exchange: str = "nccl"):
         if dist.is_available() and dist.is_initialized():
             self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         else:
@@ -257,7 +318,21 @@ class ShardedAttention:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
-        self.ws = self.steps.workspace(self.layout.total_bytes, self.device)
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange must be 'nccl' or 'peer'")
+        self.exchange = exchange if self.world > 1 else "nccl"
+        if self.exchange == "peer":
+            if steps is not None:
+                raise ValueError("the peer exchange runs the native steps only")
+            # the peer steps wait on each other across ranks: one GPU per rank
+            ids = [None] * self.world
+            dist.all_gather_object(ids, str(torch.cuda.get_device_properties(self.device).uuid), group=group)
+            if len(set(ids)) != self.world:
+                raise RuntimeError("long_context_attention: the peer exchange needs one GPU per rank")
+            self.ws = _PeerBuffer(self.steps.lib, self.layout.total_bytes, self.rank, self.world, group,
+                                  self.device)
+        else:
+            self.ws = self.steps.workspace(self.layout.total_bytes, self.device)
         self.out = torch.empty(batch, heads, ln, head_dim, dtype=torch.float32, device=self.device)
         self.lse = torch.empty(batch, heads, ln, dtype=torch.float32, device=self.device) if return_lse else None
         self.graph = None
@@ -279,6 +354,13 @@ class ShardedAttention:
 
     def _run(self, Q, K, V):
         spec, lay, ws = self.spec, self.layout, self.ws
+        if self.exchange == "peer":
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            self.steps.prepare(spec, Q, K, V, self.tokens, ws)
+            self.steps.exchange_peer(spec, self.tokens, ws.peers, ws.nbytes, stream)
+            self.steps.forward(spec, Q, K, V, self.out, self.lse, self.tokens, ws)
+            self.steps.finish_peer(spec, self.out, self.lse, self.tokens, ws.peers, ws.nbytes, stream)
+            return
         self.steps.prepare(spec, Q, K, V, self.tokens, ws)
         exchange_p2p(ws, lay, self.runs, self.rank, self.world, self.group)
         self.steps.forward(spec, Q, K, V, self.out, self.lse, self.tokens, ws)
@@ -320,9 +402,15 @@ class ShardedAttention:
 
     def release(self) -> None:
         """Drop the captured graph (it holds NCCL work: release it before destroying the
-        process group)."""
+        process group) and, for the peer exchange, unmap the other ranks' workspaces and
+        free this one once every rank is done with them (a collective call)."""
         self.graph = None
         self._graph_inputs = None
+        if isinstance(self.ws, _PeerBuffer):
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            self.ws.free()
+            self.ws = None
 
 
 def sliding_window_attention_sharded(

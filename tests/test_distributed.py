@@ -66,7 +66,7 @@ def test_shard_layout_sizes():
     # no globals: no global-row regions; one shard: no halo
     st, lay0 = c.shard_layout(_spec().desc(), 0)
     assert st == c.OK and lay0.globals_bytes == 0 and lay0.rowpart_bytes == 0 and lay0.halo_side_bytes > 0
-    st, lay1 = c.shard_layout(_spec(world_size=1, offset=0, length=131072).desc(), 16)
+    st, lay1 = c.shard_layout(_spec(world_size=1, rank=0, offset=0, length=131072).desc(), 16)
     assert st == c.OK and lay1.halo_rows == 0 and lay1.halo_side_bytes == 0
 
 
@@ -79,6 +79,7 @@ def test_shard_validation():
         (_spec(world_size=0), c.ERR_INVALID_ARGUMENT),
         (_spec(head_dim=96), c.ERR_UNSUPPORTED),
         (_spec(window=-1), c.ERR_INVALID_ARGUMENT),
+        (_spec(rank=8), c.ERR_INVALID_ARGUMENT),                  # rank outside [0, world_size)
     ]
     for spec, code in bad:
         st, _ = c.shard_layout(spec.desc(), 4)

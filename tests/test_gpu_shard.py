@@ -186,3 +186,63 @@ def test_nccl_ranks_match_oracle(tmp_path):
     assert max_abs(out, ref_o) <= MAX_ABS_TOL
     assert rel_l2(out, ref_o) <= REL_L2_TOL
     assert max_abs(lse, ref_l) <= LSE_ABS_TOL
+
+
+def _peer_rank(rank, world, port, outdir, cases):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        from long_context_attention.distributed import ShardedAttention
+
+        for ci, (n, d, w, g, seed) in enumerate(cases):
+            q, k, v = make_inputs(seed, 1, 2, n, d, torch.bfloat16)
+            plan = ShardedAttention(1, 2, n, d, w, g, 0.1, torch.bfloat16, device=dev, return_lse=True,
+                                    exchange="peer")
+            off, ln = plan.shard
+            qs, ks, vs = (t[:, :, off:off + ln].contiguous().to(dev) for t in (q, k, v))
+            outs = []
+            for _ in range(3):  # eager steps (the step counter advances each time)
+                o, l = plan(qs, ks, vs)
+                outs.append((o.clone(), l.clone()))
+            plan.capture(qs, ks, vs)
+            for _ in range(3):
+                o, l = plan.replay()
+            torch.cuda.synchronize()
+            outs.append((o.clone(), l.clone()))
+            assert lca.device_error() == 0
+            for i, (o, l) in enumerate(outs):
+                np.save(os.path.join(outdir, f"c{ci}_s{i}_o{rank}.npy"), o.cpu().numpy())
+                np.save(os.path.join(outdir, f"c{ci}_s{i}_l{rank}.npy"), l.cpu().numpy())
+            plan.release()
+    finally:
+        dist.destroy_process_group()
+
+
+PEER_CASES = [(4096, 64, 300, [0, 1, 2047, 2048, 4000], 77), (2048, 128, 128, [], 78), (1920, 64, 64, [1919], 79)]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_exchange_ranks_match_oracle(tmp_path):
+    """The peer-memory exchange (NVLink stores into the other ranks' workspaces, no
+    collectives in the step): eager steps and CUDA-graph replays on 2-4 GPUs."""
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    mp.spawn(_peer_rank, args=(world, _free_port(), str(tmp_path), PEER_CASES), nprocs=world, join=True)
+    for ci, (n, d, w, g, seed) in enumerate(PEER_CASES):
+        q, k, v = make_inputs(seed, 1, 2, n, d, torch.bfloat16)
+        ref_o, ref_l = swa_oracle.sliding_window_attention(q.float().numpy(), k.float().numpy(),
+                                                           v.float().numpy(), w, g, 0.1)
+        for i in range(4):
+            out = np.concatenate([np.load(tmp_path / f"c{ci}_s{i}_o{r}.npy") for r in range(world)], axis=2)
+            lse = np.concatenate([np.load(tmp_path / f"c{ci}_s{i}_l{r}.npy") for r in range(world)], axis=2)
+            assert max_abs(out, ref_o) <= MAX_ABS_TOL, (ci, i)
+            assert rel_l2(out, ref_o) <= REL_L2_TOL, (ci, i)
+            assert max_abs(lse, ref_l) <= LSE_ABS_TOL, (ci, i)
