@@ -36,7 +36,9 @@
 // them into its own accumulator O_{X,h}; the H partial results of a row are merged by
 // log-sum-exp in the epilogue.  Thread r of a warpgroup <-> query row r <-> TMEM lane r.
 //   d = 64 : warps 0-15 softmax (A0, A1, B0, B1), warp 16 TMA producer, warps 17/18 MMA
-//            issuers for A/B (608 threads, no register split)
+//            issuers for A/B, warp 19 idle (640 threads; setmaxnreg: warpgroup 4 drops
+//            to 64 registers, warpgroups 0-3 rise to 104; 128*64 + 512*104 = 640*96, the
+//            launch allocation)
 //   d = 128: warps 0-7 softmax (A, B), warp 8 TMA, warps 9/10 MMA issuers for A/B, warp 11
 //            idle
 //            (384 threads; setmaxnreg: warpgroup 2 drops to 72 registers, warpgroups 0-1
@@ -89,9 +91,12 @@ struct Cfg {
     static constexpr int kSoftmaxWarps = 8 * kHalves;
     static constexpr int kTmaWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
-    static constexpr bool kRegSplit = (kHalves == 1);
-    static constexpr int kThreads = kRegSplit ? 384 : (kSoftmaxWarps + 3) * 32;
-    static constexpr int kRegsLaunch = 168, kRegsSoftmax = 216, kRegsControl = 72;
+    // softmax warpgroups, then one control warpgroup (TMA warp, two MMA warps, one idle)
+    static constexpr int kThreads = (kSoftmaxWarps + 4) * 32;
+    // registers per thread: at launch, after setmaxnreg in the softmax / control warpgroups
+    static constexpr int kRegsLaunch = (D == 64) ? 96 : 168;
+    static constexpr int kRegsSoftmax = (D == 64) ? 104 : 216;
+    static constexpr int kRegsControl = (D == 64) ? 64 : 72;
     static constexpr int kEpiCols = D / kHalves;           // output columns per warpgroup
     static constexpr int kPanels = D / 64;
     static constexpr int kTileBytes = BM * D * 2;
@@ -106,8 +111,9 @@ struct Cfg {
     static constexpr int kXchgBytes = (kHalves == 2) ? 2 * 2 * 2 * 128 * 2 * 4 : 0;
     static constexpr int kSmemBytes = kOffXchg + kXchgBytes + 1024;  // +1024 for base alignment
     static constexpr int kOCol = 256;
-    static_assert(!kRegSplit || 128 * kRegsControl + 256 * kRegsSoftmax == kThreads * kRegsLaunch,
+    static_assert(128 * kRegsControl + kSoftmaxWarps * 32 * kRegsSoftmax == kThreads * kRegsLaunch,
                   "register split must match the launch allocation");
+    static_assert(kThreads * kRegsLaunch <= 65536, "launch allocation exceeds the register file");
     static_assert(kOCol + 2 * kHalves * D <= kTmemCols, "TMEM columns");
 };
 
@@ -221,6 +227,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, r);
 }
 
+// Bit e set iff column c0 + e lies in [a, b) (e = 0..31; empty when b <= a).
+__device__ __forceinline__ uint32_t span_bits(int a, int b, int c0) {
+    const int x = min(max(a - c0, 0), 32);
+    const int y = min(max(b - c0, 0), 32);
+    return (uint32_t)((1ull << y) - 1ull) & ~(uint32_t)((1ull << x) - 1ull);
+}
+
 __device__ __forceinline__ uint32_t swz128(int row, int chunk16) {
     // byte offset of 16-byte chunk `chunk16` (0..7) of row `row` in a 128-byte-swizzled panel
     return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
@@ -279,7 +292,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
     const uint32_t tmem = ctl->tmem_base;
 
     if (warp >= C::kSoftmaxWarps) {
-        if constexpr (C::kRegSplit) ptx::setmaxnreg_dec<C::kRegsControl>();
+        ptx::setmaxnreg_dec<C::kRegsControl>();
         if (warp == C::kTmaWarp) {
             // ======================================================== TMA producer
             if (ptx::elect_one()) {
@@ -523,7 +536,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
             }
         }
     } else {
-        if constexpr (C::kRegSplit) ptx::setmaxnreg_inc<C::kRegsSoftmax>();
+        ptx::setmaxnreg_inc<C::kRegsSoftmax>();
         // ============================================================ softmax warpgroups
         const int sw = warp >> 2;         // softmax warpgroup
         const int X = sw / H;             // query tile of this warpgroup
@@ -619,19 +632,16 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     }
                     const bool need = lo > 0 || hi < KC - 1 || (h_lo < h_hi && h_hi > 0 && h_lo < KC);
                     const bool any_mask = __any_sync(0xffffffffu, need);
+                    // visible columns of each 32-column chunk as a bit mask: [lo, hi] minus
+                    // [h_lo, h_hi) (all ones when the warp needs no mask)
+                    uint32_t vis[KC / 32];
+#pragma unroll
+                    for (int c = 0; c < KC / 32; ++c)
+                        vis[c] = any_mask ? (span_bits(lo, hi + 1, c * 32) & ~span_bits(h_lo, h_hi, c * 32)) : ~0u;
                     ptx::tmem_wait_ld();
                     if (any_mask) {
-                        // column c is visible iff c in [lo, hi] and c outside [h_lo, h_hi)
-                        // (one unsigned range test each; an empty [lo, hi] passes no column)
-                        const int lo_m = hi < lo ? -1 : lo;
-                        const unsigned vis_len = hi < lo ? 0u : (unsigned)(hi - lo);
-                        const int hl = h_lo < h_hi ? h_lo : -KC - 1;
-                        const unsigned hole_len = h_lo < h_hi ? (unsigned)(h_hi - h_lo) : 0u;
 #pragma unroll
-                        for (int c = 0; c < KC; ++c) {
-                            const bool vis = (unsigned)(c - lo_m) <= vis_len && (unsigned)(c - hl) >= hole_len;
-                            s[c] = vis ? s[c] : sent;
-                        }
+                        for (int c = 0; c < KC; ++c) s[c] = ((vis[c >> 5] >> (c & 31)) & 1u) ? s[c] : sent;
                     }
                     float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
                     if (!neg_scale) {
@@ -682,45 +692,44 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     // maps to 0), row sum, 16-bit pairs written over the chunk's own S columns
                     // (hi pairs, then lo pairs for bf16).  Chunks masked for the whole warp skip
                     // the exponentials.
+                    // Pairs of columns go through the packed fp32x2 pipe: one FMA for the
+                    // exponent arguments, one add for the row sums and, for bf16, one
+                    // subtract for the low parts.
                     const float neg_m = (m == -INFINITY) ? 0.f : -m;
-                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                    const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
+                    const uint64_t negm2 = ptx::f2_pack(neg_m, neg_m);
+                    uint64_t acc0 = 0ull, acc1 = 0ull;  // {+0.f, +0.f}
 #pragma unroll
                     for (int c = 0; c < KC / 32; ++c) {
                         if (c >= nchunks) break;
                         const int c0 = c * 32;
-                        const bool in_none = hi < c0 || lo > c0 + 31 || (h_lo <= c0 && h_hi > c0 + 31);
-                        if (__all_sync(0xffffffffu, in_none)) {
+                        if (__all_sync(0xffffffffu, vis[c] == 0u)) {
                             uint32_t z[16];
 #pragma unroll
                             for (int e = 0; e < 16; ++e) z[e] = 0u;
                             ptx::tmem_st16u(t_lane + s_col + c0, z);
                             if (BF16) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
                         } else {
-                            float* v = s + c0;
-#pragma unroll
-                            for (int e = 0; e < 32; e += 4) {
-                                v[e + 0] = ptx::ex2(fmaf(v[e + 0], sl2, neg_m));
-                                v[e + 1] = ptx::ex2(fmaf(v[e + 1], sl2, neg_m));
-                                v[e + 2] = ptx::ex2(fmaf(v[e + 2], sl2, neg_m));
-                                v[e + 3] = ptx::ex2(fmaf(v[e + 3], sl2, neg_m));
-                                a0 += v[e + 0];
-                                a1 += v[e + 1];
-                                a2 += v[e + 2];
-                                a3 += v[e + 3];
-                            }
+                            const float* v = s + c0;
 #pragma unroll
                             for (int g8 = 0; g8 < 2; ++g8) {  // 8 pairs (16 keys) per store
                                 uint32_t w[8];
                                 uint32_t wl[8];
 #pragma unroll
                                 for (int e = 0; e < 8; ++e) {
-                                    const float x0 = v[g8 * 16 + 2 * e], x1 = v[g8 * 16 + 2 * e + 1];
+                                    const uint64_t x = ptx::f2_fma(
+                                        ptx::f2_pack(v[g8 * 16 + 2 * e], v[g8 * 16 + 2 * e + 1]), sl2x2, negm2);
+                                    const float p0 = ptx::ex2(ptx::f2_lo(x)), p1 = ptx::ex2(ptx::f2_hi(x));
+                                    const uint64_t pp = ptx::f2_pack(p0, p1);
+                                    if (e & 1) acc1 = ptx::f2_add(acc1, pp); else acc0 = ptx::f2_add(acc0, pp);
                                     if (BF16) {
-                                        w[e] = ptx::pack_bf16x2(x0, x1);
-                                        wl[e] = ptx::pack_bf16x2(x0 - __uint_as_float(w[e] << 16),
-                                                                 x1 - __uint_as_float(w[e] & 0xFFFF0000u));
+                                        w[e] = ptx::pack_bf16x2(p0, p1);
+                                        const uint64_t rest = ptx::f2_sub(
+                                            pp, ptx::f2_pack(__uint_as_float(w[e] << 16),
+                                                             __uint_as_float(w[e] & 0xFFFF0000u)));
+                                        wl[e] = ptx::pack_bf16x2(ptx::f2_lo(rest), ptx::f2_hi(rest));
                                     } else {
-                                        w[e] = ptx::pack_f16x2(x0, x1);
+                                        w[e] = ptx::pack_f16x2(p0, p1);
                                     }
                                 }
                                 ptx::tmem_st8u(t_lane + s_col + c0 + g8 * 8, w);
@@ -728,7 +737,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                             }
                         }
                     }
-                    l += (a0 + a1) + (a2 + a3);
+                    {
+                        const uint64_t a = ptx::f2_add(acc0, acc1);
+                        l += ptx::f2_lo(a) + ptx::f2_hi(a);
+                    }
                     ptx::tmem_wait_st();
                 }
                 seen = true;
