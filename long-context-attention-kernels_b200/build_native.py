@@ -31,8 +31,9 @@ CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CABI_SOURCES = ["swa_kernels.cu", "capi.cpp", "noalloc.cu"]
-CABI_HEADERS = ["sm100_ptx.cuh", "swa_kernels.h"]
+CABI_HEADERS = ["sm100_ptx.cuh", "swa_kernels.h", "trace.cuh"]
 LIB_NAME = "liblca_b200.so"
+TRACE_LIB_NAME = "liblca_b200_trace.so"  # -DLCA_TRACE: in-kernel event trace (trace.cuh)
 EXT_NAME = "long_context_attention_kernels"
 
 
@@ -56,10 +57,10 @@ def _run(cmd: list[str]) -> None:
     subprocess.run(cmd, check=True)
 
 
-def build_cabi(force: bool = False, verbose_ptxas: bool = False) -> str:
+def build_cabi(force: bool = False, verbose_ptxas: bool = False, trace: bool = False) -> str:
     srcs = [os.path.join(CSRC, s) for s in CABI_SOURCES]
     deps = srcs + [os.path.join(CSRC, h) for h in CABI_HEADERS] + [os.path.join(INCLUDE, "lca.h")]
-    out = lib_path()
+    out = os.path.join(PKGDIR, TRACE_LIB_NAME) if trace else lib_path()
     if not force and not _stale(out, deps):
         return out
     tmp = out + ".tmp"
@@ -68,6 +69,8 @@ def build_cabi(force: bool = False, verbose_ptxas: bool = False) -> str:
            "-DLCA_BUILDING_LIBRARY", "-o", tmp, *srcs]
     if verbose_ptxas:
         cmd.insert(1, "-Xptxas=-v")
+    if trace:
+        cmd.insert(1, "-DLCA_TRACE")
     _run(cmd)
     os.replace(tmp, out)
     return out
@@ -106,8 +109,12 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--ptxas-verbose", action="store_true")
+    ap.add_argument("--trace", action="store_true",
+                    help=f"also build {TRACE_LIB_NAME}, the C ABI with the in-kernel event trace")
     a = ap.parse_args(argv)
     build(force=a.force, verbose_ptxas=a.ptxas_verbose)
+    if a.trace:
+        build_cabi(force=a.force, verbose_ptxas=a.ptxas_verbose, trace=True)
     return 0
 
 

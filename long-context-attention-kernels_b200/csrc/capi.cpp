@@ -920,4 +920,15 @@ int lca_device_error(int* code) {
     return LCA_OK;
 }
 
+#ifdef LCA_TRACE
+// Trace builds only (not in the public header): copy the main kernel's event trace out.
+LCA_API int lca_trace_read(void* host, size_t bytes) {
+    if (host == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "host is NULL");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = lca::trace_read(host, bytes);
+    if (e != cudaSuccess) return fail_cuda(e, "trace read");
+    return LCA_OK;
+}
+#endif
+
 }  // extern "C"

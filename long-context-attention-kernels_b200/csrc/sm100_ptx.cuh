@@ -79,6 +79,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
     return ok != 0;
 }
 
+// Non-blocking probe: has phase `parity` of `bar` completed?
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on phase `parity` of `bar`.  `abort_flag` is a CTA-shared word: once
 // any role of the CTA gives up, every other wait returns false promptly (within one
 // suspend period).  On timeout the CTA-wide abort flag and the device-wide error word
@@ -141,6 +154,11 @@ __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bu
 // (tensor cores reading a descriptor, TMA stores).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Arrive on a named barrier without waiting (the other `count` - 32k threads sync on it).
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // Named barrier among `count` threads (ids 1..15; 0 is __syncthreads).

@@ -61,11 +61,18 @@
 
 #include "sm100_ptx.cuh"
 #include "swa_kernels.h"
+#include "trace.cuh"
 
 namespace lca {
 
 // Device-side error word: the first bounded wait that gives up records its code here.
 __device__ int g_error_word = 0;
+
+// trace events from lane 0 of a warp (no code unless built with LCA_TRACE)
+#define LCA_TRACE_LANE0(code)                  \
+    do {                                       \
+        if (lane == 0) LCA_TRACE_EVENT(code); \
+    } while (0)
 
 namespace {
 
@@ -74,6 +81,7 @@ constexpr int BN = 128;            // keys per tile
 constexpr int kWgThreads = 128;
 constexpr int kTmemCols = 512;
 constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 bytes: one swizzle panel
+constexpr int kMaxSlots = 8;            // K / V ring slots (barrier pairs in Ctl)
 constexpr float kLn2 = 0.6931471805599453f;
 // The running max used for exponentiation is only raised when a new score exceeds it by
 // more than this many powers of two; results are exact either way because l and O are
@@ -100,8 +108,9 @@ struct Cfg {
     static constexpr int kEpiCols = D / kHalves;           // output columns per warpgroup
     static constexpr int kPanels = D / 64;
     static constexpr int kTileBytes = BM * D * 2;
-    static constexpr int kSlots = (D == 64) ? 4 : 3;
-    static constexpr int kStageBytes = 2 * kPanelBytes / kHalves;  // per softmax warpgroup
+    static constexpr int kSlots = (D == 64) ? 7 : 3;  // K / V ring: one K or V tile per slot
+    static constexpr int kStagePanels = (D == 64) ? 1 : 2;   // epilogue staging panels per softmax warpgroup
+    static constexpr int kStageBytes = kStagePanels * kPanelBytes;
     static constexpr int kOffQ = 0;
     static constexpr int kOffSlots = kOffQ + 2 * kTileBytes;
     static constexpr int kOffStage = kOffSlots + kSlots * kTileBytes;
@@ -109,19 +118,25 @@ struct Cfg {
     static constexpr int kCtlBytes = 1024;
     static constexpr int kOffXchg = kOffCtl + kCtlBytes;    // (m, l) rows exchanged by the halves
     static constexpr int kXchgBytes = (kHalves == 2) ? 2 * 2 * 2 * 128 * 2 * 4 : 0;
-    static constexpr int kSmemBytes = kOffXchg + kXchgBytes + 1024;  // +1024 for base alignment
+    // sorted global indices for the per-row searches, when at most kSmemGlobals (d = 64 has
+    // the shared memory to spare)
+    static constexpr int kSmemGlobals = (D == 64) ? 2048 : 0;
+    static constexpr int kOffGidx = kOffXchg + kXchgBytes;
+    static constexpr int kSmemBytes = kOffGidx + kSmemGlobals * 4 + 1024;  // +1024 for base alignment
     static constexpr int kOCol = 256;
     static_assert(128 * kRegsControl + kSoftmaxWarps * 32 * kRegsSoftmax == kThreads * kRegsLaunch,
                   "register split must match the launch allocation");
     static_assert(kThreads * kRegsLaunch <= 65536, "launch allocation exceeds the register file");
     static_assert(kOCol + 2 * kHalves * D <= kTmemCols, "TMEM columns");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+    static_assert(kSlots <= kMaxSlots, "ring barriers");
 };
 
 struct Ctl {
     uint64_t q_full[2];
     uint64_t q_empty[2];
-    uint64_t kv_full[4];
-    uint64_t kv_empty[4];
+    uint64_t kv_full[kMaxSlots];
+    uint64_t kv_empty[kMaxSlots];
     uint64_t s_full[2][2];   // [query tile][half]: S columns of the half ready
     uint64_t p_full[2][2];   // [query tile][half]: P of the half written
     uint64_t o_full[2];
@@ -130,6 +145,8 @@ struct Ctl {
     uint32_t tmem_base;
     int abort_flag;
 };
+
+static_assert(sizeof(Ctl) <= 1024, "control block");
 
 struct Unit {
     bool grow;        // global-row unit
@@ -258,6 +275,9 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+#ifdef LCA_TRACE
+    unsigned int trace_i = 0;  // events recorded by this thread
+#endif
     volatile int* abort_flag = &ctl->abort_flag;
     const int n_units = p.n_grow_units + p.n_band_units;
     const uint64_t tmo = p.timeout_ns;
@@ -286,6 +306,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
         ptx::tmem_alloc(&ctl->tmem_base, kTmemCols);
         ptx::tmem_relinquish();
     }
+    int* sGidx = reinterpret_cast<int*>(smem + C::kOffGidx);
+    const bool gidx_in_smem = p.g_tiles > 0 && p.num_global <= C::kSmemGlobals;
+    if (gidx_in_smem)
+        for (int i = threadIdx.x; i < p.num_global; i += blockDim.x) sGidx[i] = __ldg(p.gidx + i);
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
@@ -330,12 +354,14 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                         const Tile t = tile_of(p, un, j);
                         for (int kv = 0; kv < 2; ++kv) {
                             const int slot = L % C::kSlots;
+                            LCA_TRACE_EVENT(trace::EV_TMA_SLOT_WAIT);
                             if (L >= C::kSlots &&
                                 !ptx::mbar_wait(&ctl->kv_empty[slot], ((L / C::kSlots) + 1) & 1, abort_flag, p.err,
                                                 LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
                                 ok = false;
                                 break;
                             }
+                            LCA_TRACE_EVENT(trace::EV_TMA_SLOT_FREE);
                             const CUtensorMap* m = t.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
                             int y = t.row0, z = un.bh;
                             if (t.global_key) {
@@ -452,12 +478,15 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     // holding that P.  The first half also waits for the accumulators to be free
                     // and for the V tile.
                     auto pv_half = [&](int h) -> bool {
+                        LCA_TRACE_EVENT(trace::EV_MMA_P_WAIT);
                         if (!W(&ctl->p_full[X][h], pc)) return false;
+                        LCA_TRACE_EVENT(trace::EV_MMA_P_READY);
                         if (h == 0) {
                             if (first && oc > 0 && !W(&ctl->o_free[X], oc - 1)) return false;
                             if (!W(&ctl->kv_full[pend_lv % C::kSlots], pend_lv / C::kSlots)) return false;
                         }
                         issue_pv(pend_lv % C::kSlots, pend_cols, first, h);
+                        LCA_TRACE_EVENT(trace::EV_MMA_PV_ISSUED);
                         return true;
                     };
                     auto pv_done = [&]() {
@@ -481,16 +510,21 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                                 if (!pv_ok) break;
                                 pv_done();
                             }
+                            LCA_TRACE_EVENT(trace::EV_MMA_K_WAIT);
                             if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
+                            LCA_TRACE_EVENT(trace::EV_MMA_K_READY);
                             if (mem) {
                                 issue_s(lk % C::kSlots, t.ncols, 0);
                                 ptx::mma_commit(&ctl->s_full[X][0]);
+                                LCA_TRACE_EVENT(trace::EV_MMA_S_ISSUED);
                             }
                         } else {
                             // Two halves (4-slot ring): K of this tile can land while the
                             // pending V is held, so each half runs its own chain, P*V of the
                             // pending tile then S of this one, as soon as its P is written.
+                            LCA_TRACE_EVENT(trace::EV_MMA_K_WAIT);
                             if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
+                            LCA_TRACE_EVENT(trace::EV_MMA_K_READY);
                             bool s_ok = true;
 #pragma unroll
                             for (int h = 0; h < H; ++h) {
@@ -500,6 +534,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                                 }
                                 issue_s(lk % C::kSlots, t.ncols, h);
                                 ptx::mma_commit(&ctl->s_full[X][h]);
+                                LCA_TRACE_EVENT(trace::EV_MMA_S_ISSUED);
                             }
                             if (!s_ok) break;
                             if (pend_lv >= 0) pv_done();
@@ -561,6 +596,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
 
         for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
             const Unit un = decode_unit(p, u);
+            LCA_TRACE_LANE0(trace::EV_UNIT_DECODED);
             const bool active_x = X ? un.active[1] : un.active[0];
             if (!active_x) continue;
             const int qrow_x = X ? un.qrow[1] : un.qrow[0];
@@ -576,28 +612,32 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                 jlo = qa - p.window > 0 ? qa - p.window : 0;
                 jhi = (qa + p.window < p.n_total - 1) ? qa + p.window : p.n_total - 1;
                 if (p.g_tiles > 0) {
+                    const int* gl = gidx_in_smem ? sGidx : p.gidx;
                     int a = 0, b = p.num_global;
                     while (a < b) {
                         const int mid = (a + b) >> 1;
-                        if (__ldg(p.gidx + mid) < qa - p.window) a = mid + 1; else b = mid;
+                        if (gl[mid] < qa - p.window) a = mid + 1; else b = mid;
                     }
                     g_lo = a;
                     b = p.num_global;
                     while (a < b) {
                         const int mid = (a + b) >> 1;
-                        if (__ldg(p.gidx + mid) <= qa + p.window) a = mid + 1; else b = mid;
+                        if (gl[mid] <= qa + p.window) a = mid + 1; else b = mid;
                     }
                     g_hi = a;
                 }
             }
+            LCA_TRACE_LANE0(trace::EV_UNIT_READY);
             float m = -INFINITY;  // reference max (log2 units)
             float l = 0.f;
             bool seen = false;    // a previous member tile of this unit was processed
             for (int j = 0; j < un.ntiles; ++j) {
                 const Tile t = tile_of(p, un, j);
                 if (!(X ? t.mem[1] : t.mem[0])) continue;
+                LCA_TRACE_LANE0(trace::EV_S_WAIT);
                 if (ok) ok = warp_wait(&ctl->s_full[X][H == 1 ? 0 : hh], sc & 1, abort_flag, p.err,
                                        LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+                LCA_TRACE_LANE0(trace::EV_S_READY);
                 ++sc;
                 const int col0 = t.row0 + KC * hh;  // key (band) or compact global row of column 0
                 const int ncols_h = t.ncols - KC * hh;
@@ -643,6 +683,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
 #pragma unroll
                         for (int c = 0; c < KC; ++c) s[c] = ((vis[c >> 5] >> (c & 31)) & 1u) ? s[c] : sent;
                     }
+                    LCA_TRACE_LANE0(trace::EV_S_LOADED);
                     float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
                     if (!neg_scale) {
 #pragma unroll
@@ -695,6 +736,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                     // Pairs of columns go through the packed fp32x2 pipe: one FMA for the
                     // exponent arguments, one add for the row sums and, for bf16, one
                     // subtract for the low parts.
+                    LCA_TRACE_LANE0(trace::EV_MAX_DONE);
                     const float neg_m = (m == -INFINITY) ? 0.f : -m;
                     const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
                     const uint64_t negm2 = ptx::f2_pack(neg_m, neg_m);
@@ -741,16 +783,20 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                         const uint64_t a = ptx::f2_add(acc0, acc1);
                         l += ptx::f2_lo(a) + ptx::f2_hi(a);
                     }
+                    LCA_TRACE_LANE0(trace::EV_EXP_DONE);
                     ptx::tmem_wait_st();
                 }
                 seen = true;
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&ctl->p_full[X][H == 1 ? 0 : hh]);
+                LCA_TRACE_LANE0(trace::EV_P_ARRIVED);
             }
 
             // ---- epilogue: merge the halves, O / l -> fp32 rows via staging + TMA store
+            LCA_TRACE_LANE0(trace::EV_EPI_WAIT);
             if (ok) ok = warp_wait(&ctl->o_full[X], oc & 1, abort_flag, p.err, LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+            LCA_TRACE_LANE0(trace::EV_EPI_READY);
             if (ok) ptx::tc_fence_after();
             float M = m, Lsum = l, w_own = 1.f, w_oth = 0.f;
             if constexpr (H == 2) {
@@ -765,6 +811,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                 w_oth = (mo == -INFINITY) ? 0.f : ptx::ex2(mo - M);
                 Lsum = l * w_own + lo2 * w_oth;
             }
+            LCA_TRACE_LANE0(trace::EV_EPI_MERGED);
             ++oc;
             // staging from this warpgroup's previous unit must have been read by its TMA stores
             if (r == 0) ptx::tma_store_wait_read<0>();
@@ -778,9 +825,9 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
 #pragma unroll
             for (int c = 0; c < C::kEpiCols / 32; ++c) {
                 const int ocol = hh * C::kEpiCols + c * 32;  // output column of this chunk
-                uint8_t* panel = stage + (c & 1) * kPanelBytes;
-                if (c >= 2) {
-                    if (r == 0) ptx::tma_store_wait_read<1>();
+                uint8_t* panel = stage + (c % C::kStagePanels) * kPanelBytes;
+                if (c >= C::kStagePanels) {  // the store issued kStagePanels chunks ago has read this panel
+                    if (r == 0) ptx::tma_store_wait_read<C::kStagePanels - 1>();
                     ptx::named_bar_sync(wg_bar, kWgThreads);
                 }
                 if (ok) {
@@ -814,6 +861,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&ctl->o_free[X]);
+            LCA_TRACE_LANE0(trace::EV_EPI_DONE);
             if (ok && hh == 0) {
                 const float lse = (((M == -INFINITY) ? 0.f : M) + __log2f(Lsum)) * kLn2;
                 if (un.grow) {
@@ -827,6 +875,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
         if (r == 0) ptx::tma_store_wait_all();
     }
 
+    LCA_TRACE_FLUSH();
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
@@ -1091,6 +1140,20 @@ int main_smem_bytes(int head_dim, bool bf16) {
     if (head_dim == 64) return bf16 ? Cfg<64, true>::kSmemBytes : Cfg<64, false>::kSmemBytes;
     return bf16 ? Cfg<128, true>::kSmemBytes : Cfg<128, false>::kSmemBytes;
 }
+
+#ifdef LCA_TRACE
+cudaError_t trace_read(void* host, size_t bytes) {
+    const size_t need = sizeof(trace::g_trace) + sizeof(trace::g_trace_count);
+    if (bytes < need) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemcpyFromSymbol(host, trace::g_trace, sizeof(trace::g_trace));
+    if (e == cudaSuccess)
+        e = cudaMemcpyFromSymbol(static_cast<uint8_t*>(host) + sizeof(trace::g_trace), trace::g_trace_count,
+                                 sizeof(trace::g_trace_count));
+    static const unsigned int zeros[trace::kTraceCtas][trace::kTraceWarps] = {};
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(trace::g_trace_count, zeros, sizeof(zeros));
+    return e;
+}
+#endif
 
 cudaError_t error_word_address(int** out) {
     void* p = nullptr;

@@ -159,4 +159,9 @@ int report_error(int status, const char* fmt, ...);
 // Device address (on the current device) of the device-side error word.
 cudaError_t error_word_address(int** out);
 
+#ifdef LCA_TRACE
+// Copy the main kernel's event trace (trace.cuh) to `host` and clear its counters.
+cudaError_t trace_read(void* host, size_t bytes);
+#endif
+
 }  // namespace lca
