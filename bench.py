@@ -426,6 +426,10 @@ def run_sequence(args):
     else:
         flops_max = flops_rank
     tokens = w.tokens()
+    # DRAM bytes of one whole-sequence launch (ncu, profiles/traffic.json), split evenly over
+    # the shards (the per-shard band work is uniform)
+    full_traffic = load_traffic(w.name)
+    shard_traffic = full_traffic / world if full_traffic is not None else None
     peak_tf, peak_gbs, peak_src = load_peaks()
     achieved_tf = flops_max / (main_ms * 1e-3) / 1e12
     if rank == 0:
@@ -445,7 +449,7 @@ def run_sequence(args):
                        "exchange": plan.exchange,
                        "l2": "inputs larger than L2 (shard Q/K/V/O resident: %.0f MB)" % (shard_io / 1e6)},
             "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved_tf / peak_tf, "traffic": None, "kernel": "lca_swa_main",
+                         "frac": achieved_tf / peak_tf, "traffic": shard_traffic, "kernel": "lca_swa_main",
                          "kernel_ms": main_ms, "peak_source": peak_src,
                          "note": "largest shard's useful FLOPs / max-over-ranks main-kernel time"},
             "cpu_baseline": cpu,
