@@ -215,7 +215,15 @@ struct Layout {
     size_t off_gidx = 0, off_globals = 0, off_po = 0, off_plse = 0;
     size_t off_send = 0, off_recv = 0, halo_block = 0;  // halo_block: one side, [2][bh][halo][d]
     size_t off_rowpart = 0, rowpart_bytes = 0, off_rowpart_all = 0;  // rowpart_all: two buffers
-    size_t total = 0;
+    size_t total = 0;  // bytes the forward needs
+    // Optional suffix for bf16 inputs (single-device forward only): an fp16 copy of V
+    // [bh][n][d] and of the compact global V rows [G][bh][d], and a word that says whether
+    // every value converted without loss that matters (lca_convert_v16).  When it did, P*V
+    // runs once per tile in fp16 instead of twice (bf16 P split into hi + lo).
+    // total_fast >= total; a workspace of total_fast bytes enables it.
+    int v16_blocks = 0;
+    size_t off_v16 = 0, off_vg16 = 0, off_v16bad = 0;
+    size_t total_fast = 0;
 };
 
 // Split of the keys of the global-row units (all n keys, or the shard's own).  A unit
@@ -283,6 +291,19 @@ Layout make_layout(const Problem& P) {
         off = align_up(off + (size_t)parts * bh * G * 4, kAlign);
     }
     L.total = off;
+    L.total_fast = off;
+    if (!P.sharded && P.dtype == LCA_DTYPE_BF16 && bh > 0 && P.n > 0) {
+        L.v16_blocks = (int)((P.n + lca::kTileRows - 1) / lca::kTileRows);
+        L.off_v16 = off;
+        off = align_up(off + (size_t)bh * P.n * d * 2, kAlign);
+        if (glob) {
+            L.off_vg16 = off;
+            off = align_up(off + (size_t)G * bh * d * 2, kAlign);
+        }
+        L.off_v16bad = off;
+        off = align_up(off + sizeof(int), kAlign);
+        L.total_fast = off;
+    }
     return L;
 }
 
@@ -307,11 +328,11 @@ int encode_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* bas
 // whole compact row, box 64 columns x 1 head x 128 rows (lands in shared memory exactly
 // like a 64 x 128 box of a [bh][n][d] tensor).
 int encode_compact(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d, uint64_t bh, uint64_t G,
-                   const char* name) {
+                   const char* name, uint64_t planes_per_row = 3) {
     EncodeTiledFn enc = get_encode_fn();
     if (enc == nullptr) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
     cuuint64_t dims[3] = {d, bh, G};
-    cuuint64_t strides[2] = {d * 2, 3 * bh * d * 2};
+    cuuint64_t strides[2] = {d * 2, planes_per_row * bh * d * 2};
     cuuint32_t box[3] = {64, 1, (cuuint32_t)lca::kTileRows};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -378,7 +399,7 @@ int enqueue_gather(const Problem& P, const Layout& L, const void* q, const void*
 
 // The main kernel over band and global-row units.
 int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, const void* q, const void* k,
-                 const void* v, float* out, float* lse, uint8_t* ws, cudaStream_t stream) {
+                 const void* v, float* out, float* lse, uint8_t* ws, cudaStream_t stream, bool v16 = false) {
     const bool bf16 = P.dtype == LCA_DTYPE_BF16;
     const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int n = (int)P.n;
@@ -455,6 +476,17 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
         tm.vg = tm.v;
         tm.po = tm.o;
     }
+    tm.v16 = tm.v;
+    tm.vg16 = tm.vg;
+    if (v16) {
+        const CUtensorMapDataType f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        if ((st = encode_3d(&tm.v16, f16, 2, ws + L.off_v16, d, n, bh, 64, "v_fp16")) != LCA_OK) return st;
+        if (P.G > 0 &&
+            (st = encode_compact(&tm.vg16, f16, ws + L.off_vg16, d, bh, (uint64_t)P.G, "v_global_fp16", 1)) !=
+                LCA_OK)
+            return st;
+        p.v16_bad = reinterpret_cast<const int*>(ws + L.off_v16bad);
+    }
 
     p.q_pairs = (p.q_tiles + 1) / 2;
     const long long units = (long long)p.n_grow_units + (long long)P.bh * p.q_pairs;
@@ -465,7 +497,7 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     cudaError_t e;
     if (timed && (e = cudaEventRecord(g_ev_before_main, stream)) != cudaSuccess)
         return fail_cuda(e, "timing event record");
-    e = lca::launch_main(d, bf16, tm, p, grid, stream);
+    e = lca::launch_main(d, bf16, tm, p, grid, stream, v16);
     if (e != cudaSuccess) return fail_cuda(e, "main kernel launch");
     if (timed && (e = cudaEventRecord(g_ev_after_main, stream)) != cudaSuccess)
         return fail_cuda(e, "timing event record");
@@ -550,8 +582,11 @@ int lca_normalize_global_tokens(const int64_t* tokens, int64_t count, int64_t se
     return LCA_OK;
 }
 
-int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
-                           int64_t num_unique_global, int dtype, size_t* out_bytes) {
+}  // extern "C"
+
+namespace lca {
+int workspace_bytes(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
+                    int64_t num_unique_global, int dtype, bool with_fp16_v, size_t* out_bytes) {
     if (out_bytes == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "out_bytes is NULL");
     if (batch < 0 || heads < 0 || seq_len < 0 || num_unique_global < 0)
         return fail(LCA_ERR_INVALID_ARGUMENT, "negative size");
@@ -565,8 +600,18 @@ int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_
     P.window = std::min(window_size, seq_len);
     P.G = std::min(num_unique_global, seq_len);
     P.dtype = dtype;
-    *out_bytes = make_layout(P).total;
+    const Layout L = make_layout(P);
+    *out_bytes = with_fp16_v ? L.total_fast : L.total;
     return LCA_OK;
+}
+}  // namespace lca
+
+extern "C" {
+
+int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
+                           int64_t num_unique_global, int dtype, size_t* out_bytes) {
+    return lca::workspace_bytes(batch, heads, seq_len, head_dim, window_size, num_unique_global, dtype, true,
+                                out_bytes);
 }
 
 int lca_swa_forward(const void* q, const void* k, const void* v, float* out, float* lse, int dtype,
@@ -587,9 +632,31 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
     if ((st = check_workspace(L, workspace, workspace_bytes)) != LCA_OK) return st;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    // 1. gather the global rows, 2. band + global-row units, 3. merge the global-row splits
+    const bool v16 = L.total_fast > L.total && workspace_bytes >= L.total_fast;
+    // 1. gather the global rows, (2. fp16 copy of V), 3. band + global-row units, 4. merge
+    //    the global-row splits
     if ((st = enqueue_gather(P, L, q, k, v, ws, stream)) != LCA_OK) return st;
-    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream)) != LCA_OK) return st;
+    if (v16) {
+        lca::ConvertParams cv;
+        memset(&cv, 0, sizeof(cv));
+        cv.bh = (int)P.bh;
+        cv.n = (int)P.n;
+        cv.blocks = L.v16_blocks;
+        cv.num_global = (int)P.G;
+        cv.g_tiles = L.g_tiles;
+        cv.v = static_cast<const uint16_t*>(v);
+        cv.v16 = reinterpret_cast<uint16_t*>(ws + L.off_v16);
+        cv.any_bad = reinterpret_cast<int*>(ws + L.off_v16bad);
+        if (P.G > 0) {
+            // compact rows [G][3][bh][d]: the v plane of row g starts 2 * bh * d elements in
+            cv.vg = reinterpret_cast<const uint16_t*>(ws + L.off_globals) + 2 * (size_t)P.bh * P.d;
+            cv.vg16 = reinterpret_cast<uint16_t*>(ws + L.off_vg16);
+        }
+        cudaError_t e = cudaMemsetAsync(cv.any_bad, 0, sizeof(int), stream);
+        if (e == cudaSuccess) e = lca::launch_convert_v16((int)P.d, cv, stream);
+        if (e != cudaSuccess) return fail_cuda(e, "fp16 V copy launch");
+    }
+    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16)) != LCA_OK) return st;
     return enqueue_combine_splits(P, L, out, lse, ws, stream);
 }
 

@@ -53,8 +53,8 @@ extern "C" int lca_swa_forward_noalloc(const void* q, const void* k, const void*
     int64_t G = 0;
     int st = lca_normalize_global_tokens(global_tokens, num_global_tokens, seq_len, norm.data(), &G);
     if (st != LCA_OK) return st;
-    size_t need = 0;
-    st = lca_swa_workspace_size(batch, heads, seq_len, head_dim, window_size, G, dtype, &need);
+    size_t need = 0;  // the forward's minimum (it adds the optional fp16 copy of V only if that fits too)
+    st = lca::workspace_bytes(batch, heads, seq_len, head_dim, window_size, G, dtype, false, &need);
     if (st != LCA_OK) return st;
     if (need > (size_t)LCA_NOALLOC_SCRATCH_BYTES)
         return lca::report_error(LCA_ERR_UNSUPPORTED,

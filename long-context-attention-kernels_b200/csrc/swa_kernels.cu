@@ -90,10 +90,12 @@ constexpr float kRescaleThreshold = 8.0f;
 
 // For bf16 inputs P is split as P_hi + P_lo (P_hi = rn_bf16(p), P_lo = rn_bf16(p - P_hi))
 // and P*V is issued twice into the same accumulator: a single bf16 P carries ~1.5e-3
-// relative L2 error into O, the split ~2^-16.  fp16 P is accurate enough on its own.
-template <int D, bool BF16>
+// relative L2 error into O, the split ~2^-16.  fp16 P is accurate enough on its own, so the
+// V16 variant (bf16 inputs whose V has an fp16 copy in the workspace that holds every value
+// without loss that matters) writes fp16 P and runs P*V once, from the copy.
+template <int D, bool BF16, bool V16 = false>
 struct Cfg {
-    static constexpr bool kSplitP = BF16;
+    static constexpr bool kSplitP = BF16 && !V16;
     static constexpr int kHalves = (D == 64) ? 2 : 1;      // softmax warpgroups per query tile
     static constexpr int kCols = BN / kHalves;             // S columns per softmax thread
     static constexpr int kSoftmaxWarps = 8 * kHalves;
@@ -256,15 +258,22 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk16) {
     return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
 }
 
-template <int D, bool BF16>
-__global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
+template <int D, bool BF16, bool V16>
+__global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
     lca_swa_main(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kh,
                  const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_qg,
                  const __grid_constant__ CUtensorMap tm_kg, const __grid_constant__ CUtensorMap tm_vg,
                  const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_po,
+                 const __grid_constant__ CUtensorMap tm_v16, const __grid_constant__ CUtensorMap tm_vg16,
                  const MainParams p) {
-    using C = Cfg<D, BF16>;
+    using C = Cfg<D, BF16, V16>;
+    if (p.v16_bad != nullptr) {
+        // bf16 with an fp16 copy of V: both variants are launched and one does the work --
+        // this one (V16) if every value of V fitted fp16, else the split one
+        const bool bad = *reinterpret_cast<const volatile int*>(p.v16_bad) != 0;
+        if (V16 ? bad : !bad) return;
+    }
     constexpr int H = C::kHalves;
     constexpr int KC = C::kCols;
     extern __shared__ uint8_t smem_raw[];
@@ -362,7 +371,8 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                                 break;
                             }
                             LCA_TRACE_EVENT(trace::EV_TMA_SLOT_FREE);
-                            const CUtensorMap* m = t.global_key ? (kv ? &tm_vg : &tm_kg) : (kv ? &tm_v : &tm_k);
+                            const CUtensorMap* m = t.global_key ? (kv ? (V16 ? &tm_vg16 : &tm_vg) : &tm_kg)
+                                                                : (kv ? (V16 ? &tm_v16 : &tm_v) : &tm_k);
                             int y = t.row0, z = un.bh;
                             if (t.global_key) {
                                 y = un.bh;
@@ -413,7 +423,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                 const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
                 const uint32_t qlo = ptx::smem_desc_sw128_lo(ptx::smem_u32(sQ) + X * C::kTileBytes, 0);
                 const uint32_t idesc_s_full = ptx::idesc_f16(BF16, BM, KC, false);
-                const uint32_t idesc_pv = ptx::idesc_f16(BF16, BM, D, true);
+                const uint32_t idesc_pv = ptx::idesc_f16(BF16 && !V16, BM, D, true);  // P and V types
                 const uint32_t sx = tmem + X * 128;
                 int L = 0, qn = 0, pc = 0, oc = 0;
                 bool ok = true;
@@ -750,7 +760,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
 #pragma unroll
                             for (int e = 0; e < 16; ++e) z[e] = 0u;
                             ptx::tmem_st16u(t_lane + s_col + c0, z);
-                            if (BF16) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
+                            if (C::kSplitP) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
                         } else {
                             const float* v = s + c0;
 #pragma unroll
@@ -764,7 +774,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                                     const float p0 = ptx::ex2(ptx::f2_lo(x)), p1 = ptx::ex2(ptx::f2_hi(x));
                                     const uint64_t pp = ptx::f2_pack(p0, p1);
                                     if (e & 1) acc1 = ptx::f2_add(acc1, pp); else acc0 = ptx::f2_add(acc0, pp);
-                                    if (BF16) {
+                                    if (C::kSplitP) {
                                         w[e] = ptx::pack_bf16x2(p0, p1);
                                         const uint64_t rest = ptx::f2_sub(
                                             pp, ptx::f2_pack(__uint_as_float(w[e] << 16),
@@ -775,7 +785,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16>::kThreads, 1)
                                     }
                                 }
                                 ptx::tmem_st8u(t_lane + s_col + c0 + g8 * 8, w);
-                                if (BF16) ptx::tmem_st8u(t_lane + s_col + c0 + 16 + g8 * 8, wl);
+                                if (C::kSplitP) ptx::tmem_st8u(t_lane + s_col + c0 + 16 + g8 * 8, wl);
                             }
                         }
                     }
@@ -908,6 +918,67 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
         const size_t dst_off = (((size_t)g * 3 + which) * gp.bh + bh) * D;
         *reinterpret_cast<uint4*>(gp.compact + dst_off + cc * 8) =
             *reinterpret_cast<const uint4*>(src + src_off + cc * 8);
+    }
+}
+
+// ------------------------------------------------------------------------ fp16 copy of V
+
+// One block per 128-row block of one head: blocks [0, bh * blocks) cover V, the rest the
+// compact global V rows (g_tiles * bh of them).  Each thread converts 16-byte chunks (8
+// values); a block whose values the copy cannot stand in for sets *any_bad (see
+// ConvertParams).
+template <int D>
+__global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
+    constexpr int kChunksPerRow = D / 8;
+    const long long blk = blockIdx.x;
+    const long long main_blocks = (long long)cp.bh * cp.blocks;
+    const bool compact = blk >= main_blocks;
+    int b, r0, rows;
+    if (!compact) {
+        b = (int)(blk / cp.blocks);
+        r0 = (int)(blk % cp.blocks) * 128;
+        rows = min(128, cp.n - r0);
+    } else {
+        const long long t = blk - main_blocks;
+        const int gt = (int)(t / cp.bh);
+        b = (int)(t % cp.bh);
+        r0 = gt * 128;
+        rows = min(128, cp.num_global - r0);
+    }
+    bool bad = false, inexact = false;
+    float amax = 0.f;
+    for (int c = threadIdx.x; c < rows * kChunksPerRow; c += blockDim.x) {
+        const int r = r0 + c / kChunksPerRow;
+        const int col = (c % kChunksPerRow) * 8;
+        const size_t src = compact ? ((size_t)r * 3 * cp.bh + b) * D + col : ((size_t)b * cp.n + r) * D + col;
+        const size_t dst = compact ? ((size_t)r * cp.bh + b) * D + col : src;
+        const uint4 in = *reinterpret_cast<const uint4*>((compact ? cp.vg : cp.v) + src);
+        const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float f0 = __uint_as_float(w[i] << 16), f1 = __uint_as_float(w[i] & 0xFFFF0000u);
+            const __half2 h = __floats2half2_rn(f0, f1);
+            const float2 back = __half22float2(h);
+            // bf16 values in the fp16 normal range convert exactly; below 2^-14 they round to
+            // fp16 subnormals (error <= 2^-25); beyond 65504 (or NaN) they do not fit
+            if (back.x != f0) (fabsf(f0) < 6.103515625e-05f ? inexact : bad) = true;
+            if (back.y != f1) (fabsf(f1) < 6.103515625e-05f ? inexact : bad) = true;
+            amax = fmaxf(amax, fmaxf(fabsf(f0), fabsf(f1)));
+            o[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>((compact ? cp.vg16 : cp.v16) + dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    __shared__ float s_max[8];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = amax;
+    const bool blk_bad = __syncthreads_or(bad);
+    const bool blk_inexact = __syncthreads_or(inexact);
+    if (threadIdx.x == 0) {
+        float m = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, s_max[i]);
+        if (blk_bad || (blk_inexact && m < 0.0625f)) *cp.any_bad = 1;
     }
 }
 
@@ -1074,22 +1145,28 @@ __global__ void __launch_bounds__(256) lca_peer_put(PeerPutParams pp) {
 
 // ------------------------------------------------------------------------ launchers
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool V16 = false>
 static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int grid, cudaStream_t stream) {
-    auto kern = lca_swa_main<D, BF16>;
-    const int smem = Cfg<D, BF16>::kSmemBytes;
+    auto kern = lca_swa_main<D, BF16, V16>;
+    const int smem = Cfg<D, BF16, V16>::kSmemBytes;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, Cfg<D, BF16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kh, tm.vh, tm.qg, tm.kg, tm.vg, tm.o,
-                                                         tm.po, p);
+    kern<<<grid, Cfg<D, BF16, V16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kh, tm.vh, tm.qg, tm.kg, tm.vg,
+                                                              tm.o, tm.po, tm.v16, tm.vg16, p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_main(int head_dim, bool bf16, const TensorMaps& tm, const MainParams& p, int grid,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool v16) {
+    if (head_dim != 64 && head_dim != 128) return cudaErrorInvalidValue;
+    if (bf16 && v16) {
+        // both variants; each reads p.v16_bad first and one returns at once
+        cudaError_t e = head_dim == 64 ? launch_main_t<64, true, true>(tm, p, grid, stream)
+                                       : launch_main_t<128, true, true>(tm, p, grid, stream);
+        if (e != cudaSuccess) return e;
+    }
     if (head_dim == 64) return bf16 ? launch_main_t<64, true>(tm, p, grid, stream) : launch_main_t<64, false>(tm, p, grid, stream);
-    if (head_dim == 128) return bf16 ? launch_main_t<128, true>(tm, p, grid, stream) : launch_main_t<128, false>(tm, p, grid, stream);
-    return cudaErrorInvalidValue;
+    return bf16 ? launch_main_t<128, true>(tm, p, grid, stream) : launch_main_t<128, false>(tm, p, grid, stream);
 }
 
 cudaError_t launch_gather(int head_dim, const void* q, const void* k, const void* v, const GatherParams& gp,
@@ -1118,6 +1195,19 @@ cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t s
         lca_combine_global_rows<64><<<grid, 128, 0, stream>>>(cp);
     else if (head_dim == 128)
         lca_combine_global_rows<128><<<grid, 128, 0, stream>>>(cp);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_convert_v16(int head_dim, const ConvertParams& cp, cudaStream_t stream) {
+    const long long blocks = (long long)cp.bh * cp.blocks + (cp.num_global > 0 ? (long long)cp.g_tiles * cp.bh : 0);
+    if (blocks <= 0) return cudaSuccess;
+    if (blocks > INT_MAX) return cudaErrorInvalidValue;
+    if (head_dim == 64)
+        lca_convert_v16<64><<<(unsigned)blocks, 256, 0, stream>>>(cp);
+    else if (head_dim == 128)
+        lca_convert_v16<128><<<(unsigned)blocks, 256, 0, stream>>>(cp);
     else
         return cudaErrorInvalidValue;
     return cudaGetLastError();

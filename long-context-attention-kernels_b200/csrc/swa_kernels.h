@@ -41,6 +41,8 @@ struct TensorMaps {
                              // (rows >= G read as zeros)
     CUtensorMap o;           // output [bh][n][d] fp32, box 32 x 128 rows, 128B swizzle
     CUtensorMap po;          // global-row partial outputs [2*splits*bh][G][d] fp32
+    CUtensorMap v16, vg16;   // bf16 inputs: fp16 copies of V [bh][n][d] and of the compact global V
+                             // rows [G][bh][d] (maps {d, bh, G}); the bf16 maps when unused
 };
 
 // Key and query indices below are absolute positions in the full sequence unless named
@@ -72,6 +74,10 @@ struct MainParams {
     const int* gidx;  // [G] sorted absolute global indices
     float* lse;       // [bh][n] natural-log LSE, or nullptr
     float* part_lse;  // [2 * n_splits][bh][G]
+    // bf16 inputs with an fp16 copy of V (else nullptr): 0 when every value of V converted
+    // to fp16 without loss that matters (lca_convert_v16), else nonzero.  Both main-kernel
+    // variants are launched; the one that does not match returns at once.
+    const int* v16_bad;
     int* err;         // device error word (first error wins)
     unsigned long long timeout_ns;  // per-wait budget
 };
@@ -124,6 +130,28 @@ struct CombineParams {
     size_t parity_floats;
 };
 
+// fp16 copy of bf16 V in 128-row blocks: v16[b][r][:] = fp16(v[b][r][:]) for r < n, and
+// the same for the compact global V rows (`vg`, row g of head b at vg + (g * 3 * bh + b) *
+// d) into vg16 [G][bh][d].  A block passes when every value converts without overflow and
+// either exactly or, for magnitudes below 2^-14 (fp16 subnormals, absolute error at most
+// 2^-25), in a block whose largest magnitude is at least 2^-4; a block that fails sets
+// *any_bad (which the host zeroes beforehand).
+struct ConvertParams {
+    int bh, n, blocks;
+    int num_global, g_tiles;
+    const uint16_t* v;
+    uint16_t* v16;
+    const uint16_t* vg;
+    uint16_t* vg16;
+    int* any_bad;
+};
+cudaError_t launch_convert_v16(int head_dim, const ConvertParams& cp, cudaStream_t stream);
+
+// Workspace bytes of lca_swa_forward: the minimum, or with the optional fp16 copy of V
+// (what lca_swa_workspace_size reports).
+int workspace_bytes(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
+                    int64_t num_unique_global, int dtype, bool with_fp16_v, size_t* out_bytes);
+
 // Copies contiguous 16-byte-aligned ranges into other ranks' workspaces (or this rank's),
 // then bumps one counter on every other rank and, in block 0, waits until this rank's
 // counters from every other rank reach (epoch + 1) * gridDim.x.  The destination of job
@@ -145,8 +173,11 @@ struct PeerPutParams {
 
 cudaError_t launch_peer_put(const PeerPutParams& pp, int blocks, cudaStream_t stream);
 
+// Main kernel.  `v16`: bf16 inputs with the fp16 copy of V in tm.v16 / tm.vg16 -- launches
+// the variant that reads it (fp16 P, one P*V per tile) and the one that splits bf16 P;
+// p.v16_bad selects which of the two runs.
 cudaError_t launch_main(int head_dim, bool bf16, const TensorMaps& tm, const MainParams& p, int grid,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool v16 = false);
 cudaError_t launch_gather(int head_dim, const void* q, const void* k, const void* v, const GatherParams& gp,
                           int bh, cudaStream_t stream);
 cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t stream);

@@ -61,13 +61,18 @@ def test_normalize_out_of_range(tokens):
 
 def test_workspace_size():
     cabi = _native.cabi()
-    st, b0 = cabi.workspace_size(1, 16, 65536, 64, 256, 0, cabi.DTYPE_BF16)
+    st, b0 = cabi.workspace_size(1, 16, 65536, 64, 256, 0, cabi.DTYPE_F16)
     assert st == cabi.OK and b0 == 0
-    st, b1 = cabi.workspace_size(1, 16, 65536, 64, 256, 65, cabi.DTYPE_BF16)
+    # bf16: the recommended size includes the fp16 copy of V (16 heads x 65536 x 64 x 2B)
+    st, b0 = cabi.workspace_size(1, 16, 65536, 64, 256, 0, cabi.DTYPE_BF16)
+    assert st == cabi.OK and b0 >= 16 * 65536 * 64 * 2
+    st, b1 = cabi.workspace_size(1, 16, 65536, 64, 256, 65, cabi.DTYPE_F16)
     assert st == cabi.OK
     # compact Q/K/V global rows (16 heads x 65 rows x 64 x 2B each) + at least two split partials
     assert b1 >= 3 * 16 * 65 * 64 * 2 + 2 * 16 * 65 * 64 * 4
     assert b1 % 1024 == 0
+    st, b2 = cabi.workspace_size(1, 16, 65536, 64, 256, 65, cabi.DTYPE_BF16)
+    assert st == cabi.OK and b2 >= b1 + 16 * 65536 * 64 * 2 + 65 * 16 * 64 * 2 and b2 % 1024 == 0
     st, _ = cabi.workspace_size(1, 16, 65536, 96, 256, 65, cabi.DTYPE_BF16)
     assert st == cabi.ERR_UNSUPPORTED
 
