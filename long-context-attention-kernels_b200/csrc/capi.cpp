@@ -216,13 +216,15 @@ struct Layout {
     size_t off_send = 0, off_recv = 0, halo_block = 0;  // halo_block: one side, [2][bh][halo][d]
     size_t off_rowpart = 0, rowpart_bytes = 0, off_rowpart_all = 0;  // rowpart_all: two buffers
     size_t total = 0;  // bytes the forward needs
-    // Optional suffix for bf16 inputs (single-device forward only): an fp16 copy of V
-    // [bh][n][d] and of the compact global V rows [G][bh][d], and a word that says whether
-    // every value converted without loss that matters (lca_convert_v16).  When it did, P*V
-    // runs once per tile in fp16 instead of twice (bf16 P split into hi + lo).
-    // total_fast >= total; a workspace of total_fast bytes enables it.
-    int v16_blocks = 0;
-    size_t off_v16 = 0, off_vg16 = 0, off_v16bad = 0;
+    // Optional suffix for bf16 inputs: an fp16 copy of V [bh][n][d], of the compact global V
+    // rows [G][bh][d] and, for a sequence shard, of the received halo blocks (laid out like
+    // the receive region, V planes filled), and a word that says whether some value did not
+    // convert without loss that matters (lca_convert_v16).  When none failed, P*V runs once
+    // per tile in fp16 instead of twice (bf16 P split into hi + lo).  The suffix follows
+    // every other region (for a shard: after this rank's own regions, so the exchanged
+    // regions keep their offsets).  total_fast >= total; a workspace of total_fast bytes
+    // enables it.
+    size_t off_v16 = 0, off_vg16 = 0, off_vh16 = 0, off_v16bad = 0;
     size_t total_fast = 0;
 };
 
@@ -292,13 +294,16 @@ Layout make_layout(const Problem& P) {
     }
     L.total = off;
     L.total_fast = off;
-    if (!P.sharded && P.dtype == LCA_DTYPE_BF16 && bh > 0 && P.n > 0) {
-        L.v16_blocks = (int)((P.n + lca::kTileRows - 1) / lca::kTileRows);
+    if (P.dtype == LCA_DTYPE_BF16 && bh > 0 && P.n > 0) {
         L.off_v16 = off;
         off = align_up(off + (size_t)bh * P.n * d * 2, kAlign);
         if (glob) {
             L.off_vg16 = off;
             off = align_up(off + (size_t)G * bh * d * 2, kAlign);
+        }
+        if (L.halo_block > 0) {
+            L.off_vh16 = off;
+            off = align_up(off + 2 * L.halo_block, kAlign);
         }
         L.off_v16bad = off;
         off = align_up(off + sizeof(int), kAlign);
@@ -398,6 +403,46 @@ int enqueue_gather(const Problem& P, const Layout& L, const void* q, const void*
 }
 
 // The main kernel over band and global-row units.
+// fp16 copy of V (the optional workspace suffix): this rank's V rows, the compact global V
+// rows (complete once gathered, and for a shard once exchanged) and the received halos.
+int enqueue_convert_v16(const Problem& P, const Layout& L, const void* v, uint8_t* ws, cudaStream_t stream) {
+    lca::ConvertParams cv;
+    memset(&cv, 0, sizeof(cv));
+    const long long d = P.d, bh = P.bh;
+    auto add = [&](const uint16_t* src, uint16_t* dst, long long planes, long long rows, long long src_plane,
+                   long long src_row, long long dst_plane, long long dst_row) {
+        lca::ConvertSegment& g = cv.seg[cv.n_segments++];
+        g.src = src;
+        g.dst = dst;
+        g.planes = (int)planes;
+        g.rows = (int)rows;
+        g.src_plane = src_plane;
+        g.src_row = src_row;
+        g.dst_plane = dst_plane;
+        g.dst_row = dst_row;
+    };
+    add(static_cast<const uint16_t*>(v), reinterpret_cast<uint16_t*>(ws + L.off_v16), bh, P.n, P.n * d, d, P.n * d, d);
+    if (P.G > 0) {
+        // compact rows [G][3][bh][d]: the v plane of row g starts 2 * bh * d elements in
+        const uint16_t* vg = reinterpret_cast<const uint16_t*>(ws + L.off_globals) + 2 * bh * d;
+        add(vg, reinterpret_cast<uint16_t*>(ws + L.off_vg16), bh, P.G, d, 3 * bh * d, d, bh * d);
+    }
+    if (L.halo_block > 0) {
+        // receive blocks [2 sides][2 (k, v)][bh][halo][d]: the V planes of side s
+        const long long halo = P.halo(), plane = halo * d;
+        for (int side = 0; side < 2; ++side) {
+            const size_t off = ((size_t)(2 * side + 1) * bh) * plane * 2;
+            add(reinterpret_cast<const uint16_t*>(ws + L.off_recv + off), reinterpret_cast<uint16_t*>(ws + L.off_vh16 + off),
+                bh, halo, plane, d, plane, d);
+        }
+    }
+    cv.any_bad = reinterpret_cast<int*>(ws + L.off_v16bad);
+    cudaError_t e = cudaMemsetAsync(cv.any_bad, 0, sizeof(int), stream);
+    if (e == cudaSuccess) e = lca::launch_convert_v16((int)P.d, cv, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "fp16 V copy launch");
+    return LCA_OK;
+}
+
 int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, const void* q, const void* k,
                  const void* v, float* out, float* lse, uint8_t* ws, cudaStream_t stream, bool v16 = false) {
     const bool bf16 = P.dtype == LCA_DTYPE_BF16;
@@ -478,7 +523,14 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     }
     tm.v16 = tm.v;
     tm.vg16 = tm.vg;
+    tm.vh16 = tm.vh;
     if (v16) {
+        if (p.halo > 0) {
+            const size_t plane = (size_t)p.halo * d * 2;
+            if ((st = encode_3d(&tm.vh16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws + L.off_vh16 + bh * plane, d, p.halo,
+                                3 * bh, 64, "v_halo_fp16")) != LCA_OK)
+                return st;
+        }
         const CUtensorMapDataType f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
         if ((st = encode_3d(&tm.v16, f16, 2, ws + L.off_v16, d, n, bh, 64, "v_fp16")) != LCA_OK) return st;
         if (P.G > 0 &&
@@ -636,26 +688,7 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
     // 1. gather the global rows, (2. fp16 copy of V), 3. band + global-row units, 4. merge
     //    the global-row splits
     if ((st = enqueue_gather(P, L, q, k, v, ws, stream)) != LCA_OK) return st;
-    if (v16) {
-        lca::ConvertParams cv;
-        memset(&cv, 0, sizeof(cv));
-        cv.bh = (int)P.bh;
-        cv.n = (int)P.n;
-        cv.blocks = L.v16_blocks;
-        cv.num_global = (int)P.G;
-        cv.g_tiles = L.g_tiles;
-        cv.v = static_cast<const uint16_t*>(v);
-        cv.v16 = reinterpret_cast<uint16_t*>(ws + L.off_v16);
-        cv.any_bad = reinterpret_cast<int*>(ws + L.off_v16bad);
-        if (P.G > 0) {
-            // compact rows [G][3][bh][d]: the v plane of row g starts 2 * bh * d elements in
-            cv.vg = reinterpret_cast<const uint16_t*>(ws + L.off_globals) + 2 * (size_t)P.bh * P.d;
-            cv.vg16 = reinterpret_cast<uint16_t*>(ws + L.off_vg16);
-        }
-        cudaError_t e = cudaMemsetAsync(cv.any_bad, 0, sizeof(int), stream);
-        if (e == cudaSuccess) e = lca::launch_convert_v16((int)P.d, cv, stream);
-        if (e != cudaSuccess) return fail_cuda(e, "fp16 V copy launch");
-    }
+    if (v16 && (st = enqueue_convert_v16(P, L, v, ws, stream)) != LCA_OK) return st;
     if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16)) != LCA_OK) return st;
     return enqueue_combine_splits(P, L, out, lse, ws, stream);
 }
@@ -671,7 +704,7 @@ int lca_swa_shard_layout(const lca_shard_desc* desc, int64_t num_unique_global, 
     P.G = std::min(num_unique_global, P.n_total);
     const Layout L = make_layout(P);
     memset(out, 0, sizeof(*out));
-    out->total_bytes = L.total;
+    out->total_bytes = L.total_fast;
     out->halo_rows = P.halo();
     out->globals_offset = L.off_globals;
     out->globals_bytes = (size_t)P.G * L.grow_bytes;
@@ -734,7 +767,10 @@ int lca_swa_shard_forward(const lca_shard_desc* desc, const void* q, const void*
     if ((st = check_workspace(L, workspace, workspace_bytes)) != LCA_OK) return st;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream)) != LCA_OK) return st;
+    // the compact global rows and the halos are complete here (after the exchange)
+    const bool v16 = L.total_fast > L.total && workspace_bytes >= L.total_fast;
+    if (v16 && (st = enqueue_convert_v16(P, L, v, ws, stream)) != LCA_OK) return st;
+    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16)) != LCA_OK) return st;
     return enqueue_combine_splits(P, L, out, lse, ws, stream);
 }
 

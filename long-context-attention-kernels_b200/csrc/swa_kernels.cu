@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                  const __grid_constant__ CUtensorMap tm_kg, const __grid_constant__ CUtensorMap tm_vg,
                  const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_po,
                  const __grid_constant__ CUtensorMap tm_v16, const __grid_constant__ CUtensorMap tm_vg16,
-                 const MainParams p) {
+                 const __grid_constant__ CUtensorMap tm_vh16, const MainParams p) {
     using C = Cfg<D, BF16, V16>;
     if (p.v16_bad != nullptr) {
         // bf16 with an fp16 copy of V: both variants are launched and one does the work --
@@ -380,10 +380,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                             } else if (p.sharded) {
                                 // the tile lies wholly in the left halo, the shard or the right halo
                                 if (y < p.q_off) {
-                                    m = kv ? &tm_vh : &tm_kh;
+                                    m = kv ? (V16 ? &tm_vh16 : &tm_vh) : &tm_kh;
                                     y -= p.q_off - p.halo;
                                 } else if (y >= p.q_off + p.n) {
-                                    m = kv ? &tm_vh : &tm_kh;
+                                    m = kv ? (V16 ? &tm_vh16 : &tm_vh) : &tm_kh;
                                     y -= p.q_off + p.n;
                                     z += 2 * p.bh;
                                 } else {
@@ -923,36 +923,32 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
 
 // ------------------------------------------------------------------------ fp16 copy of V
 
-// One block per 128-row block of one head: blocks [0, bh * blocks) cover V, the rest the
-// compact global V rows (g_tiles * bh of them).  Each thread converts 16-byte chunks (8
-// values); a block whose values the copy cannot stand in for sets *any_bad (see
-// ConvertParams).
+// One block per 128-row block of one plane of one segment (segments in order); each thread
+// converts 16-byte chunks (8 values) of the block's rows.
 template <int D>
 __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
     constexpr int kChunksPerRow = D / 8;
-    const long long blk = blockIdx.x;
-    const long long main_blocks = (long long)cp.bh * cp.blocks;
-    const bool compact = blk >= main_blocks;
-    int b, r0, rows;
-    if (!compact) {
-        b = (int)(blk / cp.blocks);
-        r0 = (int)(blk % cp.blocks) * 128;
-        rows = min(128, cp.n - r0);
-    } else {
-        const long long t = blk - main_blocks;
-        const int gt = (int)(t / cp.bh);
-        b = (int)(t % cp.bh);
-        r0 = gt * 128;
-        rows = min(128, cp.num_global - r0);
+    long long blk = blockIdx.x;
+    int si = 0;
+    for (; si < cp.n_segments; ++si) {
+        const long long nb = (long long)cp.seg[si].planes * ((cp.seg[si].rows + 127) / 128);
+        if (blk < nb) break;
+        blk -= nb;
     }
+    if (si >= cp.n_segments) return;
+    const ConvertSegment sg = cp.seg[si];
+    const int per_plane = (sg.rows + 127) / 128;
+    const int pl = (int)(blk / per_plane);
+    const int r0 = (int)(blk % per_plane) * 128;
+    const int rows = min(128, sg.rows - r0);
     bool bad = false, inexact = false;
     float amax = 0.f;
     for (int c = threadIdx.x; c < rows * kChunksPerRow; c += blockDim.x) {
-        const int r = r0 + c / kChunksPerRow;
+        const long long r = r0 + c / kChunksPerRow;
         const int col = (c % kChunksPerRow) * 8;
-        const size_t src = compact ? ((size_t)r * 3 * cp.bh + b) * D + col : ((size_t)b * cp.n + r) * D + col;
-        const size_t dst = compact ? ((size_t)r * cp.bh + b) * D + col : src;
-        const uint4 in = *reinterpret_cast<const uint4*>((compact ? cp.vg : cp.v) + src);
+        const long long src = pl * sg.src_plane + r * sg.src_row + col;
+        const long long dst = pl * sg.dst_plane + r * sg.dst_row + col;
+        const uint4 in = *reinterpret_cast<const uint4*>(sg.src + src);
         const uint32_t w[4] = {in.x, in.y, in.z, in.w};
         uint32_t o[4];
 #pragma unroll
@@ -967,7 +963,7 @@ __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
             amax = fmaxf(amax, fmaxf(fabsf(f0), fabsf(f1)));
             o[i] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        *reinterpret_cast<uint4*>((compact ? cp.vg16 : cp.v16) + dst) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(sg.dst + dst) = make_uint4(o[0], o[1], o[2], o[3]);
     }
     __shared__ float s_max[8];
 #pragma unroll
@@ -1152,7 +1148,7 @@ static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, Cfg<D, BF16, V16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kh, tm.vh, tm.qg, tm.kg, tm.vg,
-                                                              tm.o, tm.po, tm.v16, tm.vg16, p);
+                                                              tm.o, tm.po, tm.v16, tm.vg16, tm.vh16, p);
     return cudaGetLastError();
 }
 
@@ -1201,7 +1197,8 @@ cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t s
 }
 
 cudaError_t launch_convert_v16(int head_dim, const ConvertParams& cp, cudaStream_t stream) {
-    const long long blocks = (long long)cp.bh * cp.blocks + (cp.num_global > 0 ? (long long)cp.g_tiles * cp.bh : 0);
+    long long blocks = 0;
+    for (int i = 0; i < cp.n_segments; ++i) blocks += (long long)cp.seg[i].planes * ((cp.seg[i].rows + 127) / 128);
     if (blocks <= 0) return cudaSuccess;
     if (blocks > INT_MAX) return cudaErrorInvalidValue;
     if (head_dim == 64)

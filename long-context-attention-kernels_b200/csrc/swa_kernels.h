@@ -43,6 +43,7 @@ struct TensorMaps {
     CUtensorMap po;          // global-row partial outputs [2*splits*bh][G][d] fp32
     CUtensorMap v16, vg16;   // bf16 inputs: fp16 copies of V [bh][n][d] and of the compact global V
                              // rows [G][bh][d] (maps {d, bh, G}); the bf16 maps when unused
+    CUtensorMap vh16;        // fp16 copy of the V halo blocks (encoded like vh); vh when unused
 };
 
 // Key and query indices below are absolute positions in the full sequence unless named
@@ -130,19 +131,23 @@ struct CombineParams {
     size_t parity_floats;
 };
 
-// fp16 copy of bf16 V in 128-row blocks: v16[b][r][:] = fp16(v[b][r][:]) for r < n, and
-// the same for the compact global V rows (`vg`, row g of head b at vg + (g * 3 * bh + b) *
-// d) into vg16 [G][bh][d].  A block passes when every value converts without overflow and
-// either exactly or, for magnitudes below 2^-14 (fp16 subnormals, absolute error at most
-// 2^-25), in a block whose largest magnitude is at least 2^-4; a block that fails sets
-// *any_bad (which the host zeroes beforehand).
+// fp16 copy of bf16 V rows.  A segment is `planes` arrays of `rows` rows of d values: row
+// r of plane pl at src + pl * src_plane + r * src_row (elements), written to the same
+// place of dst with dst_plane / dst_row.  Rows are converted in blocks of 128.  A block
+// passes when every value converts without overflow and either exactly or, for magnitudes
+// below 2^-14 (fp16 subnormals, absolute error at most 2^-25), in a block whose largest
+// magnitude is at least 2^-4; a block that fails sets *any_bad (which the host zeroes
+// beforehand).
+constexpr int kMaxConvertSegments = 4;
+struct ConvertSegment {
+    const uint16_t* src;
+    uint16_t* dst;
+    int planes, rows;
+    long long src_plane, src_row, dst_plane, dst_row;
+};
 struct ConvertParams {
-    int bh, n, blocks;
-    int num_global, g_tiles;
-    const uint16_t* v;
-    uint16_t* v16;
-    const uint16_t* vg;
-    uint16_t* vg16;
+    int n_segments;
+    ConvertSegment seg[kMaxConvertSegments];
     int* any_bad;
 };
 cudaError_t launch_convert_v16(int head_dim, const ConvertParams& cp, cudaStream_t stream);
