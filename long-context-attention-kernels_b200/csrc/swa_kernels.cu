@@ -488,13 +488,15 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                     // holding that P.  The first half also waits for the accumulators to be free
                     // and for the V tile.
                     auto pv_half = [&](int h) -> bool {
-                        LCA_TRACE_EVENT(trace::EV_MMA_P_WAIT);
-                        if (!W(&ctl->p_full[X][h], pc)) return false;
-                        LCA_TRACE_EVENT(trace::EV_MMA_P_READY);
+                        // (the accumulators and the V tile are usually ready long before P:
+                        // check them first, off the P -> P*V -> S chain)
                         if (h == 0) {
                             if (first && oc > 0 && !W(&ctl->o_free[X], oc - 1)) return false;
                             if (!W(&ctl->kv_full[pend_lv % C::kSlots], pend_lv / C::kSlots)) return false;
                         }
+                        LCA_TRACE_EVENT(trace::EV_MMA_P_WAIT);
+                        if (!W(&ctl->p_full[X][h], pc)) return false;
+                        LCA_TRACE_EVENT(trace::EV_MMA_P_READY);
                         issue_pv(pend_lv % C::kSlots, pend_cols, first, h);
                         LCA_TRACE_EVENT(trace::EV_MMA_PV_ISSUED);
                         return true;
