@@ -97,7 +97,12 @@ template <int D, bool BF16, bool V16 = false>
 struct Cfg {
     static constexpr bool kSplitP = BF16 && !V16;
     static constexpr int kHalves = (D == 64) ? 2 : 1;      // softmax warpgroups per query tile
-    static constexpr int kCols = BN / kHalves;             // S columns per softmax thread
+    // Each S tile is two 64-key chains (S -> P -> P*V per chain).  At d = 64 each chain has
+    // its own warpgroup and accumulator; at d = 128 one warpgroup runs both chains in turn
+    // into one accumulator, so the second chain's S is ready while the first one's P*V and
+    // next S run.
+    static constexpr int kChains = 2;
+    static constexpr int kCols = BN / kChains;             // S columns per chain
     static constexpr int kSoftmaxWarps = 8 * kHalves;
     static constexpr int kTmaWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
@@ -139,8 +144,9 @@ struct Ctl {
     uint64_t q_empty[2];
     uint64_t kv_full[kMaxSlots];
     uint64_t kv_empty[kMaxSlots];
-    uint64_t s_full[2][2];   // [query tile][half]: S columns of the half ready
-    uint64_t p_full[2][2];   // [query tile][half]: P of the half written
+    uint64_t s_full[2][2];   // [query tile][chain]: S columns of the chain ready
+    uint64_t p_full[2][2];   // [query tile][chain]: P of the chain written
+    uint64_t pv_done[2][2];  // [query tile][chain]: P*V of the chain completed (one phase per member tile)
     uint64_t o_full[2];
     uint64_t o_free[2];
     uint64_t mma_drained[2];
@@ -275,6 +281,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
         if (V16 ? bad : !bad) return;
     }
     constexpr int H = C::kHalves;
+    constexpr int NC = C::kChains;
     constexpr int KC = C::kCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -298,6 +305,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
             for (int h = 0; h < 2; ++h) {
                 ptx::mbar_init(&ctl->s_full[x][h], 1);
                 ptx::mbar_init(&ctl->p_full[x][h], 4);
+                ptx::mbar_init(&ctl->pv_done[x][h], 1);
             }
             ptx::mbar_init(&ctl->o_full[x], 1);
             ptx::mbar_init(&ctl->o_free[x], 4 * H);
@@ -459,7 +467,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                 auto issue_pv = [&](int slot, int ncols, bool first, int h) {
                     const uint32_t vlo = ptx::smem_desc_sw128_lo(sslots + slot * C::kTileBytes, kPanelBytes);
                     {
-                        const uint32_t dcol = tmem + C::kOCol + (X * H + h) * D;
+                        // d = 64: chain h's own accumulator; d = 128: one accumulator, which
+                        // chain 1 adds to from its first MMA on
+                        const uint32_t dcol = tmem + C::kOCol + (X * H + (H == 2 ? h : 0)) * D;
+                        const bool fresh = first && (H == 2 || h == 0);
 #pragma unroll
                         for (int part = 0; part < (C::kSplitP ? 2 : 1); ++part) {
 #pragma unroll
@@ -468,7 +479,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                                 if (key < ncols) {
                                     const uint32_t acol = sx + (key >> 5) * 32 + part * 16 + ((key >> 4) & 1) * 8;
                                     ptx::mma_f16_ts(dcol, acol, ptx::desc_join(vlo + ((key * 128) >> 4), dhi),
-                                                    idesc_pv, (!first || part > 0 || kk > 0) ? 1u : 0u);
+                                                    idesc_pv, (!fresh || part > 0 || kk > 0) ? 1u : 0u);
                                 }
                             }
                         }
@@ -498,6 +509,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                         if (!W(&ctl->p_full[X][h], pc)) return false;
                         LCA_TRACE_EVENT(trace::EV_MMA_P_READY);
                         issue_pv(pend_lv % C::kSlots, pend_cols, first, h);
+                        ptx::mma_commit(&ctl->pv_done[X][h]);
                         LCA_TRACE_EVENT(trace::EV_MMA_PV_ISSUED);
                         return true;
                     };
@@ -511,38 +523,38 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                         const Tile t = tile_of(p, un, j);
                         const bool mem = act && (X ? t.mem[1] : t.mem[0]);
                         const int lk = L + 2 * j, lv = lk + 1;
-                        if (H == 1 || !mem) {
-                            // The pending P*V goes first: it releases its V slot, which the
-                            // producer may need before it can load this tile (a 3-slot ring
-                            // holds one tile plus one V), and it must precede the next S MMA.
+                        if (!mem) {
+                            // Not a member tile: the pending P*V goes first (it releases its V
+                            // slot, which the producer may need before it can load this tile),
+                            // then this tile's K and V slots are released once landed.
                             if (pend_lv >= 0) {
                                 bool pv_ok = true;
 #pragma unroll
-                                for (int h = 0; h < H; ++h) pv_ok = pv_ok && pv_half(h);
+                                for (int h = 0; h < NC; ++h) pv_ok = pv_ok && pv_half(h);
                                 if (!pv_ok) break;
                                 pv_done();
                             }
                             LCA_TRACE_EVENT(trace::EV_MMA_K_WAIT);
                             if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
                             LCA_TRACE_EVENT(trace::EV_MMA_K_READY);
-                            if (mem) {
-                                issue_s(lk % C::kSlots, t.ncols, 0);
-                                ptx::mma_commit(&ctl->s_full[X][0]);
-                                LCA_TRACE_EVENT(trace::EV_MMA_S_ISSUED);
-                            }
                         } else {
-                            // Two halves (4-slot ring): K of this tile can land while the
-                            // pending V is held, so each half runs its own chain, P*V of the
-                            // pending tile then S of this one, as soon as its P is written.
-                            LCA_TRACE_EVENT(trace::EV_MMA_K_WAIT);
-                            if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) break;
-                            LCA_TRACE_EVENT(trace::EV_MMA_K_READY);
+                            // Member tile: each chain runs P*V of the pending tile, then S of
+                            // this one, as soon as that chain's P is written.  Chain 0's P*V
+                            // goes before the wait for this tile's K (it does not need it).
                             bool s_ok = true;
 #pragma unroll
-                            for (int h = 0; h < H; ++h) {
+                            for (int h = 0; h < NC; ++h) {
                                 if (pend_lv >= 0 && !pv_half(h)) {
                                     s_ok = false;
                                     break;
+                                }
+                                if (h == 0) {
+                                    LCA_TRACE_EVENT(trace::EV_MMA_K_WAIT);
+                                    if (!W(&ctl->kv_full[lk % C::kSlots], lk / C::kSlots)) {
+                                        s_ok = false;
+                                        break;
+                                    }
+                                    LCA_TRACE_EVENT(trace::EV_MMA_K_READY);
                                 }
                                 issue_s(lk % C::kSlots, t.ncols, h);
                                 ptx::mma_commit(&ctl->s_full[X][h]);
@@ -567,7 +579,7 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                     if (pend_lv >= 0) {
                         bool pv_ok = true;
 #pragma unroll
-                        for (int h = 0; h < H; ++h) pv_ok = pv_ok && pv_half(h);
+                        for (int h = 0; h < NC; ++h) pv_ok = pv_ok && pv_half(h);
                         if (!pv_ok) break;
                         pv_done();
                     }
@@ -593,7 +605,6 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
         const int tile_bar = 1 + X;       // named barrier: all warpgroups of tile X
         const int wg_bar = 3 + sw;        // named barrier: this warpgroup
         const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
-        const uint32_t s_col = X * 128 + KC * hh;            // this warpgroup's S / P columns
         const uint32_t o_col = C::kOCol + (X * H + hh) * D;  // this warpgroup's accumulator
         const uint32_t o_col0 = C::kOCol + (X * H) * D;      // accumulator of half 0 of tile X
         uint8_t* stage = smem + C::kOffStage + sw * C::kStageBytes;
@@ -646,163 +657,179 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
             for (int j = 0; j < un.ntiles; ++j) {
                 const Tile t = tile_of(p, un, j);
                 if (!(X ? t.mem[1] : t.mem[0])) continue;
-                LCA_TRACE_LANE0(trace::EV_S_WAIT);
-                if (ok) ok = warp_wait(&ctl->s_full[X][H == 1 ? 0 : hh], sc & 1, abort_flag, p.err,
-                                       LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
-                LCA_TRACE_LANE0(trace::EV_S_READY);
-                ++sc;
-                const int col0 = t.row0 + KC * hh;  // key (band) or compact global row of column 0
-                const int ncols_h = t.ncols - KC * hh;
-                if (ok && warp_live && ncols_h > 0) {
-                    ptx::tc_fence_after();
-                    // visible columns of this row in this tile: [lo, hi] minus the hole [h_lo, h_hi)
-                    int lo, hi, h_lo = 0, h_hi = 0;
-                    if (t.global_key) {
-                        lo = 0;
-                        hi = p.num_global - 1 - col0;
-                        h_lo = g_lo - col0;
-                        h_hi = g_hi - col0;
-                    } else {
-                        lo = jlo - col0;
-                        hi = jhi - col0;
-                    }
-                    if (hi > ncols_h - 1) hi = ncols_h - 1;
-                    const int nchunks = ((ncols_h < KC ? ncols_h : KC) + 31) >> 5;
-                    // ---- pass 1: S row into registers, masked row max
-                    float s[KC];
-#pragma unroll
-                    for (int c = 0; c < KC / 32; ++c) {
-                        if (c < nchunks) {
-                            float tmp[32];
-                            ptx::tmem_ld32(t_lane + s_col + c * 32, tmp);
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) s[c * 32 + e] = tmp[e];
+                // the chains of this tile this warpgroup runs: its own (d = 64) or both (d = 128)
+                for (int ch = (H == 2 ? hh : 0); ch < (H == 2 ? hh + 1 : NC); ++ch) {
+                    LCA_TRACE_LANE0(trace::EV_S_WAIT);
+                    if (ok) ok = warp_wait(&ctl->s_full[X][ch], sc & 1, abort_flag, p.err,
+                                           LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+                    LCA_TRACE_LANE0(trace::EV_S_READY);
+                    const uint32_t s_col = X * 128 + KC * ch;  // this chain's S / P columns
+                    const int col0 = t.row0 + KC * ch;  // key (band) or compact global row of column 0
+                    const int ncols_h = t.ncols - KC * ch;
+                    if (ok && warp_live && ncols_h > 0) {
+                        ptx::tc_fence_after();
+                        // visible columns of this row in this tile: [lo, hi] minus the hole [h_lo, h_hi)
+                        int lo, hi, h_lo = 0, h_hi = 0;
+                        if (t.global_key) {
+                            lo = 0;
+                            hi = p.num_global - 1 - col0;
+                            h_lo = g_lo - col0;
+                            h_hi = g_hi - col0;
                         } else {
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) s[c * 32 + e] = sent;
+                            lo = jlo - col0;
+                            hi = jhi - col0;
                         }
-                    }
-                    const bool need = lo > 0 || hi < KC - 1 || (h_lo < h_hi && h_hi > 0 && h_lo < KC);
-                    const bool any_mask = __any_sync(0xffffffffu, need);
-                    // visible columns of each 32-column chunk as a bit mask: [lo, hi] minus
-                    // [h_lo, h_hi) (all ones when the warp needs no mask)
-                    uint32_t vis[KC / 32];
-#pragma unroll
-                    for (int c = 0; c < KC / 32; ++c)
-                        vis[c] = any_mask ? (span_bits(lo, hi + 1, c * 32) & ~span_bits(h_lo, h_hi, c * 32)) : ~0u;
-                    ptx::tmem_wait_ld();
-                    if (any_mask) {
-#pragma unroll
-                        for (int c = 0; c < KC; ++c) s[c] = ((vis[c >> 5] >> (c & 31)) & 1u) ? s[c] : sent;
-                    }
-                    LCA_TRACE_LANE0(trace::EV_S_LOADED);
-                    float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
-                    if (!neg_scale) {
-#pragma unroll
-                        for (int c = 0; c < KC; c += 8) {
-                            r0 = ptx::fmax3(r0, s[c + 0], s[c + 1]);
-                            r1 = ptx::fmax3(r1, s[c + 2], s[c + 3]);
-                            r2 = ptx::fmax3(r2, s[c + 4], s[c + 5]);
-                            r3 = ptx::fmax3(r3, s[c + 6], s[c + 7]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int c = 0; c < KC; c += 8) {
-                            r0 = ptx::fmin3(r0, s[c + 0], s[c + 1]);
-                            r1 = ptx::fmin3(r1, s[c + 2], s[c + 3]);
-                            r2 = ptx::fmin3(r2, s[c + 4], s[c + 5]);
-                            r3 = ptx::fmin3(r3, s[c + 6], s[c + 7]);
-                        }
-                    }
-                    const float mr =
-                        neg_scale ? fminf(fminf(r0, r1), fminf(r2, r3)) : fmaxf(fmaxf(r0, r1), fmaxf(r2, r3));
-                    const float mt = (mr == sent) ? -INFINITY : mr * sl2;
-
-                    // ---- online softmax with lazy rescale (O is stable: see header)
-                    bool rescale = false;
-                    float alpha = 1.f;
-                    if (mt > m + kRescaleThreshold || (m == -INFINITY && mt > -INFINITY)) {
-                        rescale = seen && (m != -INFINITY);
-                        alpha = (m == -INFINITY) ? 0.f : ptx::ex2(m - mt);
-                        m = mt;
-                        l *= alpha;
-                    }
-                    if (__any_sync(0xffffffffu, rescale)) {
-                        // rare: rescale this row's accumulator, 8 columns at a time (few live registers)
-                        const float a = rescale ? alpha : 1.f;
-#pragma unroll 1
-                        for (int c = 0; c < D / 8; ++c) {
-                            uint32_t o[8];
-                            ptx::tmem_ld8(t_lane + o_col + c * 8, o);
-                            ptx::tmem_wait_ld();
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
-                            ptx::tmem_st8u(t_lane + o_col + c * 8, o);
-                        }
-                    }
-                    // ---- pass 2, from the registers of pass 1, one 32-key chunk at a time:
-                    // p = 2^(s * scale * log2(e) - m) (masked scores are already `sent`, which
-                    // maps to 0), row sum, 16-bit pairs written over the chunk's own S columns
-                    // (hi pairs, then lo pairs for bf16).  Chunks masked for the whole warp skip
-                    // the exponentials.
-                    // Pairs of columns go through the packed fp32x2 pipe: one FMA for the
-                    // exponent arguments, one add for the row sums and, for bf16, one
-                    // subtract for the low parts.
-                    LCA_TRACE_LANE0(trace::EV_MAX_DONE);
-                    const float neg_m = (m == -INFINITY) ? 0.f : -m;
-                    const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
-                    const uint64_t negm2 = ptx::f2_pack(neg_m, neg_m);
-                    uint64_t acc0 = 0ull, acc1 = 0ull;  // {+0.f, +0.f}
-#pragma unroll
-                    for (int c = 0; c < KC / 32; ++c) {
-                        if (c >= nchunks) break;
-                        const int c0 = c * 32;
-                        if (__all_sync(0xffffffffu, vis[c] == 0u)) {
-                            uint32_t z[16];
-#pragma unroll
-                            for (int e = 0; e < 16; ++e) z[e] = 0u;
-                            ptx::tmem_st16u(t_lane + s_col + c0, z);
-                            if (C::kSplitP) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
-                        } else {
-                            const float* v = s + c0;
-#pragma unroll
-                            for (int g8 = 0; g8 < 2; ++g8) {  // 8 pairs (16 keys) per store
-                                uint32_t w[8];
-                                uint32_t wl[8];
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) {
-                                    const uint64_t x = ptx::f2_fma(
-                                        ptx::f2_pack(v[g8 * 16 + 2 * e], v[g8 * 16 + 2 * e + 1]), sl2x2, negm2);
-                                    const float p0 = ptx::ex2(ptx::f2_lo(x)), p1 = ptx::ex2(ptx::f2_hi(x));
-                                    const uint64_t pp = ptx::f2_pack(p0, p1);
-                                    if (e & 1) acc1 = ptx::f2_add(acc1, pp); else acc0 = ptx::f2_add(acc0, pp);
-                                    if (C::kSplitP) {
-                                        w[e] = ptx::pack_bf16x2(p0, p1);
-                                        const uint64_t rest = ptx::f2_sub(
-                                            pp, ptx::f2_pack(__uint_as_float(w[e] << 16),
-                                                             __uint_as_float(w[e] & 0xFFFF0000u)));
-                                        wl[e] = ptx::pack_bf16x2(ptx::f2_lo(rest), ptx::f2_hi(rest));
-                                    } else {
-                                        w[e] = ptx::pack_f16x2(p0, p1);
-                                    }
-                                }
-                                ptx::tmem_st8u(t_lane + s_col + c0 + g8 * 8, w);
-                                if (C::kSplitP) ptx::tmem_st8u(t_lane + s_col + c0 + 16 + g8 * 8, wl);
+                        if (hi > ncols_h - 1) hi = ncols_h - 1;
+                        const int nchunks = ((ncols_h < KC ? ncols_h : KC) + 31) >> 5;
+                        // ---- pass 1: S row into registers, masked row max
+                        float s[KC];
+    #pragma unroll
+                        for (int c = 0; c < KC / 32; ++c) {
+                            if (c < nchunks) {
+                                float tmp[32];
+                                ptx::tmem_ld32(t_lane + s_col + c * 32, tmp);
+    #pragma unroll
+                                for (int e = 0; e < 32; ++e) s[c * 32 + e] = tmp[e];
+                            } else {
+    #pragma unroll
+                                for (int e = 0; e < 32; ++e) s[c * 32 + e] = sent;
                             }
                         }
+                        const bool need = lo > 0 || hi < KC - 1 || (h_lo < h_hi && h_hi > 0 && h_lo < KC);
+                        const bool any_mask = __any_sync(0xffffffffu, need);
+                        // visible columns of each 32-column chunk as a bit mask: [lo, hi] minus
+                        // [h_lo, h_hi) (all ones when the warp needs no mask)
+                        uint32_t vis[KC / 32];
+    #pragma unroll
+                        for (int c = 0; c < KC / 32; ++c)
+                            vis[c] = any_mask ? (span_bits(lo, hi + 1, c * 32) & ~span_bits(h_lo, h_hi, c * 32)) : ~0u;
+                        ptx::tmem_wait_ld();
+                        if (any_mask) {
+    #pragma unroll
+                            for (int c = 0; c < KC; ++c) s[c] = ((vis[c >> 5] >> (c & 31)) & 1u) ? s[c] : sent;
+                        }
+                        LCA_TRACE_LANE0(trace::EV_S_LOADED);
+                        float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
+                        if (!neg_scale) {
+    #pragma unroll
+                            for (int c = 0; c < KC; c += 8) {
+                                r0 = ptx::fmax3(r0, s[c + 0], s[c + 1]);
+                                r1 = ptx::fmax3(r1, s[c + 2], s[c + 3]);
+                                r2 = ptx::fmax3(r2, s[c + 4], s[c + 5]);
+                                r3 = ptx::fmax3(r3, s[c + 6], s[c + 7]);
+                            }
+                        } else {
+    #pragma unroll
+                            for (int c = 0; c < KC; c += 8) {
+                                r0 = ptx::fmin3(r0, s[c + 0], s[c + 1]);
+                                r1 = ptx::fmin3(r1, s[c + 2], s[c + 3]);
+                                r2 = ptx::fmin3(r2, s[c + 4], s[c + 5]);
+                                r3 = ptx::fmin3(r3, s[c + 6], s[c + 7]);
+                            }
+                        }
+                        const float mr =
+                            neg_scale ? fminf(fminf(r0, r1), fminf(r2, r3)) : fmaxf(fmaxf(r0, r1), fmaxf(r2, r3));
+                        const float mt = (mr == sent) ? -INFINITY : mr * sl2;
+
+                        // ---- online softmax with lazy rescale (O is stable: see header)
+                        bool rescale = false;
+                        float alpha = 1.f;
+                        if (mt > m + kRescaleThreshold || (m == -INFINITY && mt > -INFINITY)) {
+                            rescale = seen && (m != -INFINITY);
+                            alpha = (m == -INFINITY) ? 0.f : ptx::ex2(m - mt);
+                            m = mt;
+                            l *= alpha;
+                        }
+                        if (__any_sync(0xffffffffu, rescale)) {
+                            // rare: rescale this row's accumulator, 8 columns at a time (few live
+                            // registers).  At d = 64 the accumulator's last P*V is this chain's,
+                            // covered by the commit of this S.  At d = 128 it is the other chain's
+                            // (of the previous tile for chain 0, of this tile for chain 1): wait for
+                            // it; its completion is the current or the preceding phase of that
+                            // chain's barrier (this S's commit covers the one before).
+                            if constexpr (H == 1) {
+                                const int pc_ch = ch == 0 ? 1 : 0;
+                                const int pc_tile = ch == 0 ? sc - 1 : sc;
+                                if (ok) ok = warp_wait(&ctl->pv_done[X][pc_ch], pc_tile & 1, abort_flag, p.err,
+                                                       LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+                                if (ok) ptx::tc_fence_after();
+                            }
+                            const float a = rescale ? alpha : 1.f;
+    #pragma unroll 1
+                            for (int c = 0; c < D / 8 && ok; ++c) {
+                                uint32_t o[8];
+                                ptx::tmem_ld8(t_lane + o_col + c * 8, o);
+                                ptx::tmem_wait_ld();
+    #pragma unroll
+                                for (int e = 0; e < 8; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
+                                ptx::tmem_st8u(t_lane + o_col + c * 8, o);
+                            }
+                        }
+                        // ---- pass 2, from the registers of pass 1, one 32-key chunk at a time:
+                        // p = 2^(s * scale * log2(e) - m) (masked scores are already `sent`, which
+                        // maps to 0), row sum, 16-bit pairs written over the chunk's own S columns
+                        // (hi pairs, then lo pairs for bf16).  Chunks masked for the whole warp skip
+                        // the exponentials.
+                        // Pairs of columns go through the packed fp32x2 pipe: one FMA for the
+                        // exponent arguments, one add for the row sums and, for bf16, one
+                        // subtract for the low parts.
+                        LCA_TRACE_LANE0(trace::EV_MAX_DONE);
+                        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+                        const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
+                        const uint64_t negm2 = ptx::f2_pack(neg_m, neg_m);
+                        uint64_t acc0 = 0ull, acc1 = 0ull;  // {+0.f, +0.f}
+    #pragma unroll
+                        for (int c = 0; c < KC / 32; ++c) {
+                            if (c >= nchunks) break;
+                            const int c0 = c * 32;
+                            if (__all_sync(0xffffffffu, vis[c] == 0u)) {
+                                uint32_t z[16];
+    #pragma unroll
+                                for (int e = 0; e < 16; ++e) z[e] = 0u;
+                                ptx::tmem_st16u(t_lane + s_col + c0, z);
+                                if (C::kSplitP) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
+                            } else {
+                                const float* v = s + c0;
+    #pragma unroll
+                                for (int g8 = 0; g8 < 2; ++g8) {  // 8 pairs (16 keys) per store
+                                    uint32_t w[8];
+                                    uint32_t wl[8];
+    #pragma unroll
+                                    for (int e = 0; e < 8; ++e) {
+                                        const uint64_t x = ptx::f2_fma(
+                                            ptx::f2_pack(v[g8 * 16 + 2 * e], v[g8 * 16 + 2 * e + 1]), sl2x2, negm2);
+                                        const float p0 = ptx::ex2(ptx::f2_lo(x)), p1 = ptx::ex2(ptx::f2_hi(x));
+                                        const uint64_t pp = ptx::f2_pack(p0, p1);
+                                        if (e & 1) acc1 = ptx::f2_add(acc1, pp); else acc0 = ptx::f2_add(acc0, pp);
+                                        if (C::kSplitP) {
+                                            w[e] = ptx::pack_bf16x2(p0, p1);
+                                            const uint64_t rest = ptx::f2_sub(
+                                                pp, ptx::f2_pack(__uint_as_float(w[e] << 16),
+                                                                 __uint_as_float(w[e] & 0xFFFF0000u)));
+                                            wl[e] = ptx::pack_bf16x2(ptx::f2_lo(rest), ptx::f2_hi(rest));
+                                        } else {
+                                            w[e] = ptx::pack_f16x2(p0, p1);
+                                        }
+                                    }
+                                    ptx::tmem_st8u(t_lane + s_col + c0 + g8 * 8, w);
+                                    if (C::kSplitP) ptx::tmem_st8u(t_lane + s_col + c0 + 16 + g8 * 8, wl);
+                                }
+                            }
+                        }
+                        {
+                            const uint64_t a = ptx::f2_add(acc0, acc1);
+                            l += ptx::f2_lo(a) + ptx::f2_hi(a);
+                        }
+                        LCA_TRACE_LANE0(trace::EV_EXP_DONE);
+                        ptx::tmem_wait_st();
                     }
-                    {
-                        const uint64_t a = ptx::f2_add(acc0, acc1);
-                        l += ptx::f2_lo(a) + ptx::f2_hi(a);
-                    }
-                    LCA_TRACE_LANE0(trace::EV_EXP_DONE);
-                    ptx::tmem_wait_st();
+                    seen = true;
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(&ctl->p_full[X][ch]);
+                    LCA_TRACE_LANE0(trace::EV_P_ARRIVED);
                 }
-                seen = true;
-                ptx::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(&ctl->p_full[X][H == 1 ? 0 : hh]);
-                LCA_TRACE_LANE0(trace::EV_P_ARRIVED);
+                ++sc;  // member tiles: one phase of each chain's s_full / pv_done
             }
 
             // ---- epilogue: merge the halves, O / l -> fp32 rows via staging + TMA store
