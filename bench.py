@@ -319,7 +319,9 @@ def run_ours(args):
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)),
                     "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps * (3 if g else 1),
+            # main kernel; gather and merge with global tokens; for bf16 the fp16 copy of V
+            # and the second main-kernel variant (one of the two returns at once)
+            "gpu_launches": args.steps * (1 + (2 if g else 0) + (2 if w.dtype == "bf16" else 0)),
             "clocks": clocks.report(),
         }
         print(json.dumps(line), flush=True)
@@ -457,9 +459,11 @@ def run_sequence(args):
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)) * world,
                     "d2h_bytes_per_step": oh.numel() * 4 * world, "ms_per_step": e2e_ms},
             # main, halo pack (2+ shards), the two peer puts and the peer merge (peer exchange);
-            # with global tokens also gather, local merge (and the final merge over NCCL)
+            # with global tokens also gather, local merge (and the final merge over NCCL); for
+            # bf16 the fp16 copy of V and the second main-kernel variant
             "gpu_launches": args.steps * (
-                (5 + (2 if g else 0)) if plan.exchange == "peer" else ((2 if world > 1 else 1) + (3 if g else 0))),
+                ((5 + (2 if g else 0)) if plan.exchange == "peer" else ((2 if world > 1 else 1) + (3 if g else 0)))
+                + (2 if w.dtype == "bf16" else 0)),
             "clocks": clocks.report(),
         }
         print(json.dumps(line), flush=True)
