@@ -635,6 +635,8 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                 jlo = qa - p.window > 0 ? qa - p.window : 0;
                 jhi = (qa + p.window < p.n_total - 1) ? qa + p.window : p.n_total - 1;
                 if (p.g_tiles > 0) {
+                    // first global at or after the band's start, then the run inside the band
+                    // (a few entries at most unless globals are dense: then a second search)
                     const int* gl = gidx_in_smem ? sGidx : p.gidx;
                     int a = 0, b = p.num_global;
                     while (a < b) {
@@ -642,10 +644,17 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                         if (gl[mid] < qa - p.window) a = mid + 1; else b = mid;
                     }
                     g_lo = a;
-                    b = p.num_global;
-                    while (a < b) {
-                        const int mid = (a + b) >> 1;
-                        if (gl[mid] <= qa + p.window) a = mid + 1; else b = mid;
+                    int scan = 0;
+                    while (a < p.num_global && scan < 4 && gl[a] <= qa + p.window) {
+                        ++a;
+                        ++scan;
+                    }
+                    if (scan == 4) {
+                        b = p.num_global;
+                        while (a < b) {
+                            const int mid = (a + b) >> 1;
+                            if (gl[mid] <= qa + p.window) a = mid + 1; else b = mid;
+                        }
                     }
                     g_hi = a;
                 }
@@ -972,17 +981,30 @@ __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
     const int rows = min(128, sg.rows - r0);
     bool bad = false, inexact = false;
     float amax = 0.f;
-    for (int c = threadIdx.x; c < rows * kChunksPerRow; c += blockDim.x) {
+    // every chunk load of this thread first, then the conversions and stores (the loads
+    // stay in flight together)
+    constexpr int kPer = 128 * kChunksPerRow / 256;  // chunks per thread (blockDim.x == 256)
+    const int total = rows * kChunksPerRow;
+    uint4 in[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = (int)threadIdx.x + i * 256;
+        if (c < total) {
+            const long long r = r0 + c / kChunksPerRow;
+            in[i] = *reinterpret_cast<const uint4*>(sg.src + pl * sg.src_plane + r * sg.src_row +
+                                                    (c % kChunksPerRow) * 8);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = (int)threadIdx.x + i * 256;
+        if (c >= total) break;
         const long long r = r0 + c / kChunksPerRow;
-        const int col = (c % kChunksPerRow) * 8;
-        const long long src = pl * sg.src_plane + r * sg.src_row + col;
-        const long long dst = pl * sg.dst_plane + r * sg.dst_row + col;
-        const uint4 in = *reinterpret_cast<const uint4*>(sg.src + src);
-        const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+        const uint32_t w[4] = {in[i].x, in[i].y, in[i].z, in[i].w};
         uint32_t o[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float f0 = __uint_as_float(w[i] << 16), f1 = __uint_as_float(w[i] & 0xFFFF0000u);
+        for (int e = 0; e < 4; ++e) {
+            const float f0 = __uint_as_float(w[e] << 16), f1 = __uint_as_float(w[e] & 0xFFFF0000u);
             const __half2 h = __floats2half2_rn(f0, f1);
             const float2 back = __half22float2(h);
             // bf16 values in the fp16 normal range convert exactly; below 2^-14 they round to
@@ -990,9 +1012,10 @@ __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
             if (back.x != f0) (fabsf(f0) < 6.103515625e-05f ? inexact : bad) = true;
             if (back.y != f1) (fabsf(f1) < 6.103515625e-05f ? inexact : bad) = true;
             amax = fmaxf(amax, fmaxf(fabsf(f0), fabsf(f1)));
-            o[i] = *reinterpret_cast<const uint32_t*>(&h);
+            o[e] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        *reinterpret_cast<uint4*>(sg.dst + dst) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(sg.dst + pl * sg.dst_plane + r * sg.dst_row + (c % kChunksPerRow) * 8) =
+            make_uint4(o[0], o[1], o[2], o[3]);
     }
     __shared__ float s_max[8];
 #pragma unroll
