@@ -392,6 +392,32 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
     return r;
 }
 
+// 2^x for a pair of fp32 values on the FMA and integer pipes instead of the MUFU unit.
+// x = j + f with j = floor(x) and f in [0, 1):
+//   * j comes from one round-down add of 1.5 * 2^23, which leaves floor(x) in the low
+//     mantissa bits of the sum (exact for |x| < 2^22), so that the sum's bits shifted left
+//     by 23 are j * 2^23 modulo 2^32;
+//   * 2^f is a degree-3 polynomial, p(0) = 1, whose coefficients minimise the largest
+//     relative error on [0, 1) (linear program over a dense grid; max |p / 2^f - 1| is
+//     8.6e-5 in fp32 Horner form, below half an fp16 ulp);
+//   * j is added to the exponent field of p.
+// x is clamped below at -127 (the result is then below 2^-126: a subnormal that converts
+// to 0 in fp16); -inf maps to that clamp.  The largest argument used is 2^8.
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
+    const float x0 = fmaxf(f2_lo(x), -127.f), x1 = fmaxf(f2_hi(x), -127.f);
+    const uint64_t xc = f2_pack(x0, x1);
+    const uint64_t magic = f2_pack(12582912.f, 12582912.f);  // 1.5 * 2^23
+    uint64_t t;
+    asm("add.rm.f32x2 %0, %1, %2;" : "=l"(t) : "l"(xc), "l"(magic));
+    const uint64_t f = f2_sub(xc, f2_sub(t, magic));
+    uint64_t p = f2_fma(f, f2_pack(0x1.3baadcp-4f, 0x1.3baadcp-4f), f2_pack(0x1.d23788p-3f, 0x1.d23788p-3f));
+    p = f2_fma(p, f, f2_pack(0x1.63e654p-1f, 0x1.63e654p-1f));
+    p = f2_fma(p, f, f2_pack(1.f, 1.f));
+    const uint32_t r0 = static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23);
+    const uint32_t r1 = static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
+    return (static_cast<uint64_t>(r1) << 32) | r0;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));

@@ -87,6 +87,23 @@ constexpr float kLn2 = 0.6931471805599453f;
 // more than this many powers of two; results are exact either way because l and O are
 // accumulated against the same reference max.
 constexpr float kRescaleThreshold = 8.0f;
+// Build options for measured alternatives (the defaults are the fastest measured):
+//   LCA_D64_HALVES     softmax warpgroups per query tile at d = 64 (2, or 1 as at d = 128)
+//   LCA_FAST_EXP_D64   the exponent pass before the max pass at d = 64 (spills at 104 registers)
+//   LCA_POLY_MASK_D64 / LCA_POLY_MASK_D128   pairs of each 8-pair group exponentiated on the
+//                      FMA pipe (Cfg::kPolyMask)
+#ifndef LCA_D64_HALVES
+#define LCA_D64_HALVES 2
+#endif
+#ifndef LCA_FAST_EXP_D64
+#define LCA_FAST_EXP_D64 0
+#endif
+#ifndef LCA_POLY_MASK_D64
+#define LCA_POLY_MASK_D64 0u
+#endif
+#ifndef LCA_POLY_MASK_D128
+#define LCA_POLY_MASK_D128 0u
+#endif
 
 // For bf16 inputs P is split as P_hi + P_lo (P_hi = rn_bf16(p), P_lo = rn_bf16(p - P_hi))
 // and P*V is issued twice into the same accumulator: a single bf16 P carries ~1.5e-3
@@ -96,7 +113,12 @@ constexpr float kRescaleThreshold = 8.0f;
 template <int D, bool BF16, bool V16 = false>
 struct Cfg {
     static constexpr bool kSplitP = BF16 && !V16;
-    static constexpr int kHalves = (D == 64) ? 2 : 1;      // softmax warpgroups per query tile
+    // Pairs of each 8-pair (16-key) group whose exponentials run as a polynomial on the FMA
+    // pipe instead of the MUFU unit (bit e: pair e), so the two pipes share the exponent
+    // pass.  fp16 P only: the polynomial's relative error (8.6e-5) is below half an fp16
+    // ulp but above the 16-bit precision of the split bf16 P.
+    static constexpr unsigned kPolyMask = kSplitP ? 0u : (D == 64 ? LCA_POLY_MASK_D64 : LCA_POLY_MASK_D128);
+    static constexpr int kHalves = (D == 64) ? LCA_D64_HALVES : 1;  // softmax warpgroups per query tile
     // Each S tile is two 64-key chains (S -> P -> P*V per chain).  At d = 64 each chain has
     // its own warpgroup and accumulator; at d = 128 one warpgroup runs both chains in turn
     // into one accumulator, so the second chain's S is ready while the first one's P*V and
@@ -104,19 +126,23 @@ struct Cfg {
     static constexpr int kChains = 2;
     static constexpr int kCols = BN / kChains;             // S columns per chain
     static constexpr int kSoftmaxWarps = 8 * kHalves;
+    // Exponentiate against the current reference max before knowing the row max (the max
+    // pass then runs only when an argument exceeds the rescale threshold).  The scores stay
+    // live through the pass, which the 104-register softmax warps of d = 64 cannot afford.
+    static constexpr bool kFastExp = (kHalves == 1) || LCA_FAST_EXP_D64;
     static constexpr int kTmaWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
     // softmax warpgroups, then one control warpgroup (TMA warp, two MMA warps, one idle)
     static constexpr int kThreads = (kSoftmaxWarps + 4) * 32;
     // registers per thread: at launch, after setmaxnreg in the softmax / control warpgroups
-    static constexpr int kRegsLaunch = (D == 64) ? 96 : 168;
-    static constexpr int kRegsSoftmax = (D == 64) ? 104 : 216;
-    static constexpr int kRegsControl = (D == 64) ? 64 : 72;
+    static constexpr int kRegsLaunch = (kHalves == 2) ? 96 : 168;
+    static constexpr int kRegsSoftmax = (kHalves == 2) ? 104 : 216;
+    static constexpr int kRegsControl = (kHalves == 2) ? 64 : 72;
     static constexpr int kEpiCols = D / kHalves;           // output columns per warpgroup
     static constexpr int kPanels = D / 64;
     static constexpr int kTileBytes = BM * D * 2;
     static constexpr int kSlots = (D == 64) ? 7 : 3;  // K / V ring: one K or V tile per slot
-    static constexpr int kStagePanels = (D == 64) ? 1 : 2;   // epilogue staging panels per softmax warpgroup
+    static constexpr int kStagePanels = (kHalves == 2) ? 1 : 2;  // epilogue staging panels per softmax warpgroup
     static constexpr int kStageBytes = kStagePanels * kPanelBytes;
     static constexpr int kOffQ = 0;
     static constexpr int kOffSlots = kOffQ + 2 * kTileBytes;
@@ -718,112 +744,143 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                             for (int c = 0; c < KC; ++c) s[c] = ((vis[c >> 5] >> (c & 31)) & 1u) ? s[c] : sent;
                         }
                         LCA_TRACE_LANE0(trace::EV_S_LOADED);
-                        float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
-                        if (!neg_scale) {
+                        // ---- exponent pass, one 32-key chunk at a time, from the registers:
+                        // p = 2^(s * scale * log2(e) - mref) (masked scores are already `sent`,
+                        // which maps to 0), row sums into acc, 16-bit pairs written over the
+                        // chunk's own S columns (hi pairs, then lo pairs for bf16).  Chunks masked
+                        // for the whole warp skip the exponentials.  Pairs of columns go through
+                        // the packed fp32x2 pipe: one FMA for the exponent arguments, one add for
+                        // the row sums and, for bf16, one subtract for the low parts.  Returns the
+                        // largest exponent argument of the row.
+                        auto exp_pass = [&](float mref, uint64_t& acc0, uint64_t& acc1) -> float {
+                            const float neg_m = (mref == -INFINITY) ? 0.f : -mref;
+                            const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
+                            const uint64_t negm2 = ptx::f2_pack(neg_m, neg_m);
+                            float xm = -INFINITY;
     #pragma unroll
-                            for (int c = 0; c < KC; c += 8) {
-                                r0 = ptx::fmax3(r0, s[c + 0], s[c + 1]);
-                                r1 = ptx::fmax3(r1, s[c + 2], s[c + 3]);
-                                r2 = ptx::fmax3(r2, s[c + 4], s[c + 5]);
-                                r3 = ptx::fmax3(r3, s[c + 6], s[c + 7]);
-                            }
-                        } else {
+                            for (int c = 0; c < KC / 32; ++c) {
+                                if (c >= nchunks) break;
+                                const int c0 = c * 32;
+                                if (__all_sync(0xffffffffu, vis[c] == 0u)) {
+                                    uint32_t z[16];
     #pragma unroll
-                            for (int c = 0; c < KC; c += 8) {
-                                r0 = ptx::fmin3(r0, s[c + 0], s[c + 1]);
-                                r1 = ptx::fmin3(r1, s[c + 2], s[c + 3]);
-                                r2 = ptx::fmin3(r2, s[c + 4], s[c + 5]);
-                                r3 = ptx::fmin3(r3, s[c + 6], s[c + 7]);
-                            }
-                        }
-                        const float mr =
-                            neg_scale ? fminf(fminf(r0, r1), fminf(r2, r3)) : fmaxf(fmaxf(r0, r1), fmaxf(r2, r3));
-                        const float mt = (mr == sent) ? -INFINITY : mr * sl2;
-
-                        // ---- online softmax with lazy rescale (O is stable: see header)
-                        bool rescale = false;
-                        float alpha = 1.f;
-                        if (mt > m + kRescaleThreshold || (m == -INFINITY && mt > -INFINITY)) {
-                            rescale = seen && (m != -INFINITY);
-                            alpha = (m == -INFINITY) ? 0.f : ptx::ex2(m - mt);
-                            m = mt;
-                            l *= alpha;
-                        }
-                        if (__any_sync(0xffffffffu, rescale)) {
-                            // rare: rescale this row's accumulator, 8 columns at a time (few live
-                            // registers).  At d = 64 the accumulator's last P*V is this chain's,
-                            // covered by the commit of this S.  At d = 128 it is the other chain's
-                            // (of the previous tile for chain 0, of this tile for chain 1): wait for
-                            // it; its completion is the current or the preceding phase of that
-                            // chain's barrier (this S's commit covers the one before).
-                            if constexpr (H == 1) {
-                                const int pc_ch = ch == 0 ? 1 : 0;
-                                const int pc_tile = ch == 0 ? sc - 1 : sc;
-                                if (ok) ok = warp_wait(&ctl->pv_done[X][pc_ch], pc_tile & 1, abort_flag, p.err,
-                                                       LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
-                                if (ok) ptx::tc_fence_after();
-                            }
-                            const float a = rescale ? alpha : 1.f;
-    #pragma unroll 1
-                            for (int c = 0; c < D / 8 && ok; ++c) {
-                                uint32_t o[8];
-                                ptx::tmem_ld8(t_lane + o_col + c * 8, o);
-                                ptx::tmem_wait_ld();
+                                    for (int e = 0; e < 16; ++e) z[e] = 0u;
+                                    ptx::tmem_st16u(t_lane + s_col + c0, z);
+                                    if (C::kSplitP) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
+                                } else {
+                                    const float* v = s + c0;
     #pragma unroll
-                                for (int e = 0; e < 8; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
-                                ptx::tmem_st8u(t_lane + o_col + c * 8, o);
-                            }
-                        }
-                        // ---- pass 2, from the registers of pass 1, one 32-key chunk at a time:
-                        // p = 2^(s * scale * log2(e) - m) (masked scores are already `sent`, which
-                        // maps to 0), row sum, 16-bit pairs written over the chunk's own S columns
-                        // (hi pairs, then lo pairs for bf16).  Chunks masked for the whole warp skip
-                        // the exponentials.
-                        // Pairs of columns go through the packed fp32x2 pipe: one FMA for the
-                        // exponent arguments, one add for the row sums and, for bf16, one
-                        // subtract for the low parts.
-                        LCA_TRACE_LANE0(trace::EV_MAX_DONE);
-                        const float neg_m = (m == -INFINITY) ? 0.f : -m;
-                        const uint64_t sl2x2 = ptx::f2_pack(sl2, sl2);
-                        const uint64_t negm2 = ptx::f2_pack(neg_m, neg_m);
-                        uint64_t acc0 = 0ull, acc1 = 0ull;  // {+0.f, +0.f}
+                                    for (int g8 = 0; g8 < 2; ++g8) {  // 8 pairs (16 keys) per store
+                                        uint32_t w[8];
+                                        uint32_t wl[8];
     #pragma unroll
-                        for (int c = 0; c < KC / 32; ++c) {
-                            if (c >= nchunks) break;
-                            const int c0 = c * 32;
-                            if (__all_sync(0xffffffffu, vis[c] == 0u)) {
-                                uint32_t z[16];
-    #pragma unroll
-                                for (int e = 0; e < 16; ++e) z[e] = 0u;
-                                ptx::tmem_st16u(t_lane + s_col + c0, z);
-                                if (C::kSplitP) ptx::tmem_st16u(t_lane + s_col + c0 + 16, z);
-                            } else {
-                                const float* v = s + c0;
-    #pragma unroll
-                                for (int g8 = 0; g8 < 2; ++g8) {  // 8 pairs (16 keys) per store
-                                    uint32_t w[8];
-                                    uint32_t wl[8];
-    #pragma unroll
-                                    for (int e = 0; e < 8; ++e) {
-                                        const uint64_t x = ptx::f2_fma(
-                                            ptx::f2_pack(v[g8 * 16 + 2 * e], v[g8 * 16 + 2 * e + 1]), sl2x2, negm2);
-                                        const float p0 = ptx::ex2(ptx::f2_lo(x)), p1 = ptx::ex2(ptx::f2_hi(x));
-                                        const uint64_t pp = ptx::f2_pack(p0, p1);
-                                        if (e & 1) acc1 = ptx::f2_add(acc1, pp); else acc0 = ptx::f2_add(acc0, pp);
-                                        if (C::kSplitP) {
-                                            w[e] = ptx::pack_bf16x2(p0, p1);
-                                            const uint64_t rest = ptx::f2_sub(
-                                                pp, ptx::f2_pack(__uint_as_float(w[e] << 16),
-                                                                 __uint_as_float(w[e] & 0xFFFF0000u)));
-                                            wl[e] = ptx::pack_bf16x2(ptx::f2_lo(rest), ptx::f2_hi(rest));
-                                        } else {
-                                            w[e] = ptx::pack_f16x2(p0, p1);
+                                        for (int e = 0; e < 8; ++e) {
+                                            const uint64_t x = ptx::f2_fma(
+                                                ptx::f2_pack(v[g8 * 16 + 2 * e], v[g8 * 16 + 2 * e + 1]), sl2x2, negm2);
+                                            xm = ptx::fmax3(xm, ptx::f2_lo(x), ptx::f2_hi(x));
+                                            float p0, p1;
+                                            uint64_t pp;
+                                            if (((C::kPolyMask >> e) & 1u) != 0u) {
+                                                pp = ptx::f2_exp2_poly(x);
+                                                p0 = ptx::f2_lo(pp);
+                                                p1 = ptx::f2_hi(pp);
+                                            } else {
+                                                p0 = ptx::ex2(ptx::f2_lo(x));
+                                                p1 = ptx::ex2(ptx::f2_hi(x));
+                                                pp = ptx::f2_pack(p0, p1);
+                                            }
+                                            if (e & 1) acc1 = ptx::f2_add(acc1, pp); else acc0 = ptx::f2_add(acc0, pp);
+                                            if (C::kSplitP) {
+                                                w[e] = ptx::pack_bf16x2(p0, p1);
+                                                const uint64_t rest = ptx::f2_sub(
+                                                    pp, ptx::f2_pack(__uint_as_float(w[e] << 16),
+                                                                     __uint_as_float(w[e] & 0xFFFF0000u)));
+                                                wl[e] = ptx::pack_bf16x2(ptx::f2_lo(rest), ptx::f2_hi(rest));
+                                            } else {
+                                                w[e] = ptx::pack_f16x2(p0, p1);
+                                            }
                                         }
+                                        ptx::tmem_st8u(t_lane + s_col + c0 + g8 * 8, w);
+                                        if (C::kSplitP) ptx::tmem_st8u(t_lane + s_col + c0 + 16 + g8 * 8, wl);
                                     }
-                                    ptx::tmem_st8u(t_lane + s_col + c0 + g8 * 8, w);
-                                    if (C::kSplitP) ptx::tmem_st8u(t_lane + s_col + c0 + 16 + g8 * 8, wl);
                                 }
                             }
+                            return xm;
+                        };
+                        uint64_t acc0 = 0ull, acc1 = 0ull;  // {+0.f, +0.f}
+                        // Fast path: once every row of the warp has a reference max, exponentiate
+                        // against it straight away; the row max is only needed if some argument
+                        // exceeds the rescale threshold (rare), and then the chunk is redone below.
+                        bool done = false;
+                        if (C::kFastExp && !__any_sync(0xffffffffu, m == -INFINITY)) {
+                            const float xm = exp_pass(m, acc0, acc1);
+                            done = !__any_sync(0xffffffffu, xm > kRescaleThreshold);
+                            if (!done) {
+                                ptx::tmem_wait_st();  // the redo rewrites the same P columns
+                                acc0 = acc1 = 0ull;
+                            }
+                        }
+                        if (!done) {
+                            // ---- masked row max
+                            float r0 = sent, r1 = sent, r2 = sent, r3 = sent;
+                            if (!neg_scale) {
+    #pragma unroll
+                                for (int c = 0; c < KC; c += 8) {
+                                    r0 = ptx::fmax3(r0, s[c + 0], s[c + 1]);
+                                    r1 = ptx::fmax3(r1, s[c + 2], s[c + 3]);
+                                    r2 = ptx::fmax3(r2, s[c + 4], s[c + 5]);
+                                    r3 = ptx::fmax3(r3, s[c + 6], s[c + 7]);
+                                }
+                            } else {
+    #pragma unroll
+                                for (int c = 0; c < KC; c += 8) {
+                                    r0 = ptx::fmin3(r0, s[c + 0], s[c + 1]);
+                                    r1 = ptx::fmin3(r1, s[c + 2], s[c + 3]);
+                                    r2 = ptx::fmin3(r2, s[c + 4], s[c + 5]);
+                                    r3 = ptx::fmin3(r3, s[c + 6], s[c + 7]);
+                                }
+                            }
+                            const float mr =
+                                neg_scale ? fminf(fminf(r0, r1), fminf(r2, r3)) : fmaxf(fmaxf(r0, r1), fmaxf(r2, r3));
+                            const float mt = (mr == sent) ? -INFINITY : mr * sl2;
+
+                            // ---- online softmax with lazy rescale (O is stable: see header)
+                            bool rescale = false;
+                            float alpha = 1.f;
+                            if (mt > m + kRescaleThreshold || (m == -INFINITY && mt > -INFINITY)) {
+                                rescale = seen && (m != -INFINITY);
+                                alpha = (m == -INFINITY) ? 0.f : ptx::ex2(m - mt);
+                                m = mt;
+                                l *= alpha;
+                            }
+                            if (__any_sync(0xffffffffu, rescale)) {
+                                // rare: rescale this row's accumulator, 8 columns at a time (few
+                                // live registers).  At d = 64 the accumulator's last P*V is this
+                                // chain's, covered by the commit of this S.  At d = 128 it is the
+                                // other chain's (of the previous tile for chain 0, of this tile for
+                                // chain 1): wait for it; its completion is the current or the
+                                // preceding phase of that chain's barrier (this S's commit covers
+                                // the one before).
+                                if constexpr (H == 1) {
+                                    const int pc_ch = ch == 0 ? 1 : 0;
+                                    const int pc_tile = ch == 0 ? sc - 1 : sc;
+                                    if (ok) ok = warp_wait(&ctl->pv_done[X][pc_ch], pc_tile & 1, abort_flag, p.err,
+                                                           LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+                                    if (ok) ptx::tc_fence_after();
+                                }
+                                const float a = rescale ? alpha : 1.f;
+    #pragma unroll 1
+                                for (int c = 0; c < D / 8 && ok; ++c) {
+                                    uint32_t o[8];
+                                    ptx::tmem_ld8(t_lane + o_col + c * 8, o);
+                                    ptx::tmem_wait_ld();
+    #pragma unroll
+                                    for (int e = 0; e < 8; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
+                                    ptx::tmem_st8u(t_lane + o_col + c * 8, o);
+                                }
+                            }
+                            LCA_TRACE_LANE0(trace::EV_MAX_DONE);
+                            exp_pass(m, acc0, acc1);
                         }
                         {
                             const uint64_t a = ptx::f2_add(acc0, acc1);

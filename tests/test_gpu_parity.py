@@ -144,6 +144,29 @@ def test_bf16_tiny_values_keep_bf16_precision(d):
     assert max_abs(to_np(lse), want_lse) <= LSE_ABS_TOL
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("d", [64, 128])
+def test_rising_scores_rescale_every_tile(d, dtype):
+    """Scores that grow along every row (keys scaled by 1 + j/8 with q.k > 0: about
+    +10 in log2 units per 128-key tile), so the row max rises by more than the
+    lazy-rescale threshold (2^8) from one key tile to the next: the accumulator is
+    rescaled on most tiles, and an exponent pass started against the previous reference
+    max has to be redone with the new one.  The log-sum-exp reaches ~80 here, so it is
+    compared relative to its magnitude (fp32 scores carry ~1e-7 relative error)."""
+    n, w, g = 1536, 400, [2, 1000]
+    q, k, v = make_inputs(53 + d, 1, 2, n, d, dtype)
+    q = q.float().abs() * 0.5 + 0.25
+    grow = 1.0 + torch.arange(n, dtype=torch.float32) / 8.0
+    k = (k.float().abs() * 0.5 + 0.25) * grow[None, None, :, None]
+    q, k = q.to(dtype), k.to(dtype)
+    scale = 1.0 / d
+    out, lse = lca.sliding_window_attention_with_lse(q.cuda(), k.cuda(), v.cuda(), w, g, scale)
+    want, want_lse = swa_oracle.sliding_window_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                                         w, g, scale)
+    assert_parity(to_np(out), want, f"rising scores d={d} {dtype}")
+    assert (np.abs(to_np(lse) - want_lse) / np.maximum(np.abs(want_lse), 1.0)).max() <= LSE_ABS_TOL
+
+
 @pytest.mark.parametrize("scale", [-0.2, 0.0, 1e-3])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_scale_edge_cases(scale, dtype):
