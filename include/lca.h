@@ -66,13 +66,15 @@ LCA_API int lca_normalize_global_tokens(const int64_t* tokens, int64_t count, in
 /*
  * Bytes of device workspace recommended for lca_swa_forward on this problem.
  * `num_unique_global` is the count after normalisation.  Host-only.
- * The workspace holds the compact global rows and the global-row partials (nothing for fp16
- * inputs without global tokens) and, for bf16 inputs, an optional fp16 copy of V: when the
- * workspace passed to lca_swa_forward is at least this size, and every value of V fits fp16
- * (exactly, or within 2^-25 for magnitudes below 2^-14 in a 128-row block whose largest
- * magnitude is at least 2^-4), P*V runs once per key tile in fp16 instead of twice with bf16 P
- * split into hi + lo.  A smaller workspace that still holds the rest is accepted and runs the
- * split form.
+ * The workspace holds the compact global rows and the global-row partials (the required
+ * part: nothing for fp16 inputs without global tokens), then an optional part: for bf16
+ * inputs an fp16 copy of V, and for every dtype one word from which the main kernel's CTAs
+ * take work units dynamically.  When the workspace passed to lca_swa_forward is at least
+ * this size, units are handed out dynamically (else round-robin), and if every value of V
+ * fits fp16 (exactly, or within 2^-25 for magnitudes below 2^-14 in a 128-row block whose
+ * largest magnitude is at least 2^-4), P*V runs once per key tile in fp16 instead of twice
+ * with bf16 P split into hi + lo.  A smaller workspace that still holds the required part is
+ * accepted and runs without the optional part.
  */
 LCA_API int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
                                    int64_t window_size, int64_t num_unique_global, int dtype, size_t* out_bytes);
@@ -95,10 +97,10 @@ LCA_API int lca_swa_workspace_size(int64_t batch, int64_t heads, int64_t seq_len
  *   global_tokens / num_global_tokens: HOST array of token indices (any order,
  *                duplicates and negative indices allowed, as in the reference)
  *   workspace    device buffer of lca_swa_workspace_size(...) bytes, 256-byte aligned
- *                (may be NULL when that size is 0; for bf16 inputs a smaller buffer that
- *                still holds the required part runs without the fp16 copy of V, and one
- *                below that returns LCA_ERR_WORKSPACE); must not be shared by calls that
- *                can run concurrently
+ *                (a smaller buffer that still holds the required part runs without the
+ *                optional part, and may be NULL when that part is empty; one below it
+ *                returns LCA_ERR_WORKSPACE); must not be shared by calls that can run
+ *                concurrently
  */
 LCA_API int lca_swa_forward(const void* q, const void* k, const void* v, float* out, float* lse, int dtype,
                     int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,

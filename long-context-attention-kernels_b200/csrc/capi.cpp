@@ -216,15 +216,18 @@ struct Layout {
     size_t off_send = 0, off_recv = 0, halo_block = 0;  // halo_block: one side, [2][bh][halo][d]
     size_t off_rowpart = 0, rowpart_bytes = 0, off_rowpart_all = 0;  // rowpart_all: two buffers
     size_t total = 0;  // bytes the forward needs
-    // Optional suffix for bf16 inputs: an fp16 copy of V [bh][n][d], of the compact global V
-    // rows [G][bh][d] and, for a sequence shard, of the received halo blocks (laid out like
+    // Optional suffix.  For bf16 inputs: an fp16 copy of V [bh][n][d], of the compact global
+    // V rows [G][bh][d] and, for a sequence shard, of the received halo blocks (laid out like
     // the receive region, V planes filled), and a word that says whether some value did not
     // convert without loss that matters (lca_convert_v16).  When none failed, P*V runs once
-    // per tile in fp16 instead of twice (bf16 P split into hi + lo).  The suffix follows
-    // every other region (for a shard: after this rank's own regions, so the exchanged
-    // regions keep their offsets).  total_fast >= total; a workspace of total_fast bytes
-    // enables it.
+    // per tile in fp16 instead of twice (bf16 P split into hi + lo).  For every dtype: the
+    // word from which the main kernel's CTAs take work units (dynamic scheduling; without
+    // it units go round-robin).  The suffix follows every other region (for a shard: after
+    // this rank's own regions, so the exchanged regions keep their offsets).
+    // total_fast >= total; a workspace of total_fast bytes enables it.
     size_t off_v16 = 0, off_vg16 = 0, off_vh16 = 0, off_v16bad = 0;
+    bool has_v16 = false;    // bf16: the suffix holds the fp16 copy of V
+    size_t off_counter = 0;  // suffix: the main kernel's work-unit counter (zeroed per launch)
     size_t total_fast = 0;
 };
 
@@ -307,8 +310,13 @@ Layout make_layout(const Problem& P) {
         }
         L.off_v16bad = off;
         off = align_up(off + sizeof(int), kAlign);
-        L.total_fast = off;
+        L.has_v16 = true;
     }
+    if (bh > 0 && P.n > 0) {
+        L.off_counter = off;
+        off = align_up(off + sizeof(unsigned int), kAlign);
+    }
+    L.total_fast = off;
     return L;
 }
 
@@ -444,7 +452,8 @@ int enqueue_convert_v16(const Problem& P, const Layout& L, const void* v, uint8_
 }
 
 int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, const void* q, const void* k,
-                 const void* v, float* out, float* lse, uint8_t* ws, cudaStream_t stream, bool v16 = false) {
+                 const void* v, float* out, float* lse, uint8_t* ws, cudaStream_t stream, bool v16 = false,
+                 bool dynamic_units = false) {
     const bool bf16 = P.dtype == LCA_DTYPE_BF16;
     const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int n = (int)P.n;
@@ -544,7 +553,15 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     const long long units = (long long)p.n_grow_units + (long long)P.bh * p.q_pairs;
     if (units > INT_MAX) return fail(LCA_ERR_UNSUPPORTED, "problem too large (%lld work units)", units);
     p.n_band_units = (int)(P.bh * p.q_pairs);
+    // key-tile steps of one unit of each kind: the longer kind is handed out first
+    const int64_t band_steps = 2 * ((P.lead() + P.window + 2 * lca::kTileRows - 1) / lca::kTileRows + p.g_tiles);
+    p.grow_first = (P.G > 0 && (int64_t)p.split_tiles >= band_steps) ? 1 : 0;
     const int grid = (int)std::min<long long>(units, g_dev_sms[dev]);
+    if (dynamic_units) {
+        p.unit_counter = reinterpret_cast<unsigned int*>(ws + L.off_counter);
+        cudaError_t me = cudaMemsetAsync(p.unit_counter, 0, sizeof(unsigned int), stream);
+        if (me != cudaSuccess) return fail_cuda(me, "unit counter reset");
+    }
     const bool timed = g_ev_before_main != nullptr && g_ev_after_main != nullptr;
     cudaError_t e;
     if (timed && (e = cudaEventRecord(g_ev_before_main, stream)) != cudaSuccess)
@@ -684,12 +701,15 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
     if ((st = check_workspace(L, workspace, workspace_bytes)) != LCA_OK) return st;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const bool v16 = L.total_fast > L.total && workspace_bytes >= L.total_fast;
+    // the optional suffix is there (a workspace that reports 0 required bytes may be NULL)
+    const bool fast = workspace != nullptr && workspace_bytes >= L.total_fast &&
+                      reinterpret_cast<uintptr_t>(workspace) % 256 == 0;
+    const bool v16 = fast && L.has_v16;
     // 1. gather the global rows, (2. fp16 copy of V), 3. band + global-row units, 4. merge
     //    the global-row splits
     if ((st = enqueue_gather(P, L, q, k, v, ws, stream)) != LCA_OK) return st;
     if (v16 && (st = enqueue_convert_v16(P, L, v, ws, stream)) != LCA_OK) return st;
-    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16)) != LCA_OK) return st;
+    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16, fast)) != LCA_OK) return st;
     return enqueue_combine_splits(P, L, out, lse, ws, stream);
 }
 
@@ -768,9 +788,12 @@ int lca_swa_shard_forward(const lca_shard_desc* desc, const void* q, const void*
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     // the compact global rows and the halos are complete here (after the exchange)
-    const bool v16 = L.total_fast > L.total && workspace_bytes >= L.total_fast;
+    // the optional suffix is there (a workspace that reports 0 required bytes may be NULL)
+    const bool fast = workspace != nullptr && workspace_bytes >= L.total_fast &&
+                      reinterpret_cast<uintptr_t>(workspace) % 256 == 0;
+    const bool v16 = fast && L.has_v16;
     if (v16 && (st = enqueue_convert_v16(P, L, v, ws, stream)) != LCA_OK) return st;
-    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16)) != LCA_OK) return st;
+    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16, fast)) != LCA_OK) return st;
     return enqueue_combine_splits(P, L, out, lse, ws, stream);
 }
 

@@ -82,6 +82,7 @@ constexpr int kWgThreads = 128;
 constexpr int kTmemCols = 512;
 constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 bytes: one swizzle panel
 constexpr int kMaxSlots = 8;            // K / V ring slots (barrier pairs in Ctl)
+constexpr int kUnitRing = 4;            // work-unit indices the producer publishes ahead
 constexpr float kLn2 = 0.6931471805599453f;
 // The running max used for exponentiation is only raised when a new score exceeds it by
 // more than this many powers of two; results are exact either way because l and O are
@@ -176,6 +177,9 @@ struct Ctl {
     uint64_t o_full[2];
     uint64_t o_free[2];
     uint64_t mma_drained[2];
+    uint64_t unit_full[kUnitRing];   // the producer published the slot's unit index
+    uint64_t unit_empty[kUnitRing];  // every other role has read it
+    int unit_ring[kUnitRing];
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -203,12 +207,16 @@ struct Tile {
     bool mem[2];      // query tile A / B uses this key tile
 };
 
+// Units [0, n_grow_units) are global-row units and the rest band units when grow_first,
+// else band units come first: the longer kind goes first, so the short ones fill the tail.
 __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
     Unit un;
-    if (u < p.n_grow_units) {
+    const bool grow = p.grow_first ? (u < p.n_grow_units) : (u >= p.n_band_units);
+    const int t = grow ? (p.grow_first ? u : u - p.n_band_units) : (p.grow_first ? u - p.n_grow_units : u);
+    if (grow) {
         un.grow = true;
-        un.split = u % p.n_splits;
-        const int rest = u / p.n_splits;
+        un.split = t % p.n_splits;
+        const int rest = t / p.n_splits;
         const int gt = rest % p.g_tiles;
         un.bh = rest / p.g_tiles;
         un.qrow[0] = un.qrow[1] = gt * BM;
@@ -221,7 +229,6 @@ __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
     } else {
         un.grow = false;
         un.split = un.k0 = 0;
-        const int t = u - p.n_grow_units;
         const int pair = t % p.q_pairs;
         un.bh = t / p.q_pairs;
         const int q0 = pair * 2 * BM;
@@ -342,6 +349,10 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
         }
         ptx::mbar_init(&ctl->mma_drained[0], 1);
         ptx::mbar_init(&ctl->mma_drained[1], 1);
+        for (int i = 0; i < kUnitRing; ++i) {
+            ptx::mbar_init(&ctl->unit_full[i], 1);
+            ptx::mbar_init(&ctl->unit_empty[i], 2 + C::kSoftmaxWarps);  // MMA issuers, softmax warps
+        }
         ctl->abort_flag = 0;
         ptx::fence_mbar_init();
     }
@@ -373,7 +384,22 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                 int L = 0;   // K/V loads issued
                 int qn = 0;  // Q loads issued per tile buffer
                 bool ok = true;
-                for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                for (int k = 0; ok; ++k) {
+                    // Next unit: the CTA's own first one, then one from the launch-wide counter
+                    // (dynamic: the CTAs that finish first take more), or round-robin without it.
+                    // Published through the unit ring; an index >= n_units ends every role.
+                    int u = blockIdx.x + k * gridDim.x;
+                    if (k > 0 && p.unit_counter != nullptr) u = (int)gridDim.x + (int)atomicAdd(p.unit_counter, 1u);
+                    if (u > n_units) u = n_units;
+                    const int us = k % kUnitRing;
+                    if (k >= kUnitRing && !ptx::mbar_wait(&ctl->unit_empty[us], ((k / kUnitRing) - 1) & 1, abort_flag,
+                                                           p.err, LCA_DEVERR_TIMEOUT_PRODUCER, tmo)) {
+                        ok = false;
+                        break;
+                    }
+                    ctl->unit_ring[us] = u;
+                    ptx::mbar_arrive(&ctl->unit_full[us]);
+                    if (u >= n_units) break;
                     const Unit un = decode_unit(p, u);
                     const CUtensorMap* mq = un.grow ? &tm_qg : &tm_q;
                     for (int x = 0; x < 2 && ok; ++x) {
@@ -512,7 +538,12 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
                     }
                 };
 
-                for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                for (int k = 0; ok; ++k) {
+                    const int us = k % kUnitRing;
+                    if (!W(&ctl->unit_full[us], k / kUnitRing)) break;
+                    const int u = *reinterpret_cast<volatile int*>(&ctl->unit_ring[us]);
+                    ptx::mbar_arrive(&ctl->unit_empty[us]);
+                    if (u >= n_units) break;
                     const Unit un = decode_unit(p, u);
                     const bool act = X ? un.active[1] : un.active[0];
                     if (!W(&ctl->q_full[X], qn)) break;
@@ -641,9 +672,17 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
         const bool neg_scale = sl2 < 0.f;
         const float sent = neg_scale ? INFINITY : -INFINITY;
         int sc = 0, oc = 0;
-        bool ok = true;  // warp-uniform; on failure the warp keeps the barrier schedule but skips work
+        bool ok = true;  // warp-uniform; after a failed wait the warp skips work and leaves at the next unit
 
-        for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        for (int k = 0;; ++k) {
+            const int us = k % kUnitRing;
+            if (ok) ok = warp_wait(&ctl->unit_full[us], (k / kUnitRing) & 1, abort_flag, p.err,
+                                   LCA_DEVERR_TIMEOUT_SOFTMAX, tmo);
+            if (!ok) break;
+            const int u = *reinterpret_cast<volatile int*>(&ctl->unit_ring[us]);
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&ctl->unit_empty[us]);
+            if (u >= n_units) break;
             const Unit un = decode_unit(p, u);
             LCA_TRACE_LANE0(trace::EV_UNIT_DECODED);
             const bool active_x = X ? un.active[1] : un.active[0];

@@ -68,8 +68,10 @@ struct MainParams {
     int g_tiles;      // ceil(G / 128)
     int n_splits;     // key splits per (bh, global tile)
     int split_tiles;  // key tiles per split
-    int n_grow_units; // bh * g_tiles * n_splits global-row units (scheduled first)
+    int n_grow_units; // bh * g_tiles * n_splits global-row units
     int n_band_units; // bh * q_pairs band units
+    int grow_first;   // global-row units take the low unit indices (they are the longer kind)
+    unsigned int* unit_counter;  // zeroed word handing out units dynamically, or nullptr (round-robin)
     int q_pairs;      // ceil(q_tiles / 2): band units per (batch, head)
     float scale_log2; // scale * log2(e)
     const int* gidx;  // [G] sorted absolute global indices
