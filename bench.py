@@ -104,13 +104,20 @@ class ClockSampler:
         self._stop = threading.Event()
         self._t = None
 
+    def sample_now(self):
+        """One sample from the calling thread (the launch loop can starve the polling thread of
+        the interpreter lock; called right after the loop, while queued steps still run)."""
+        if not self.ok:
+            return
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+        except Exception:  # noqa: BLE001
+            pass
+
     def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
-            except Exception:  # noqa: BLE001
-                pass
+            self.sample_now()
             time.sleep(0.002)
 
     def start(self):
@@ -251,6 +258,7 @@ def run_ours(args):
         cabi.lib.lca_set_timing_events(ev_b[i].cuda_event, ev_a[i].cuda_event)
         out = fwd()
     stop.record()
+    clocks.sample_now()
     torch.cuda.synchronize()
     clocks.stop()
     cabi.lib.lca_set_timing_events(None, None)
@@ -379,6 +387,7 @@ def run_sequence(args):
     for _ in range(args.steps):
         plan.replay()
     stop.record()
+    clocks.sample_now()
     torch.cuda.synchronize()
     clocks.stop()
     ms = start.elapsed_time(stop) / args.steps
