@@ -8,7 +8,10 @@
 //   1. lca_gather_globals : copies the G global rows of Q, K, V into one compact
 //                           [G][3][bh][d] buffer (TMA reads rows >= G as zeros) and
 //                           writes the sorted index list.
-//   2. lca_swa_main       : persistent, one CTA per SM, looping over work units:
+//   2. lca_swa_main       : persistent, one CTA per SM, looping over work units (after its
+//                           first, each CTA takes the next index from a launch-wide counter
+//                           when the workspace has one, else round-robin; the TMA warp
+//                           publishes it to the other roles through a shared-memory ring):
 //        band unit      : two adjacent 128-row query tiles A, B of one (batch, head).
 //                         Key tiles: the band [q0 - w, q0 + 255 + w] in 128-key tiles
 //                         starting at q0 - lead (lead = w, or w rounded up to 128 for a
