@@ -4,8 +4,10 @@
 Default workload: B=1 x 16 heads, n=65536, d=64, w=256, 65 global tokens (64 drawn by
 seed + index 0), bf16, scale 1/8 -- the shape the headline metric is quoted on.  One
 "step" is one forward over the resident inputs.  With N GPUs (torchrun, one rank per
-GPU) every rank processes its own 16-head shard of an N*16-head job (heads are
-independent: no collective on the data path), so per-GPU work is fixed ("weak").
+GPU) the 16 heads are split over the ranks (16/N each; heads are independent, so there
+is no collective on the data path) and the whole job stays fixed ("strong").  The same
+line also carries `sequence_128k`: the 128K-token, d=128 workload cut into N contiguous
+sequence shards (halo and global-row exchange by NVLink peer stores), timed the same way.
 
 Prints one JSON line (rank 0).  `value` is tokens/s (query rows x heads per second,
 whole job); `useful_tflops` counts 4*d FLOPs per true mask entry.  `--impl reference`
@@ -33,6 +35,17 @@ from long_context_attention.workloads import WORKLOADS  # noqa: E402
 
 METRIC = "tokens/s & useful TFLOP/s, n=64K w=256 d=64 bf16, 1/2/4/8 B200 vs roofline"
 UNIT = "tokens/s"
+SEQUENCE_WORKLOAD = "context_128k_d128"
+
+
+def metric_of(w) -> str:
+    """The headline metric string for the 64K workload; the same form for the others."""
+    if w.name == "many_globals_64k":
+        return METRIC
+    n = f"{w.seq_len // 1024}K" if w.seq_len % 1024 == 0 else str(w.seq_len)
+    split = "sequence-sharded over" if w.name == SEQUENCE_WORKLOAD else ""
+    return (f"tokens/s & useful TFLOP/s, n={n} w={w.window} d={w.head_dim} {w.dtype}, "
+            f"{split + ' ' if split else ''}1/2/4/8 B200 vs roofline")
 
 
 def parse_args(argv=None):
@@ -53,10 +66,16 @@ def parse_args(argv=None):
     ap.add_argument("--parallel", choices=["heads", "sequence"], default=None,
                     help="multi-GPU split: independent head shards (default) or contiguous sequence shards "
                          "(default for context_128k_d128)")
+    ap.add_argument("--no-sequence", action="store_true",
+                    help="skip the sequence-sharded 128K measurement added to the head-sharded line")
+    ap.add_argument("--cpu-dense-all", action="store_true",
+                    help="also time the dense reference definition on the 96-head 4K workload (~40 s)")
     return ap.parse_args(argv)
 
 
 def load_peaks():
+    """(bf16 TFLOP/s, HBM GB/s, source): the pool's measured burst figures, else the
+    fallback ones."""
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
@@ -64,6 +83,27 @@ def load_peaks():
         return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return 1590.0, 6650.0, "fallback"
+
+
+def roofline(flops: float, io_bytes: float, kernel_ms: float, traffic, kernel: str) -> dict:
+    """Roofline of the main kernel: the slower of the tensor-pipe time (useful FLOPs at the
+    bf16 peak) and the HBM time (Q/K/V/O bytes at the copy bandwidth) is the bound;
+    `frac` is the roofline time over the measured kernel time.  Both pipes' fractions are
+    kept as extra fields."""
+    peak_tf, peak_gbs, src = load_peaks()
+    sec = kernel_ms * 1e-3
+    t_tensor = flops / (peak_tf * 1e12)
+    t_hbm = io_bytes / (peak_gbs * 1e9)
+    tf = flops / sec / 1e12
+    gbs = io_bytes / sec / 1e9
+    hbm_bound = t_hbm > t_tensor
+    return {"bound": "hbm" if hbm_bound else "tensor",
+            "achieved": gbs if hbm_bound else tf, "peak": peak_gbs if hbm_bound else peak_tf,
+            "unit": "GB/s" if hbm_bound else "TFLOP/s", "frac": max(t_tensor, t_hbm) / sec,
+            "traffic": traffic, "kernel": kernel, "kernel_ms": kernel_ms, "peak_source": src + " (burst)",
+            "roofline_ms": max(t_tensor, t_hbm) * 1e3,
+            "tensor_achieved_tflops": tf, "tensor_peak_tflops": peak_tf, "tensor_frac": tf / peak_tf,
+            "hbm_achieved_gbs": gbs, "hbm_peak_gbs": peak_gbs, "hbm_frac": gbs / peak_gbs}
 
 
 def load_traffic(workload: str):
@@ -145,9 +185,12 @@ def dist_setup(args):
     return world, rank, local
 
 
-def cpu_baseline(w, q, k, v, budget_s: float):
-    """The reference's dense-mask algorithm (oracle port, fp32 like the reference) on a
-    bounded sample of query rows of head 0, all host threads."""
+def cpu_baseline(w, q, k, v, budget_s: float, dense_all: bool = False):
+    """The reference's dense-mask algorithm on the host cores, on a bounded sample: the
+    oracle port (fp32 numpy, all host threads) on random query rows of head 0 of `w`,
+    plus the dense torch definition of the reference (`_reference_sliding_window_attention`,
+    python/long_context_attention/__init__.py:24-53) run whole on the small workloads where
+    its n x n scores fit in host memory."""
     from oracle import swa_oracle
 
     qs, ks, vs = (t[:1, :1].float().cpu().numpy() for t in (q, k, v))
@@ -162,9 +205,46 @@ def cpu_baseline(w, q, k, v, budget_s: float):
     t0 = time.perf_counter()
     swa_oracle.sliding_window_attention(qs, ks, vs, w.window, g, w.scale, rows=rows, dtype=np.float32, block_rows=128)
     dt = time.perf_counter() - t0
-    return {"value": rows.size / dt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{rows.size} random query rows of head 0 of {w.name} (dense-mask fp32 numpy, "
-                      f"{dt:.1f} s); value = rows/s"}
+    out = {"value": rows.size / dt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+           "sample": f"{rows.size} random query rows of head 0 of {w.name} (dense-mask fp32 numpy, "
+                     f"{dt:.1f} s); value = rows/s"}
+    out["dense_reference"] = dense_reference_small(dense_all)
+    return out
+
+
+def dense_reference_small(include_4k: bool) -> dict:
+    """Whole-workload timings of the reference's dense torch definition on the host cores
+    (tokens/s): the 2K plumbing case and the single 16K head, and the 96-head 4K batch on
+    request."""
+    import long_context_attention as lca
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    names = ["cpu_plumbing_2k", "single_head_16k"] + (["longformer_base_4k"] if include_4k else [])
+    res = {"threads": torch.get_num_threads(), "impl": "_reference_sliding_window_attention (torch, dense mask)"}
+    for name in names:
+        w = WORKLOADS[name]
+        q, k, v = w.inputs()
+        t0 = time.perf_counter()
+        lca._reference_sliding_window_attention(q, k, v, w.window, w.global_tokens(), w.scale)
+        dt = time.perf_counter() - t0
+        res[name] = {"tokens_per_s": w.tokens() / dt, "seconds": dt}
+    return res
+
+
+def config_of(w, world: int, parallelism: str) -> dict:
+    """The `config` object of a line; both arms print the same keys for one workload."""
+    return {"workload": w.name, "batch": w.batch, "heads": w.heads, "seq_len": w.seq_len, "head_dim": w.head_dim,
+            "window": w.window, "num_global": len(w.global_tokens()), "dtype": w.dtype,
+            "parallelism": parallelism, "n_gpus": world,
+            "l2": "inputs larger than L2 (Q/K/V/O: %.0f MB)" % (w.io_bytes() / 1e6)}
+
+
+def launches_per_forward(w, fast: bool = True) -> int:
+    """Kernels of one lca_swa_forward: gather and merge with global tokens, the main
+    kernel, and for bf16 the fp16 copy of V and the second main-kernel variant (one of
+    the two returns at once)."""
+    g = len(w.global_tokens()) > 0
+    return 1 + (2 if g else 0) + (2 if (w.dtype == "bf16" and fast) else 0)
 
 
 def run_reference(args):
@@ -194,17 +274,26 @@ def run_reference(args):
     value = rows_per_step * args.steps / dt
     sample = (f"{rows_per_step} random query rows of one head per step (dense Longformer-mask fp32, "
               f"numpy oracle port of the reference's _reference_sliding_window_attention)")
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+    parallel = "sequence" if w.name == SEQUENCE_WORKLOAD else "heads"
+    line = {"impl": "reference", "metric": metric_of(w), "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": w.name, "seq_len": w.seq_len, "head_dim": w.head_dim,
-                                            "window": w.window, "num_global": len(g)},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": config_of(w, args.gpus, f"{parallel}-sharded x{args.gpus} (reference: host cores)"),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "gpu_launches": 0}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _max_over_ranks(pg, dev, values):
+    if pg is None:
+        return [float(x) for x in values]
+    t = torch.tensor([float(x) for x in values], device=dev, dtype=torch.float64)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
 
 
 def run_ours(args):
@@ -218,17 +307,21 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = dist
+    import dataclasses
+
     import long_context_attention as lca
     from long_context_attention import _native
+    from long_context_attention.distributed import head_shard
+    from long_context_attention.host_pipeline import sliding_window_attention_from_host
+    from long_context_attention.workloads import useful_scores
 
-    base = WORKLOADS[args.workload]
-    # rank r owns heads [r*H, (r+1)*H) of an N*H-head job; its inputs are the workload's
-    # seeded tensors with the seed offset by the rank
-    import dataclasses
-    w = dataclasses.replace(base, seed=base.seed + rank)
+    w = WORKLOADS[args.workload]
     if args.heads is not None:
         w = dataclasses.replace(w, heads=args.heads)
-    q, k, v = w.inputs(device=dev)
+    # rank r computes heads head_shard(H, N, r) of the one seeded job
+    hs = head_shard(w.heads, world, rank)
+    h_loc = hs.stop - hs.start
+    q, k, v = w.inputs(device=dev, heads_slice=hs)
     g = w.global_tokens()
     cabi = _native.cabi()
 
@@ -255,7 +348,8 @@ def run_ours(args):
     clocks.start()
     start.record()
     for i in range(args.steps):
-        cabi.lib.lca_set_timing_events(ev_b[i].cuda_event, ev_a[i].cuda_event)
+        if h_loc:
+            cabi.lib.lca_set_timing_events(ev_b[i].cuda_event, ev_a[i].cuda_event)
         out = fwd()
     stop.record()
     clocks.sample_now()
@@ -265,73 +359,74 @@ def run_ours(args):
     if pg is not None:
         pg.barrier()
     ms = start.elapsed_time(stop) / args.steps
-    main_ms = statistics.mean(ev_b[i].elapsed_time(ev_a[i]) for i in range(args.steps))
+    main_ms = statistics.mean(ev_b[i].elapsed_time(ev_a[i]) for i in range(args.steps)) if h_loc else 0.0
     assert lca.device_error() == 0
     del out
 
-    # ---- end to end through the public API with host buffers: pinned H2D of the step's
-    # inputs, the forward, D2H of the output
+    # ---- end to end through the public host-buffer entry point: pinned H2D of the step's
+    # inputs, the forward, D2H of the output, pipelined over head chunks
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
     oh = torch.empty(q.shape, dtype=torch.float32).pin_memory()
-    qd, kd, vd = (torch.empty_like(t) for t in (q, k, v))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     def e2e_step():
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        o = lca.sliding_window_attention(qd, kd, vd, w.window, g, w.scale)
-        oh.copy_(o, non_blocking=True)
+        sliding_window_attention_from_host(qh, kh, vh, w.window, g, w.scale, out=oh)
 
     e2e_step()
     torch.cuda.synchronize()
     if pg is not None:
         pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.e2e_steps):
         e2e_step()
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in (q, k, v))
+    d2h = oh.numel() * 4
+    del qh, kh, vh, oh
 
-    if pg is not None:
-        t = torch.tensor([ms, e2e_ms, main_ms], device=dev, dtype=torch.float64)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms, e2e_ms, main_ms = (float(x) for x in t.tolist())
+    per_head = useful_scores(w.seq_len, w.window, g) * 4 * w.head_dim * w.batch
+    flops_rank = per_head * h_loc
+    io_rank = w.io_bytes() // w.heads * h_loc
+    ms, e2e_ms, main_ms, flops_max, io_max = _max_over_ranks(pg, dev, [ms, e2e_ms, main_ms, flops_rank, io_rank])
+    h2d_all, d2h_all = (h2d * world, d2h * world) if pg is None else _sum_over_ranks(pg, dev, [h2d, d2h])
+    del q, k, v
 
-    tokens = w.tokens() * world
-    value = tokens / (ms * 1e-3)
-    flops_rank = w.useful_flops()
-    peak_tf, peak_gbs, peak_src = load_peaks()
-    achieved_tf = flops_rank / (main_ms * 1e-3) / 1e12
-    line = None
+    sequence = None
+    if not args.no_sequence and w.name != SEQUENCE_WORKLOAD:
+        sequence = measure_sequence(WORKLOADS[SEQUENCE_WORKLOAD], world, rank, local, dev, pg,
+                                    steps=min(args.steps, 200), warmup=max(args.warmup, 3), exchange=args.exchange,
+                                    e2e_steps=0, cpu=False)
+
+    tokens = w.tokens()
+    traffic = load_traffic(w.name)
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(w, q, k, v, args.cpu_budget_s)
+            cpu = cpu_baseline(w, *w.inputs(heads_slice=slice(0, 1)), args.cpu_budget_s, args.cpu_dense_all)
+        rf = roofline(flops_max, io_max, main_ms,
+                      traffic * io_max / w.io_bytes() if traffic is not None else None, "lca_swa_main")
+        rf["note"] = ("largest head shard's useful FLOPs and Q/K/V/O bytes over the max-over-ranks main-kernel "
+                      "time" if world > 1 else "useful FLOPs and Q/K/V/O bytes over the main-kernel time")
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16" if w.dtype == "bf16" else w.dtype, "data": "synthetic",
-            "useful_tflops": flops_rank * world / (ms * 1e-3) / 1e12,
-            "config": {"workload": w.name, "batch": w.batch, "heads_per_gpu": w.heads, "seq_len": w.seq_len,
-                       "head_dim": w.head_dim, "window": w.window, "num_global": len(g),
-                       "tokens_per_gpu_step": w.tokens(), "parallelism": f"head-sharded x{world}",
-                       "l2": "inputs larger than L2 (Q/K/V/O resident: %.0f MB)" % (w.io_bytes() / 1e6)},
-            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved_tf / peak_tf, "traffic": load_traffic(w.name),
-                         "kernel": "lca_swa_main", "kernel_ms": main_ms, "peak_source": peak_src,
-                         "hbm_achieved_gbs": w.io_bytes() / (main_ms * 1e-3) / 1e9, "hbm_peak_gbs": peak_gbs,
-                         "hbm_frac": w.io_bytes() / (main_ms * 1e-3) / 1e9 / peak_gbs},
+            "metric": metric_of(w), "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+            "useful_tflops": w.useful_flops() / (ms * 1e-3) / 1e12,
+            "config": config_of(w, world, f"head-sharded x{world} ({w.heads // world if world <= w.heads else 1}"
+                                          f" heads per GPU)"),
+            "roofline": rf,
             "cpu_baseline": cpu,
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)),
-                    "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": e2e_ms},
-            # main kernel; gather and merge with global tokens; for bf16 the fp16 copy of V
-            # and the second main-kernel variant (one of the two returns at once)
-            "gpu_launches": args.steps * (1 + (2 if g else 0) + (2 if w.dtype == "bf16" else 0)),
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d_all,
+                    "d2h_bytes_per_step": d2h_all, "ms_per_step": e2e_ms,
+                    "path": "sliding_window_attention_from_host (pinned host buffers, head chunks pipelined "
+                            "over copy and compute streams)"},
+            "gpu_launches": args.steps * launches_per_forward(w),
             "clocks": clocks.report(),
         }
+        if sequence is not None:
+            line["sequence_128k"] = sequence
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
@@ -339,61 +434,59 @@ def run_ours(args):
     return 0
 
 
-def run_sequence(args):
+def _sum_over_ranks(pg, dev, values):
+    t = torch.tensor([float(x) for x in values], device=dev, dtype=torch.float64)
+    pg.all_reduce(t)
+    return [int(x) for x in t.tolist()]
+
+
+def measure_sequence(w, world, rank, local, dev, pg, steps, warmup, exchange, e2e_steps, cpu, heads=None,
+                     cpu_budget_s=10.0):
     """One sequence cut into contiguous shards, one per rank (strong scaling: the whole
     job is fixed).  A step is the full sharded forward on every rank -- prepare, the
-    point-to-point exchange (global rows, halos), the shard kernels, the global-row
-    partial all-gather and the merge -- replayed from one CUDA graph per rank; the step
-    time is the max over ranks."""
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    import datetime
-
-    import torch.distributed as dist
+    exchange of global rows and halos, the shard kernels, the exchange of the global-row
+    partials and their merge -- replayed from one CUDA graph per rank; the step time is
+    the max over ranks.  Returns the measurement as a dict (rank 0; None elsewhere)."""
+    import dataclasses
 
     import long_context_attention as lca
     from long_context_attention import _native
     from long_context_attention.distributed import ShardedAttention, shard_bounds
     from long_context_attention.workloads import useful_scores_shard
 
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    w = WORKLOADS[args.workload]
-    if args.heads is not None:
-        import dataclasses
-        w = dataclasses.replace(w, heads=args.heads)
+    if heads is not None:
+        w = dataclasses.replace(w, heads=heads)
     g = w.global_tokens()
     off, ln = shard_bounds(w.seq_len, world)[rank]
     qf, kf, vf = w.inputs()
     q, k, v = (t[:, :, off:off + ln].contiguous().to(dev) for t in (qf, kf, vf))
-    cpu_inputs = (qf, kf, vf) if (rank == 0 and world == 1) else None
+    cpu_inputs = (qf[:, :1], kf[:, :1], vf[:, :1]) if (cpu and rank == 0 and world == 1) else None
     del qf, kf, vf
     cabi = _native.cabi()
     plan = ShardedAttention(w.batch, w.heads, w.seq_len, w.head_dim, w.window, g, w.scale, w.torch_dtype, device=dev,
-                            exchange=args.exchange)
-    plan.capture(q, k, v, warmup=max(args.warmup, 3))
-    for _ in range(max(args.warmup, 3)):
+                            exchange=exchange)
+    plan.capture(q, k, v, warmup=warmup)
+    for _ in range(warmup):
         plan.replay()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
-    if world > 1:
-        dist.barrier()
+    if pg is not None:
+        pg.barrier()
     torch.cuda.synchronize()
     clocks.start()
     start.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         plan.replay()
     stop.record()
     clocks.sample_now()
     torch.cuda.synchronize()
     clocks.stop()
-    ms = start.elapsed_time(stop) / args.steps
+    ms = start.elapsed_time(stop) / steps
 
     # main-kernel time from eager calls of the same plan (events recorded around the launch)
-    k_steps = min(args.steps, 20)
+    k_steps = min(steps, 20)
     ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(k_steps)]
     ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(k_steps)]
     for e in ev_b + ev_a:  # torch's events count as recorded only after one record()
@@ -404,80 +497,103 @@ def run_sequence(args):
     cabi.lib.lca_set_timing_events(None, None)
     torch.cuda.synchronize()
     main_ms = statistics.mean(ev_b[i].elapsed_time(ev_a[i]) for i in range(k_steps))
-    assert lca.device_error() == 0
+    plan.raise_on_device_error()
 
-    # end to end: pinned H2D of this rank's shard into the plan's inputs, the graph, D2H
-    # of its rows
-    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
-    oh = torch.empty(plan.out.shape, dtype=torch.float32).pin_memory()
+    e2e_ms = 0.0
+    h2d = d2h = 0
+    if e2e_steps > 0:
+        # pinned H2D of this rank's shard into the plan's inputs, the graph, D2H of its rows
+        qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+        oh = torch.empty(plan.out.shape, dtype=torch.float32).pin_memory()
 
-    def e2e_step():
-        q.copy_(qh, non_blocking=True)
-        k.copy_(kh, non_blocking=True)
-        v.copy_(vh, non_blocking=True)
-        oh.copy_(plan.replay(), non_blocking=True)
+        def e2e_step():
+            q.copy_(qh, non_blocking=True)
+            k.copy_(kh, non_blocking=True)
+            v.copy_(vh, non_blocking=True)
+            oh.copy_(plan.replay(), non_blocking=True)
 
-    e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.e2e_steps):
         e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+        torch.cuda.synchronize()
+        if pg is not None:
+            pg.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        h2d = sum(t.numel() * t.element_size() for t in (q, k, v)) * world
+        d2h = oh.numel() * 4 * world
 
     flops_rank = 4 * w.head_dim * w.batch * w.heads * useful_scores_shard(w.seq_len, w.window, g, off, ln)
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms, main_ms, float(flops_rank)], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, main_ms, flops_max = (float(x) for x in t.tolist())
-    else:
-        flops_max = flops_rank
-    tokens = w.tokens()
-    # DRAM bytes of one whole-sequence launch (ncu, profiles/traffic.json), split evenly over
-    # the shards (the per-shard band work is uniform)
-    full_traffic = load_traffic(w.name)
-    shard_traffic = full_traffic / world if full_traffic is not None else None
-    peak_tf, peak_gbs, peak_src = load_peaks()
-    achieved_tf = flops_max / (main_ms * 1e-3) / 1e12
-    if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(w, *cpu_inputs, args.cpu_budget_s)
-        shard_io = w.io_bytes() / world
-        line = {
-            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
-            "useful_tflops": w.useful_flops() / (ms * 1e-3) / 1e12,
-            "config": {"workload": w.name, "batch": w.batch, "heads": w.heads, "seq_len": w.seq_len,
-                       "head_dim": w.head_dim, "window": w.window, "num_global": len(g),
-                       "tokens_per_gpu_step": ln * w.batch * w.heads,
-                       "parallelism": f"sequence-sharded x{world}", "cuda_graph": True,
-                       "exchange": plan.exchange,
-                       "l2": "inputs larger than L2 (shard Q/K/V/O resident: %.0f MB)" % (shard_io / 1e6)},
-            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved_tf / peak_tf, "traffic": shard_traffic, "kernel": "lca_swa_main",
-                         "kernel_ms": main_ms, "peak_source": peak_src,
-                         "note": "largest shard's useful FLOPs / max-over-ranks main-kernel time"},
-            "cpu_baseline": cpu,
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)) * world,
-                    "d2h_bytes_per_step": oh.numel() * 4 * world, "ms_per_step": e2e_ms},
-            # main, halo pack (2+ shards), the two peer puts and the peer merge (peer exchange);
-            # with global tokens also gather, local merge (and the final merge over NCCL); for
-            # bf16 the fp16 copy of V and the second main-kernel variant
-            "gpu_launches": args.steps * (
-                ((5 + (2 if g else 0)) if plan.exchange == "peer" else ((2 if world > 1 else 1) + (3 if g else 0)))
-                + (2 if w.dtype == "bf16" else 0)),
-            "clocks": clocks.report(),
-        }
-        print(json.dumps(line), flush=True)
+    io_rank = w.io_bytes() * ln // w.seq_len
+    ms, e2e_ms, main_ms, flops_max, io_max = _max_over_ranks(pg, dev, [ms, e2e_ms, main_ms, flops_rank, io_rank])
+    # kernels of one step: gather (global tokens), halo pack (2+ shards), the fp16 copy of V and
+    # the second main-kernel variant (bf16), the main kernel, the split merge (global tokens),
+    # then the peer exchange's two copy kernels and its merge, or the final merge alone
+    g1 = 1 if g else 0
+    halo = 1 if (world > 1 and w.window > 0) else 0
+    main = 3 if w.dtype == "bf16" else 1
+    per_step = g1 + halo + main + g1 + (3 if plan.exchange == "peer" else g1)
+    exchange_used = plan.exchange
     plan.release()
+    del q, k, v
+    if rank != 0:
+        return None
+    full_traffic = load_traffic(w.name)
+    res = {
+        "workload": w.name, "metric": metric_of(w), "value": w.tokens() / (ms * 1e-3), "unit": UNIT,
+        "ms_per_step": ms, "n_gpus": world, "steps": steps, "scaling": "strong",
+        "useful_tflops": w.useful_flops() / (ms * 1e-3) / 1e12,
+        "config": config_of(w, world, f"sequence-sharded x{world}") | {"cuda_graph": True, "exchange": exchange_used,
+                                                                          "tokens_per_gpu_step": ln * w.batch * w.heads},
+        "main_kernel_ms": main_ms,
+        "roofline": roofline(flops_max, io_max, main_ms,
+                             full_traffic * ln / w.seq_len if full_traffic is not None else None, "lca_swa_main")
+                    | {"note": "largest shard's useful FLOPs and Q/K/V/O bytes over the max-over-ranks main-kernel "
+                               "time"},
+        "gpu_launches": steps * per_step,
+        "clocks": clocks.report(),
+    }
+    if e2e_steps > 0:
+        res["e2e"] = {"value": w.tokens() / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                      "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+    if cpu_inputs is not None:
+        res["cpu_baseline"] = cpu_baseline(w, *cpu_inputs, cpu_budget_s)
+    return res
+
+
+def run_sequence(args):
+    """The sequence-sharded workload as the line's headline (``--workload context_128k_d128``)."""
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import datetime
+
+    import torch.distributed as dist
+
+    pg = None
     if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    w = WORKLOADS[args.workload]
+    res = measure_sequence(w, world, rank, local, dev, pg, steps=args.steps, warmup=max(args.warmup, 3),
+                           exchange=args.exchange, e2e_steps=args.e2e_steps, cpu=not args.no_cpu_baseline,
+                           heads=args.heads, cpu_budget_s=args.cpu_budget_s)
+    if rank == 0:
+        line = {"metric": res.pop("metric"), "value": res.pop("value"), "unit": res.pop("unit"), "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res.pop("ms_per_step"),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
+                "data": "synthetic"}
+        res.pop("n_gpus")
+        res.pop("steps")
+        res.pop("scaling")
+        res.pop("workload")
+        line.update(res)
+        line.setdefault("cpu_baseline", None)
+        print(json.dumps(line), flush=True)
+    if pg is not None:
         dist.barrier()
         dist.destroy_process_group()
     return 0

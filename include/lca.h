@@ -3,9 +3,11 @@
  *
  * Plain C: pointers, sizes and int status codes only.  Device pointers are CUDA device
  * memory on the current device; `stream` is a cudaStream_t passed as void* (NULL = the
- * legacy default stream).  Nothing here allocates device memory: outputs and the
- * workspace are owned by the caller.  Every entry point is thread-safe; work is enqueued
- * asynchronously on `stream` and no call synchronises unless its comment says so.
+ * legacy default stream).  The compute entry points allocate no device memory: outputs
+ * and the workspace are owned by the caller (lca_peer_alloc is the one call that
+ * allocates, on request, for the peer-memory exchange).  Every entry point is
+ * thread-safe; work is enqueued asynchronously on `stream` and no call synchronises
+ * unless its comment says so.
  *
  * Semantics follow the reference's dense Longformer-mask definition
  * (python/long_context_attention/__init__.py:24-53): key j is visible to query i iff
@@ -39,6 +41,18 @@ enum {
     LCA_ERR_WORKSPACE = 4,        /* workspace too small or misaligned */
     LCA_ERR_CUDA = 5,             /* a CUDA runtime/driver call or launch failed */
     LCA_ERR_DEVICE = 6            /* a kernel reported a device-side error (bounded wait gave up) */
+};
+
+/* Values of the device-side error word (lca_device_error): which bounded wait of a
+ * kernel gave up first.  A kernel whose wait gives up stops its own work and returns, so
+ * the results of that call (and, for the peer exchange, of that step) are invalid. */
+enum {
+    LCA_DEVERR_NONE = 0,
+    LCA_DEVERR_TIMEOUT_PRODUCER = 1, /* main kernel: the TMA producer waited for a free slot */
+    LCA_DEVERR_TIMEOUT_MMA = 2,      /* main kernel: an MMA issuer waited for data or P */
+    LCA_DEVERR_TIMEOUT_SOFTMAX = 3,  /* main kernel: a softmax warp waited for S or O */
+    LCA_DEVERR_TIMEOUT_DRAIN = 4,    /* main kernel: waiting for its own copies at exit */
+    LCA_DEVERR_TIMEOUT_PEER = 5      /* peer exchange: another rank's data did not arrive */
 };
 
 /* Input element types (Q, K, V share one type; the output is always fp32). */
@@ -118,9 +132,12 @@ LCA_API int lca_swa_forward(const void* q, const void* k, const void* v, float* 
  * allocator, a plugin inside a runtime that forbids allocation after start-up, a loop
  * that must not risk the synchronisation a cudaFree can cause).  No counterpart in the
  * reference.  The scratch is a fixed LCA_NOALLOC_SCRATCH_BYTES device array inside the
- * library: each GPU that uses this entry point holds it from the first call until the
- * process exits; the first call on a device looks up the array's device address and
- * should come before any stream capture on that device.  All calls on a device share the
+ * library, reserved on a GPU when the library's device code is loaded there and held until
+ * the process exits: with lazy module loading (the CUDA default) that is the first launch
+ * of one of the library's kernels on that GPU, with CUDA_MODULE_LOADING=EAGER it is
+ * context creation, whether or not this entry point is ever called.  The first call on a
+ * device looks up the array's device address and should come before any stream capture
+ * on that device.  All calls on a device share the
  * array, so calls that can overlap on the GPU race: order them.  Problems needing more
  * scratch than the array holds return LCA_ERR_UNSUPPORTED before any work is enqueued.
  */
@@ -252,8 +269,8 @@ LCA_API int lca_swa_shard_finish_peer(const lca_shard_desc* desc, float* out, fl
 LCA_API int lca_set_timing_events(void* before_main, void* after_main);
 
 /*
- * Read and clear the device-side error word of the current device (0 = no error; other
- * values identify which bounded wait of a kernel gave up).  Synchronises the device.
+ * Read and clear the device-side error word of the current device (LCA_DEVERR_NONE, or
+ * the LCA_DEVERR_* code of the first bounded wait that gave up).  Synchronises the device.
  * No counterpart in the reference, which never checks its launches
  * (csrc/bindings.cpp:49-70).
  */

@@ -11,9 +11,12 @@
 // LCA_NOALLOC_SCRATCH_BYTES.  The caller still owns Q, K, V, the output and the LSE.
 //
 // Properties a caller must know:
-//  * The array is a file-scope __device__ variable: each GPU on which this entry point
-//    is used holds LCA_NOALLOC_SCRATCH_BYTES of device memory from that first use until
-//    the process exits.
+//  * The array is a file-scope __device__ variable, part of the library's device code:
+//    a GPU holds its LCA_NOALLOC_SCRATCH_BYTES from the moment that code is loaded there
+//    until the process exits.  With lazy module loading (the CUDA default) that is the
+//    first launch of any of the library's kernels on the GPU; with
+//    CUDA_MODULE_LOADING=EAGER it is context creation, whether or not this entry point is
+//    ever called.
 //  * In host code the array's name only stands for it; the device address is obtained
 //    with cudaGetSymbolAddress, once per device, on the first call made with that device
 //    current.  That first call on a device should therefore come before any stream
@@ -53,7 +56,7 @@ extern "C" int lca_swa_forward_noalloc(const void* q, const void* k, const void*
     int64_t G = 0;
     int st = lca_normalize_global_tokens(global_tokens, num_global_tokens, seq_len, norm.data(), &G);
     if (st != LCA_OK) return st;
-    size_t need = 0;  // the forward's minimum (it adds the optional fp16 copy of V only if that fits too)
+    size_t need = 0;  // the forward's minimum; it also uses the optional part when the array holds that too
     st = lca::workspace_bytes(batch, heads, seq_len, head_dim, window_size, G, dtype, false, &need);
     if (st != LCA_OK) return st;
     if (need > (size_t)LCA_NOALLOC_SCRATCH_BYTES)
@@ -62,7 +65,7 @@ extern "C" int lca_swa_forward_noalloc(const void* q, const void* k, const void*
                                  "(use lca_swa_forward with a caller-provided workspace)",
                                  need, (size_t)LCA_NOALLOC_SCRATCH_BYTES);
     void* scratch = nullptr;
-    if (need > 0) {
+    if (batch * heads > 0 && seq_len > 0) {
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return lca::report_error(LCA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
@@ -77,7 +80,9 @@ extern "C" int lca_swa_forward_noalloc(const void* q, const void* k, const void*
         }
         scratch = g_scratch_ptr[dev];
     }
+    // The whole array goes to the forward, which uses the optional part (the fp16 copy of V,
+    // the work-unit counter) whenever the array holds it as well.
     return lca_swa_forward(q, k, v, out, lse, dtype, batch, heads, seq_len, head_dim, window_size, scale,
-                           global_tokens, num_global_tokens, scratch, need > 0 ? (size_t)LCA_NOALLOC_SCRATCH_BYTES : 0,
-                           stream);
+                           global_tokens, num_global_tokens, scratch,
+                           scratch != nullptr ? (size_t)LCA_NOALLOC_SCRATCH_BYTES : 0, stream);
 }

@@ -7,17 +7,12 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "lca.h"
+
 namespace lca {
 
-// Device-side error codes written to the error word when a bounded wait gives up.
-enum : int {
-    LCA_DEVERR_NONE = 0,
-    LCA_DEVERR_TIMEOUT_PRODUCER = 1,
-    LCA_DEVERR_TIMEOUT_MMA = 2,
-    LCA_DEVERR_TIMEOUT_SOFTMAX = 3,
-    LCA_DEVERR_TIMEOUT_DRAIN = 4,
-    LCA_DEVERR_TIMEOUT_PEER = 5,
-};
+// The device-side error codes written to the error word when a bounded wait gives up are
+// the LCA_DEVERR_* values of lca.h.
 
 constexpr int kTileRows = 128;        // query rows / keys per tile
 constexpr int kMaxPeers = 16;         // ranks of a peer-memory shard exchange

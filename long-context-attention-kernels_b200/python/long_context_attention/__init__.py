@@ -108,6 +108,27 @@ def sliding_window_attention_with_lse(
     return out, lse
 
 
+# Values of the device-side error word (include/lca.h, LCA_DEVERR_*).
+DEVICE_ERRORS = {
+    1: "main kernel: the TMA producer waited too long for a free slot",
+    2: "main kernel: an MMA issuer waited too long for data or P",
+    3: "main kernel: a softmax warp waited too long for S or O",
+    4: "main kernel: waiting for its own copies at exit took too long",
+    5: "peer exchange: another rank's halos, global rows or row partials did not arrive in time",
+}
+
+
 def device_error() -> int:
     """Read and clear the device-side error word (synchronises the current device)."""
     return native_error()
+
+
+def raise_on_device_error() -> None:
+    """Synchronise the current device, read and clear its device-side error word, and
+    raise RuntimeError if a kernel's bounded wait gave up since the last check.  Such a
+    kernel stops its own work and returns instead of hanging, so the results of the calls
+    since the last check are not to be used."""
+    code = native_error()
+    if code:
+        raise RuntimeError(f"long_context_attention: device error {code} "
+                           f"({DEVICE_ERRORS.get(code, 'unknown code')}); results since the last check are invalid")

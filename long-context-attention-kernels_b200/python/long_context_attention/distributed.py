@@ -284,7 +284,11 @@ class ShardedAttention:
     ``exchange="peer"`` moves the halos, global rows and row partials by NVLink stores
     from the library's own kernels into the other ranks' workspaces (CUDA IPC mappings
     made at construction; one GPU per rank), with bounded waits on counters there, so a
-    step runs no collective at all.  ``"nccl"`` (default) uses the process group.
+    step runs no collective at all.  ``"nccl"`` (default) uses the process group.  A rank
+    that is late or missing makes the others' waits give up after ``LCA_WAIT_TIMEOUT_MS``
+    (2 s by default): their step then runs on stale halos and global rows, and the device
+    error word says so.  Steps are asynchronous, so the error surfaces only when the host
+    looks: :meth:`raise_on_device_error` (or ``check=True`` on a call) does.
     """
 
     def __init__(self, batch: int, heads: int, seq_len: int, head_dim: int, window_size: int,
@@ -367,11 +371,25 @@ class ShardedAttention:
         exchange_rowparts(ws, lay, self.world, self.group)
         self.steps.finish(spec, self.out, self.lse, self.tokens, ws)
 
-    def __call__(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor):
-        """One forward on the current stream; returns :attr:`out` (and :attr:`lse`)."""
+    def __call__(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, check: bool = False):
+        """One forward on the current stream; returns :attr:`out` (and :attr:`lse`).
+        With ``check=True`` the call synchronises the device afterwards and raises if a
+        bounded wait of its kernels gave up (:meth:`raise_on_device_error`)."""
         self._check(Q, K, V)
         self._run(Q, K, V)
+        if check:
+            self.raise_on_device_error()
         return (self.out, self.lse) if self.lse is not None else self.out
+
+    def raise_on_device_error(self) -> None:
+        """Synchronise this rank's device and raise RuntimeError if a kernel's bounded wait
+        gave up since the last check (the device error word, read and cleared): for the
+        peer exchange, code 5 means another rank's data did not arrive in time, so the
+        outputs of the steps since the last check are invalid."""
+        from . import raise_on_device_error
+
+        with torch.cuda.device(self.device):
+            raise_on_device_error()
 
     def capture(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, warmup: int = 2) -> None:
         """Record one forward over these input tensors into a CUDA graph (after `warmup`

@@ -1,9 +1,9 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE implementation.
 
-Run in a container that has the reference checkout (default /root/reference, override
-with LCA_REFERENCE_DIR):
+Run in a container that has the reference checkout, naming its root directory in
+LCA_REFERENCE_DIR (required: the script has no default location):
 
-    python tests/golden/make_golden.py
+    LCA_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py
 
 For every case it builds seeded inputs, calls the reference's
 ``_reference_sliding_window_attention`` (python/long_context_attention/__init__.py:24-53,
@@ -35,7 +35,9 @@ _DT = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
 
 
 def load_reference():
-    ref_dir = os.environ.get("LCA_REFERENCE_DIR", "/root/reference")
+    ref_dir = os.environ.get("LCA_REFERENCE_DIR")
+    if not ref_dir:
+        raise SystemExit("set LCA_REFERENCE_DIR to the root of the reference checkout")
     path = os.path.join(ref_dir, "python", "long_context_attention", "__init__.py")
     spec = importlib.util.spec_from_file_location("_lca_reference_impl", path)
     mod = importlib.util.module_from_spec(spec)

@@ -256,3 +256,59 @@ def test_side_stream_and_duplicate_globals():
     b = lca.sliding_window_attention(q, k, v, 33, [519, 200, 5])
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("name", ["ref_gpu_case_fp16", "ref_gpu_case_bf16", "dup_neg_globals", "no_globals_w0",
+                                  "ragged_n_d128", "two_global_tiles"])
+def test_extension_called_as_the_reference_dispatch_calls_it(name):
+    """The reference's dispatch (python/long_context_attention/__init__.py:77-80) turns the
+    global-token list into an int32 tensor on Q's device and calls the extension's
+    ``sliding_window_attention_forward(Q, K, V, window_size, tensor, scale)``: the same call
+    here, with negative and duplicate indices and an empty list among the cases, against the
+    oracle and the reference's stored outputs.  (The extension reads that tensor on the host,
+    so a CUDA tensor costs one blocking device-to-host copy per call.)"""
+    c = load_golden(name)
+    ext = _native.extension()
+    q, k, v = (t.cuda() for t in (c["q"], c["k"], c["v"]))
+    idx = torch.as_tensor(list(c["globals"]), dtype=torch.int32, device=q.device)
+    out = ext.sliding_window_attention_forward(q, k, v, c["window"], idx, c["scale"])
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32 and out.shape == q.shape
+    rows = c["rows"]
+    got = to_np(out)[:, :, rows]
+    assert_parity(got, c["out"], f"{name} (reference dispatch) vs reference output")
+    want, _ = _oracle(c, rows)
+    assert_parity(got, want, f"{name} (reference dispatch) vs oracle")
+    # the index tensor may also live on the host, as the reference's binding allows
+    out_host_idx = ext.sliding_window_attention_forward(q, k, v, c["window"], idx.cpu(), c["scale"])
+    assert torch.equal(out_host_idx, out)
+
+
+def test_extension_index_tensor_out_of_range_raises():
+    q, k, v = make_inputs(3, 1, 1, 256, 64, torch.float16, device="cuda")
+    with pytest.raises(IndexError):
+        _native.extension().sliding_window_attention_forward(
+            q, k, v, 16, torch.tensor([0, 256], dtype=torch.int32, device="cuda"), 0.125)
+    empty = torch.empty(0, dtype=torch.int32, device="cuda")
+    out = _native.extension().sliding_window_attention_forward(q, k, v, 16, empty, 0.125)
+    want, _ = swa_oracle.sliding_window_attention(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                                  v.float().cpu().numpy(), 16, [], 0.125)
+    assert_parity(to_np(out), want, "empty index tensor")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_many_globals_beyond_shared_index_list(dtype):
+    """More global tokens (3000) than the d=64 kernel keeps in shared memory (2048): the
+    band rows then search the sorted index list in global memory.  Checked on every global
+    row (the global-row units) and a sample of the others against the oracle."""
+    n, w = 8192, 128
+    rng = np.random.default_rng(11)
+    g = sorted(int(x) for x in rng.choice(n, 3000, replace=False))
+    q, k, v = make_inputs(12, 1, 1, n, 64, dtype)
+    out, lse = lca.sliding_window_attention_with_lse(q.cuda(), k.cuda(), v.cuda(), w, g, 0.125)
+    rows = np.asarray(sorted(set(rng.choice(n, 300, replace=False).tolist()) | set(g[::10]) | {0, n - 1}))
+    want, want_lse = swa_oracle.sliding_window_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                                         w, g, 0.125, rows=rows)
+    assert_parity(to_np(out)[:, :, rows], want, f"3000 globals {dtype}")
+    assert max_abs(to_np(lse)[:, :, rows], want_lse) <= LSE_ABS_TOL
+    assert lca.device_error() == 0
