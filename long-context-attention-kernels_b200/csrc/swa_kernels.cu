@@ -1296,8 +1296,17 @@ template <int D, bool BF16, bool V16 = false>
 static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int grid, cudaStream_t stream) {
     auto kern = lca_swa_main<D, BF16, V16>;
     const int smem = Cfg<D, BF16, V16>::kSmemBytes;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // the shared-memory attribute is set once per device (it persists in the context)
+    constexpr int kDevices = 64;
+    static bool attr_set[kDevices];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kDevices || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < kDevices) attr_set[dev] = true;
+    }
     kern<<<grid, Cfg<D, BF16, V16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kh, tm.vh, tm.qg, tm.kg, tm.vg,
                                                               tm.o, tm.po, tm.v16, tm.vg16, tm.vh16, p);
     return cudaGetLastError();
