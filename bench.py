@@ -241,10 +241,9 @@ def config_of(w, world: int, parallelism: str) -> dict:
 
 def launches_per_forward(w, fast: bool = True) -> int:
     """Kernels of one lca_swa_forward: gather and merge with global tokens, the main
-    kernel, and for bf16 the fp16 copy of V and the second main-kernel variant (one of
-    the two returns at once)."""
+    kernel, and for bf16 the fp16 copy of V."""
     g = len(w.global_tokens()) > 0
-    return 1 + (2 if g else 0) + (2 if (w.dtype == "bf16" and fast) else 0)
+    return 1 + (2 if g else 0) + (1 if (w.dtype == "bf16" and fast) else 0)
 
 
 def run_reference(args):
@@ -529,12 +528,12 @@ def measure_sequence(w, world, rank, local, dev, pg, steps, warmup, exchange, e2
     flops_rank = 4 * w.head_dim * w.batch * w.heads * useful_scores_shard(w.seq_len, w.window, g, off, ln)
     io_rank = w.io_bytes() * ln // w.seq_len
     ms, e2e_ms, main_ms, flops_max, io_max = _max_over_ranks(pg, dev, [ms, e2e_ms, main_ms, flops_rank, io_rank])
-    # kernels of one step: gather (global tokens), halo pack (2+ shards), the fp16 copy of V and
-    # the second main-kernel variant (bf16), the main kernel, the split merge (global tokens),
-    # then the peer exchange's two copy kernels and its merge, or the final merge alone
+    # kernels of one step: gather (global tokens), halo pack (2+ shards), the fp16 copy of V
+    # (bf16), the main kernel, the split merge (global tokens), then the peer exchange's two
+    # copy kernels and its merge, or the final merge alone
     g1 = 1 if g else 0
     halo = 1 if (world > 1 and w.window > 0) else 0
-    main = 3 if w.dtype == "bf16" else 1
+    main = 2 if w.dtype == "bf16" else 1
     per_step = g1 + halo + main + g1 + (3 if plan.exchange == "peer" else g1)
     exchange_used = plan.exchange
     plan.release()

@@ -308,11 +308,12 @@ Layout make_layout(const Problem& P) {
             L.off_vh16 = off;
             off = align_up(off + 2 * L.halo_block, kAlign);
         }
+        // the word and the work-unit counter sit side by side, so one memset clears both
         L.off_v16bad = off;
-        off = align_up(off + sizeof(int), kAlign);
+        L.off_counter = off + sizeof(int);
+        off = align_up(off + 2 * sizeof(int), kAlign);
         L.has_v16 = true;
-    }
-    if (bh > 0 && P.n > 0) {
+    } else if (bh > 0 && P.n > 0) {
         L.off_counter = off;
         off = align_up(off + sizeof(unsigned int), kAlign);
     }
@@ -445,7 +446,8 @@ int enqueue_convert_v16(const Problem& P, const Layout& L, const void* v, uint8_
         }
     }
     cv.any_bad = reinterpret_cast<int*>(ws + L.off_v16bad);
-    cudaError_t e = cudaMemsetAsync(cv.any_bad, 0, sizeof(int), stream);
+    // clears the word and, next to it, the main kernel's work-unit counter
+    cudaError_t e = cudaMemsetAsync(cv.any_bad, 0, 2 * sizeof(int), stream);
     if (e == cudaSuccess) e = lca::launch_convert_v16((int)P.d, cv, stream);
     if (e != cudaSuccess) return fail_cuda(e, "fp16 V copy launch");
     return LCA_OK;
@@ -626,8 +628,10 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     const int grid = (int)std::min<long long>(units, g_dev_sms[dev]);
     if (dynamic_units) {
         p.unit_counter = reinterpret_cast<unsigned int*>(ws + L.off_counter);
-        cudaError_t me = cudaMemsetAsync(p.unit_counter, 0, sizeof(unsigned int), stream);
-        if (me != cudaSuccess) return fail_cuda(me, "unit counter reset");
+        if (!v16) {  // (with the fp16 copy of V, the copy's memset cleared it)
+            cudaError_t me = cudaMemsetAsync(p.unit_counter, 0, sizeof(unsigned int), stream);
+            if (me != cudaSuccess) return fail_cuda(me, "unit counter reset");
+        }
     }
     const bool timed = g_ev_before_main != nullptr && g_ev_after_main != nullptr;
     cudaError_t e;

@@ -300,22 +300,17 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk16) {
     return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
 }
 
+// The main kernel's body: tensor maps by reference to the kernel's __grid_constant__
+// parameters (TMA reads them where they lie).
 template <int D, bool BF16, bool V16>
-__global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
-    lca_swa_main(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kh,
-                 const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_qg,
-                 const __grid_constant__ CUtensorMap tm_kg, const __grid_constant__ CUtensorMap tm_vg,
-                 const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_po,
-                 const __grid_constant__ CUtensorMap tm_v16, const __grid_constant__ CUtensorMap tm_vg16,
-                 const __grid_constant__ CUtensorMap tm_vh16, const MainParams p) {
+__device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                              const CUtensorMap& tm_kh, const CUtensorMap& tm_vh,
+                                              const CUtensorMap& tm_qg, const CUtensorMap& tm_kg,
+                                              const CUtensorMap& tm_vg, const CUtensorMap& tm_o,
+                                              const CUtensorMap& tm_po, const CUtensorMap& tm_v16,
+                                              const CUtensorMap& tm_vg16, const CUtensorMap& tm_vh16,
+                                              const MainParams& p) {
     using C = Cfg<D, BF16, V16>;
-    if (p.v16_bad != nullptr) {
-        // bf16 with an fp16 copy of V: both variants are launched and one does the work --
-        // this one (V16) if every value of V fitted fp16, else the split one
-        const bool bad = *reinterpret_cast<const volatile int*>(p.v16_bad) != 0;
-        if (V16 ? bad : !bad) return;
-    }
     constexpr int H = C::kHalves;
     constexpr int NC = C::kChains;
     constexpr int KC = C::kCols;
@@ -1029,6 +1024,36 @@ __global__ void __launch_bounds__(Cfg<D, BF16, V16>::kThreads, 1)
     if (warp == C::kMmaWarp) ptx::tmem_dealloc(tmem, kTmemCols);
 }
 
+#define LCA_MAIN_PARAMS                                                                                           \
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,                           \
+        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kh,                      \
+        const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_qg,                     \
+        const __grid_constant__ CUtensorMap tm_kg, const __grid_constant__ CUtensorMap tm_vg,                     \
+        const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_po,                      \
+        const __grid_constant__ CUtensorMap tm_v16, const __grid_constant__ CUtensorMap tm_vg16,                  \
+        const __grid_constant__ CUtensorMap tm_vh16, const MainParams p
+#define LCA_MAIN_ARGS tm_q, tm_k, tm_v, tm_kh, tm_vh, tm_qg, tm_kg, tm_vg, tm_o, tm_po, tm_v16, tm_vg16, tm_vh16, p
+
+// fp16 inputs (fp16 P), or bf16 inputs without the fp16 copy of V (bf16 P split into hi + lo)
+template <int D, bool BF16>
+__global__ void __launch_bounds__(Cfg<D, BF16, false>::kThreads, 1) lca_swa_main(LCA_MAIN_PARAMS) {
+    swa_main_body<D, BF16, false>(LCA_MAIN_ARGS);
+}
+
+// bf16 inputs with the fp16 copy of V: one launch that reads the word lca_convert_v16 set and
+// runs fp16 P with one P*V per tile from the copy when every value of V fitted fp16, else the
+// split bf16 P (no host synchronisation, so the choice stays capturable in a graph)
+template <int D>
+__global__ void __launch_bounds__(Cfg<D, true, true>::kThreads, 1) lca_swa_main_v16(LCA_MAIN_PARAMS) {
+    static_assert(Cfg<D, true, true>::kSmemBytes == Cfg<D, true, false>::kSmemBytes &&
+                      Cfg<D, true, true>::kThreads == Cfg<D, true, false>::kThreads,
+                  "both paths share one launch configuration");
+    if (*reinterpret_cast<const volatile int*>(p.v16_bad) == 0)
+        swa_main_body<D, true, true>(LCA_MAIN_ARGS);
+    else
+        swa_main_body<D, true, false>(LCA_MAIN_ARGS);
+}
+
 // ------------------------------------------------------------------------ gather
 
 template <int D>
@@ -1294,7 +1319,7 @@ __global__ void __launch_bounds__(256) lca_peer_put(PeerPutParams pp) {
 
 template <int D, bool BF16, bool V16 = false>
 static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int grid, cudaStream_t stream) {
-    auto kern = lca_swa_main<D, BF16, V16>;
+    auto kern = V16 ? lca_swa_main_v16<D> : lca_swa_main<D, BF16>;
     const int smem = Cfg<D, BF16, V16>::kSmemBytes;
     // the shared-memory attribute is set once per device (it persists in the context)
     constexpr int kDevices = 64;
@@ -1315,12 +1340,9 @@ static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int 
 cudaError_t launch_main(int head_dim, bool bf16, const TensorMaps& tm, const MainParams& p, int grid,
                         cudaStream_t stream, bool v16) {
     if (head_dim != 64 && head_dim != 128) return cudaErrorInvalidValue;
-    if (bf16 && v16) {
-        // both variants; each reads p.v16_bad first and one returns at once
-        cudaError_t e = head_dim == 64 ? launch_main_t<64, true, true>(tm, p, grid, stream)
-                                       : launch_main_t<128, true, true>(tm, p, grid, stream);
-        if (e != cudaSuccess) return e;
-    }
+    if (bf16 && v16)  // one launch; it picks fp16 P or the split on the device (p.v16_bad)
+        return head_dim == 64 ? launch_main_t<64, true, true>(tm, p, grid, stream)
+                              : launch_main_t<128, true, true>(tm, p, grid, stream);
     if (head_dim == 64) return bf16 ? launch_main_t<64, true>(tm, p, grid, stream) : launch_main_t<64, false>(tm, p, grid, stream);
     return bf16 ? launch_main_t<128, true>(tm, p, grid, stream) : launch_main_t<128, false>(tm, p, grid, stream);
 }
