@@ -55,8 +55,9 @@ enum {
     LCA_DEVERR_TIMEOUT_PEER = 5      /* peer exchange: another rank's data did not arrive */
 };
 
-/* Input element types (Q, K, V share one type; the output is always fp32). */
-enum { LCA_DTYPE_F16 = 0, LCA_DTYPE_BF16 = 1 };
+/* Element types: Q, K, V share LCA_DTYPE_F16 or LCA_DTYPE_BF16; the output is fp32
+ * (LCA_DTYPE_F32) except through lca_swa_forward_typed, which also writes fp16 or bf16. */
+enum { LCA_DTYPE_F16 = 0, LCA_DTYPE_BF16 = 1, LCA_DTYPE_F32 = 2 };
 
 /* ABI version of the loaded library (== LCA_ABI_VERSION it was built with). */
 LCA_API int lca_abi_version(void);
@@ -120,6 +121,19 @@ LCA_API int lca_swa_forward(const void* q, const void* k, const void* v, float* 
                     int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
                     float scale, const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
                     size_t workspace_bytes, void* stream);
+
+/*
+ * lca_swa_forward with a choice of output type: `out` is [batch, heads, seq_len,
+ * head_dim] of `out_dtype` (LCA_DTYPE_F32, LCA_DTYPE_F16 or LCA_DTYPE_BF16), 16-byte
+ * aligned.  The arithmetic is the same (fp32 accumulation); a 16-bit output is the fp32
+ * result rounded to nearest, and halves the bytes the forward writes.  `lse` stays fp32.
+ * No counterpart in the reference, whose extension always returns fp32
+ * (csrc/bindings.cpp:44).
+ */
+LCA_API int lca_swa_forward_typed(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
+                                  int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                                  int64_t window_size, float scale, const int64_t* global_tokens,
+                                  int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Bytes of the fixed device scratch array used by lca_swa_forward_noalloc.

@@ -123,6 +123,7 @@ struct Problem {
     int64_t world = 1;     // shards
     bool sharded = false;
     int dtype = LCA_DTYPE_BF16;
+    int out_dtype = LCA_DTYPE_F32;  // type of out (16-bit only through lca_swa_forward_typed)
     float scale = 1.f;
     std::vector<int32_t> gl;  // sorted unique global indices (absolute)
     int64_t halo() const { return sharded && world > 1 ? window : 0; }
@@ -324,7 +325,8 @@ Layout make_layout(const Problem& P) {
 // ------------------------------------------------------------------ tensor maps
 
 int encode_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t d, uint64_t rows,
-              uint64_t planes, uint32_t box_x, const char* name) {
+              uint64_t planes, uint32_t box_x, const char* name,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiledFn enc = get_encode_fn();
     if (enc == nullptr) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
     cuuint64_t dims[3] = {d, rows, planes};
@@ -332,8 +334,7 @@ int encode_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* bas
     cuuint32_t box[3] = {box_x, (cuuint32_t)lca::kTileRows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
     return LCA_OK;
 }
@@ -464,7 +465,7 @@ struct MapKey {
     const void* out;
     const void* ws;
     int64_t n, n_total, q_off, d, bh, G, window, world;
-    int dtype, sharded, v16, n_splits, dev;
+    int dtype, out_dtype, sharded, v16, n_splits, dev;
 };
 constexpr int kMapCache = 4;
 thread_local MapKey g_map_key[kMapCache];
@@ -472,7 +473,7 @@ thread_local lca::TensorMaps g_map_val[kMapCache];
 thread_local bool g_map_ok[kMapCache];
 thread_local int g_map_next = 0;
 
-int encode_maps(const Problem& P, const Layout& L, const void* q, const void* k, const void* v, float* out,
+int encode_maps(const Problem& P, const Layout& L, const void* q, const void* k, const void* v, void* out,
                 uint8_t* ws, bool v16, lca::TensorMaps& tm) {
     const bool bf16 = P.dtype == LCA_DTYPE_BF16;
     const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -485,7 +486,14 @@ int encode_maps(const Problem& P, const Layout& L, const void* q, const void* k,
     if ((st = encode_3d(&tm.q, tdt, 2, q, d, n, bh, 64, "q")) != LCA_OK) return st;
     if ((st = encode_3d(&tm.k, tdt, 2, k, d, n, bh, 64, "k")) != LCA_OK) return st;
     if ((st = encode_3d(&tm.v, tdt, 2, v, d, n, bh, 64, "v")) != LCA_OK) return st;
-    if ((st = encode_3d(&tm.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, d, n, bh, 32, "out")) != LCA_OK) return st;
+    if (P.out_dtype == LCA_DTYPE_F32) {
+        if ((st = encode_3d(&tm.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, d, n, bh, 32, "out")) != LCA_OK) return st;
+    } else {
+        // 16-bit output: 32-column boxes of 64-byte rows, unswizzled
+        const CUtensorMapDataType odt =
+            P.out_dtype == LCA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        if ((st = encode_3d(&tm.o, odt, 2, out, d, n, bh, 32, "out", CU_TENSOR_MAP_SWIZZLE_NONE)) != LCA_OK) return st;
+    }
     if (halo > 0) {
         // recv block [2 sides][2 (k, v)][bh][halo][d]: K planes at z = side * 2bh + b from
         // the block start, V planes the same from bh planes further on
@@ -512,7 +520,7 @@ int encode_maps(const Problem& P, const Layout& L, const void* q, const void* k,
         tm.qg = tm.q;
         tm.kg = tm.k;
         tm.vg = tm.v;
-        tm.po = tm.o;
+        tm.po = tm.q;
     }
     tm.v16 = tm.v;
     tm.vg16 = tm.vg;
@@ -533,7 +541,7 @@ int encode_maps(const Problem& P, const Layout& L, const void* q, const void* k,
     return LCA_OK;
 }
 
-int cached_maps(const Problem& P, const Layout& L, int dev, const void* q, const void* k, const void* v, float* out,
+int cached_maps(const Problem& P, const Layout& L, int dev, const void* q, const void* k, const void* v, void* out,
                 uint8_t* ws, bool v16, lca::TensorMaps& tm) {
     MapKey key;
     memset(&key, 0, sizeof(key));  // padding too: keys are compared bytewise
@@ -551,6 +559,7 @@ int cached_maps(const Problem& P, const Layout& L, int dev, const void* q, const
     key.window = P.window;
     key.world = P.world;
     key.dtype = P.dtype;
+    key.out_dtype = P.out_dtype;
     key.sharded = P.sharded ? 1 : 0;
     key.v16 = v16 ? 1 : 0;
     key.n_splits = L.n_splits;
@@ -572,7 +581,7 @@ int cached_maps(const Problem& P, const Layout& L, int dev, const void* q, const
 }
 
 int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, const void* q, const void* k,
-                 const void* v, float* out, float* lse, uint8_t* ws, cudaStream_t stream, bool v16 = false,
+                 const void* v, void* out, float* lse, uint8_t* ws, cudaStream_t stream, bool v16 = false,
                  bool dynamic_units = false) {
     const bool bf16 = P.dtype == LCA_DTYPE_BF16;
     const int n = (int)P.n;
@@ -608,6 +617,7 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     p.lse = lse;
     p.err = err_word;
     p.timeout_ns = wait_timeout_ns();
+    p.out16 = P.out_dtype == LCA_DTYPE_F32 ? 0 : (P.out_dtype == LCA_DTYPE_BF16 ? lca::kOut16BF16 : lca::kOut16F16);
     if (P.G > 0) {
         p.g_tiles = L.g_tiles;
         p.n_splits = L.n_splits;
@@ -646,7 +656,7 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
 
 // Merge of the main kernel's global-row partials: over the rows of out / lse, or (for a
 // shard) into this shard's packed row partial.
-int enqueue_combine_splits(const Problem& P, const Layout& L, float* out, float* lse, uint8_t* ws,
+int enqueue_combine_splits(const Problem& P, const Layout& L, void* out, float* lse, uint8_t* ws,
                            cudaStream_t stream) {
     if (P.G == 0) return LCA_OK;
     lca::CombineParams cp;
@@ -667,6 +677,7 @@ int enqueue_combine_splits(const Problem& P, const Layout& L, float* out, float*
     } else {
         cp.o = out;
         cp.lse = lse;
+        cp.out16 = P.out_dtype == LCA_DTYPE_F32 ? 0 : (P.out_dtype == LCA_DTYPE_BF16 ? lca::kOut16BF16 : lca::kOut16F16);
         cp.n_rows = (int)P.n;
         cp.row_off = 0;
     }
@@ -758,11 +769,22 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
                     int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
                     float scale, const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
                     size_t workspace_bytes, void* stream_ptr) {
+    return lca_swa_forward_typed(q, k, v, out, LCA_DTYPE_F32, lse, dtype, batch, heads, seq_len, head_dim, window_size,
+                                 scale, global_tokens, num_global_tokens, workspace, workspace_bytes, stream_ptr);
+}
+
+int lca_swa_forward_typed(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
+                          int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                          int64_t window_size, float scale, const int64_t* global_tokens, int64_t num_global_tokens,
+                          void* workspace, size_t workspace_bytes, void* stream_ptr) {
     g_last_error.clear();
+    if (out_dtype != LCA_DTYPE_F32 && out_dtype != LCA_DTYPE_F16 && out_dtype != LCA_DTYPE_BF16)
+        return fail(LCA_ERR_UNSUPPORTED, "out_dtype %d is not supported (fp32, fp16 or bf16)", out_dtype);
     Problem P;
     int st = parse_common(P, dtype, batch, heads, seq_len, head_dim, window_size, scale, global_tokens,
                           num_global_tokens);
     if (st != LCA_OK) return st;
+    P.out_dtype = out_dtype;
     if (P.bh == 0 || P.n == 0) return LCA_OK;  // nothing to compute
     if ((st = check_io(q, k, v, out, lse)) != LCA_OK) return st;
     int dev = 0;

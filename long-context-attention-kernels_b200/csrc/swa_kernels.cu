@@ -964,6 +964,7 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
             const float w1 = (hh == 0) ? w_oth : w_own;
             const CUtensorMap* mo = un.grow ? &tm_po : &tm_o;
             const int oz = un.grow ? ((2 * un.split + X) * p.bh + un.bh) : un.bh;
+            const int out16 = un.grow ? 0 : p.out16;  // global-row partials stay fp32
 #pragma unroll
             for (int c = 0; c < C::kEpiCols / 32; ++c) {
                 const int ocol = hh * C::kEpiCols + c * 32;  // output column of this chunk
@@ -987,11 +988,25 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                         for (int e = 0; e < 32; ++e) o[e] *= inv_l;
                     }
                     const uint32_t sbase = ptx::smem_u32(panel);
+                    if (out16) {
+                        // 16-bit rows of 64 bytes, unswizzled (the 16-bit output map's layout)
 #pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        ptx::st_shared_v4(sbase + swz128(r, q), __float_as_uint(o[q * 4 + 0]),
-                                          __float_as_uint(o[q * 4 + 1]), __float_as_uint(o[q * 4 + 2]),
-                                          __float_as_uint(o[q * 4 + 3]));
+                        for (int q = 0; q < 4; ++q) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float a = o[q * 8 + 2 * e], b = o[q * 8 + 2 * e + 1];
+                                w[e] = out16 == kOut16BF16 ? ptx::pack_bf16x2(a, b) : ptx::pack_f16x2(a, b);
+                            }
+                            ptx::st_shared_v4(sbase + r * 64 + q * 16, w[0], w[1], w[2], w[3]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            ptx::st_shared_v4(sbase + swz128(r, q), __float_as_uint(o[q * 4 + 0]),
+                                              __float_as_uint(o[q * 4 + 1]), __float_as_uint(o[q * 4 + 2]),
+                                              __float_as_uint(o[q * 4 + 3]));
+                    }
                 }
                 ptx::fence_proxy_async_smem();
                 ptx::named_bar_sync(wg_bar, kWgThreads);
@@ -1254,19 +1269,30 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
     const float lse = mx + __logf(wtot);
     float* out_row = nullptr;
     float* lse_out = nullptr;
+    size_t out_idx = 0;  // 16-bit output: element index of the row
+    int out16 = 0;
     if (cp.out_o != nullptr) {
         out_row = cp.out_o + row * D;
         lse_out = cp.out_lse + row;
     } else {
         const int orow = cp.gidx[g] - cp.row_off;
         if (orow >= 0 && orow < cp.n_rows) {  // else owned by another shard
-            out_row = cp.o + ((size_t)bh * cp.n_rows + orow) * D;
+            out_idx = ((size_t)bh * cp.n_rows + orow) * D;
+            out16 = cp.out16;
+            out_row = static_cast<float*>(cp.o) + (out16 ? 0 : out_idx);
             lse_out = cp.lse != nullptr ? cp.lse + (size_t)bh * cp.n_rows + orow : nullptr;
         }
     }
     if (out_row != nullptr) {
-        for (int c = threadIdx.x; c < D; c += blockDim.x)
-            out_row[c] = ((s_acc[0][c] + s_acc[1][c]) + (s_acc[2][c] + s_acc[3][c])) * inv;
+        for (int c = threadIdx.x; c < D; c += blockDim.x) {
+            const float val = ((s_acc[0][c] + s_acc[1][c]) + (s_acc[2][c] + s_acc[3][c])) * inv;
+            if (out16 == kOut16BF16)
+                static_cast<__nv_bfloat16*>(cp.o)[out_idx + c] = __float2bfloat16_rn(val);
+            else if (out16 == kOut16F16)
+                static_cast<__half*>(cp.o)[out_idx + c] = __float2half_rn(val);
+            else
+                out_row[c] = val;
+        }
         if (threadIdx.x == 0 && lse_out != nullptr) *lse_out = lse;
     }
     if (cp.epoch != nullptr) {

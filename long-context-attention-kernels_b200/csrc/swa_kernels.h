@@ -34,7 +34,8 @@ struct TensorMaps {
     CUtensorMap kh, vh;      // sequence shards: K / V halo blocks (z = bh + b left, 2*bh + b right)
     CUtensorMap qg, kg, vg;  // compact global rows [G][3 (q, k, v)][bh][d]; maps {d, bh, G}, box 64 x 1 x 128
                              // (rows >= G read as zeros)
-    CUtensorMap o;           // output [bh][n][d] fp32, box 32 x 128 rows, 128B swizzle
+    CUtensorMap o;           // output [bh][n][d]: fp32 with box 32 x 128 rows and 128B swizzle, or
+                             // 16-bit (MainParams::out16) with box 32 x 128 rows and no swizzle
     CUtensorMap po;          // global-row partial outputs [2*splits*bh][G][d] fp32
     CUtensorMap v16, vg16;   // bf16 inputs: fp16 copies of V [bh][n][d] and of the compact global V
                              // rows [G][bh][d] (maps {d, bh, G}); the bf16 maps when unused
@@ -78,7 +79,10 @@ struct MainParams {
     const int* v16_bad;
     int* err;         // device error word (first error wins)
     unsigned long long timeout_ns;  // per-wait budget
+    int out16;        // band rows' output type: 0 fp32, kOut16F16 fp16, kOut16BF16 bf16
 };
+constexpr int kOut16F16 = 1;
+constexpr int kOut16BF16 = 2;
 
 // Copies the global rows owned by this shard into the compact buffer [G][3][bh][d] and
 // writes the sorted index list; rows owned by other shards are left untouched (their
@@ -115,8 +119,9 @@ struct CombineParams {
     const float* part_o;
     const float* part_lse;
     const int* gidx;
-    float* o;
+    void* o;          // fp32, or 16-bit per out16
     float* lse;
+    int out16;        // type of o: 0 fp32, kOut16F16, kOut16BF16
     int n_rows, row_off;
     float* out_o;
     float* out_lse;

@@ -71,6 +71,7 @@ def sliding_window_attention(
     global_tokens: Sequence[int] = (),
     scale: float | None = None,
     force_reference: bool = False,
+    out_dtype: torch.dtype | None = None,
 ) -> torch.Tensor:
     """Longformer-style sparse attention forward.
 
@@ -79,14 +80,20 @@ def sliding_window_attention(
     global_tokens: token indices with full rows and columns (negative indices count from
     the end; duplicates are harmless).  scale defaults to 1/sqrt(head_dim).
     Returns a new fp32 tensor [batch, heads, seq_len, head_dim] on Q's device, computed
-    on the current CUDA stream.
+    on the current CUDA stream.  ``out_dtype`` (an addition; the reference always returns
+    fp32) may be torch.float16 or torch.bfloat16: the same fp32-accumulated result,
+    rounded to that type by the kernel, with half the output bytes.
     """
     if force_reference:
         if scale is None:
             scale = 1.0 / math.sqrt(Q.shape[-1])
-        return _reference_sliding_window_attention(Q, K, V, window_size, global_tokens, scale)
+        out = _reference_sliding_window_attention(Q, K, V, window_size, global_tokens, scale)
+        return out if out_dtype in (None, torch.float32) else out.to(out_dtype)
     scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
-    return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
+    if out_dtype in (None, torch.float32):
+        return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
+    return extension().sliding_window_attention_forward_typed(Q, K, V, window_size, tokens, scale, out_dtype,
+                                                              False)[0]
 
 
 def sliding_window_attention_with_lse(
@@ -96,6 +103,7 @@ def sliding_window_attention_with_lse(
     window_size: int,
     global_tokens: Sequence[int] = (),
     scale: float | None = None,
+    out_dtype: torch.dtype | None = None,
 ):
     """As :func:`sliding_window_attention`, also returning the per-row log-sum-exp.
 
@@ -104,7 +112,11 @@ def sliding_window_attention_with_lse(
     or a cross-shard merge needs).  No counterpart in the reference.
     """
     scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
-    out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
+    if out_dtype in (None, torch.float32):
+        out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
+    else:
+        out, lse = extension().sliding_window_attention_forward_typed(Q, K, V, window_size, tokens, scale,
+                                                                      out_dtype, True)
     return out, lse
 
 

@@ -53,3 +53,20 @@ def test_forward_validation_before_device_work():
     # a NULL tensor pointer is rejected before any launch
     assert _fwd(c) == c.ERR_INVALID_ARGUMENT
     assert "non-NULL" in c.last_error()
+
+
+def test_typed_forward_validation_before_device_work():
+    c = _native.cabi()
+
+    def typed(out_dtype, **kw):
+        args = dict(q_ptr=None, k_ptr=None, v_ptr=None, o_ptr=None, out_dtype=out_dtype, lse_ptr=None,
+                    dtype=c.DTYPE_BF16, batch=1, heads=1, seq_len=128, head_dim=64, window=4, scale=0.125, tokens=[],
+                    ws_ptr=None, ws_bytes=0, stream_ptr=None)
+        args.update(kw)
+        return c.forward_typed(**args)
+
+    assert typed(7) == c.ERR_UNSUPPORTED
+    assert "out_dtype" in c.last_error()
+    for dt in (c.DTYPE_F32, c.DTYPE_F16, c.DTYPE_BF16):
+        assert typed(dt, batch=0) == c.OK
+        assert typed(dt) == c.ERR_INVALID_ARGUMENT  # NULL tensors, before any launch
