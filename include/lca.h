@@ -56,7 +56,7 @@ enum {
 };
 
 /* Element types: Q, K, V share LCA_DTYPE_F16 or LCA_DTYPE_BF16; the output is fp32
- * (LCA_DTYPE_F32) except through lca_swa_forward_typed, which also writes fp16 or bf16. */
+ * (LCA_DTYPE_F32) except through lca_swa_forward_ex, which also writes fp16 or bf16. */
 enum { LCA_DTYPE_F16 = 0, LCA_DTYPE_BF16 = 1, LCA_DTYPE_F32 = 2 };
 
 /* ABI version of the loaded library (== LCA_ABI_VERSION it was built with). */
@@ -122,18 +122,28 @@ LCA_API int lca_swa_forward(const void* q, const void* k, const void* v, float* 
                     float scale, const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Flags of lca_swa_forward_ex. */
+enum {
+    /* Causal (one-sided) variant: the mask above intersected with j <= i -- the band
+     * becomes [i - window_size, i], a global key is visible to the rows at or after it,
+     * and a global row sees the keys up to itself. */
+    LCA_FLAG_CAUSAL = 1
+};
+
 /*
- * lca_swa_forward with a choice of output type: `out` is [batch, heads, seq_len,
- * head_dim] of `out_dtype` (LCA_DTYPE_F32, LCA_DTYPE_F16 or LCA_DTYPE_BF16), 16-byte
- * aligned.  The arithmetic is the same (fp32 accumulation); a 16-bit output is the fp32
- * result rounded to nearest, and halves the bytes the forward writes.  `lse` stays fp32.
- * No counterpart in the reference, whose extension always returns fp32
- * (csrc/bindings.cpp:44).
+ * lca_swa_forward with options, none of which the reference has (its extension always
+ * returns fp32 and has no causal mode, csrc/bindings.cpp:31-73):
+ *   out_dtype    type of `out` ([batch, heads, seq_len, head_dim], 16-byte aligned):
+ *                LCA_DTYPE_F32, or LCA_DTYPE_F16 / LCA_DTYPE_BF16 -- the same fp32-accumulated
+ *                result rounded to nearest, with half the output bytes.  `lse` stays fp32.
+ *   flags        0 or LCA_FLAG_CAUSAL.
+ * The other arguments are lca_swa_forward's; lca_swa_forward(...) is
+ * lca_swa_forward_ex(..., LCA_DTYPE_F32, ..., 0, ...).
  */
-LCA_API int lca_swa_forward_typed(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
-                                  int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
-                                  int64_t window_size, float scale, const int64_t* global_tokens,
-                                  int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream);
+LCA_API int lca_swa_forward_ex(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
+                               int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                               int64_t window_size, float scale, int flags, const int64_t* global_tokens,
+                               int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Bytes of the fixed device scratch array used by lca_swa_forward_noalloc.

@@ -33,7 +33,8 @@ void raise_status(int st, const char* what) {
 
 std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Tensor& K, const torch::Tensor& V,
                                         int64_t window_size, const std::vector<int64_t>& globals, double scale,
-                                        bool want_lse, c10::ScalarType out_type = torch::kFloat32) {
+                                        bool want_lse, c10::ScalarType out_type = torch::kFloat32,
+                                        bool causal = false) {
     check_input(Q, "Q");
     check_input(K, "K");
     check_input(V, "V");
@@ -70,10 +71,11 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
     cudaStream_t stream = at::cuda::getCurrentCUDAStream();
     const int out_dtype = out_type == torch::kFloat32 ? LCA_DTYPE_F32
                           : (out_type == torch::kBFloat16 ? LCA_DTYPE_BF16 : LCA_DTYPE_F16);
-    const int st = lca_swa_forward_typed(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), out_dtype,
-                                         want_lse ? L.data_ptr<float>() : nullptr, dtype, batch, heads, seq_len,
-                                         head_dim, window_size, static_cast<float>(scale), globals.data(),
-                                         (int64_t)globals.size(), ws_ptr, ws_bytes, static_cast<void*>(stream));
+    const int st = lca_swa_forward_ex(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), out_dtype,
+                                      want_lse ? L.data_ptr<float>() : nullptr, dtype, batch, heads, seq_len, head_dim,
+                                      window_size, static_cast<float>(scale), causal ? LCA_FLAG_CAUSAL : 0,
+                                      globals.data(), (int64_t)globals.size(), ws_ptr, ws_bytes,
+                                      static_cast<void*>(stream));
     raise_status(st, "sliding_window_attention_forward");
     if (want_lse) return {O, L};
     return {O};
@@ -104,11 +106,11 @@ std::vector<torch::Tensor> sliding_window_attention_forward_lse(torch::Tensor Q,
     return forward_impl(Q, K, V, window_size, global_tokens, scale, true);
 }
 
-std::vector<torch::Tensor> sliding_window_attention_forward_typed(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
-                                                                  int64_t window_size,
-                                                                  std::vector<int64_t> global_tokens, double scale,
-                                                                  c10::ScalarType out_dtype, bool want_lse) {
-    return forward_impl(Q, K, V, window_size, global_tokens, scale, want_lse, out_dtype);
+std::vector<torch::Tensor> sliding_window_attention_forward_ex(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                                                               int64_t window_size, std::vector<int64_t> global_tokens,
+                                                               double scale, c10::ScalarType out_dtype, bool causal,
+                                                               bool want_lse) {
+    return forward_impl(Q, K, V, window_size, global_tokens, scale, want_lse, out_dtype, causal);
 }
 
 int device_error() {
@@ -129,10 +131,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("sliding_window_attention_forward_lse", &sliding_window_attention_forward_lse,
           "Forward returning (O, LSE); LSE is the natural-log log-sum-exp per query row", py::arg("Q"),
           py::arg("K"), py::arg("V"), py::arg("window_size"), py::arg("global_tokens"), py::arg("scale"));
-    m.def("sliding_window_attention_forward_typed", &sliding_window_attention_forward_typed,
-          "Forward with the output in out_dtype (float32, float16 or bfloat16); returns [O] or [O, LSE]",
+    m.def("sliding_window_attention_forward_ex", &sliding_window_attention_forward_ex,
+          "Forward with the output in out_dtype (float32, float16 or bfloat16), optionally causal (keys j <= i); "
+          "returns [O] or [O, LSE]",
           py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("window_size"), py::arg("global_tokens"),
-          py::arg("scale"), py::arg("out_dtype"), py::arg("want_lse"));
+          py::arg("scale"), py::arg("out_dtype"), py::arg("causal"), py::arg("want_lse"));
     m.def("device_error", &device_error, "Read and clear the device-side error word (synchronises)");
     m.attr("abi_version") = lca_abi_version();
 }

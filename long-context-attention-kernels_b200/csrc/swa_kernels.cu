@@ -240,7 +240,8 @@ __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
         un.active[0] = true;
         un.active[1] = q0 + BM < p.n;
         un.kstart = p.q_off + q0 - p.lead;
-        un.nA = (p.lead + p.window + BM + BN - 1) / BN;
+        // causal: A's rows [q0, q0 + 127] need keys up to q0 + 127 only
+        un.nA = p.causal ? (p.lead + BM - 1) / BN + 1 : (p.lead + p.window + BM + BN - 1) / BN;
         const int p_first = un.kstart < p.key_lo ? (p.key_lo - un.kstart) / BN : 0;
         int p_last = un.active[1] ? un.nA : un.nA - 1;
         const int p_overlap_last = (p.key_hi - 1 - un.kstart) / BN;
@@ -694,9 +695,16 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
             int jlo = p.gk_lo, jhi = p.gk_lo + p.gk_n - 1;
             // run [g_lo, g_hi) of sorted global indices inside the row's band (band units)
             int g_lo = 0, g_hi = 0;
-            if (!un.grow) {
+            if (un.grow) {
+                // causal: a global row sees the keys up to its own token
+                if (p.causal && qi < p.num_global) {
+                    const int g_tok = (gidx_in_smem ? sGidx : p.gidx)[qi];
+                    if (g_tok < jhi) jhi = g_tok;
+                }
+            } else {
                 jlo = qa - p.window > 0 ? qa - p.window : 0;
                 jhi = (qa + p.window < p.n_total - 1) ? qa + p.window : p.n_total - 1;
+                if (p.causal && qa < jhi) jhi = qa;  // causal band [i - w, i]
                 if (p.g_tiles > 0) {
                     // first global at or after the band's start, then the run inside the band
                     // (a few entries at most unless globals are dense: then a second search)
@@ -747,6 +755,10 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                             hi = p.num_global - 1 - col0;
                             h_lo = g_lo - col0;
                             h_hi = g_hi - col0;
+                            if (p.causal) {  // only the globals before the band: the rest are in it or after i
+                                hi = g_lo - 1 - col0;
+                                h_lo = h_hi = 0;
+                            }
                         } else {
                             lo = jlo - col0;
                             hi = jhi - col0;

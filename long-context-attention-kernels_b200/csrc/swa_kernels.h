@@ -80,6 +80,8 @@ struct MainParams {
     int* err;         // device error word (first error wins)
     unsigned long long timeout_ns;  // per-wait budget
     int out16;        // band rows' output type: 0 fp32, kOut16F16 fp16, kOut16BF16 bf16
+    int causal;       // only keys j <= i (whole-sequence problems): band [i - w, i], global keys
+                      // before the band, global rows up to themselves
 };
 constexpr int kOut16F16 = 1;
 constexpr int kOut16BF16 = 2;

@@ -51,6 +51,21 @@ def _reference_sliding_window_attention(
     return torch.einsum("bhqk,bhkd->bhqd", torch.softmax(scores, dim=-1), V.float())
 
 
+def _dense_causal_attention(Q, K, V, window_size, global_tokens, scale):
+    """The dense definition above intersected with j <= i (``causal=True`` together with
+    ``force_reference=True``): the reference's mask, then its upper triangle removed."""
+    seq_len = Q.shape[2]
+    idx = torch.arange(seq_len, device=Q.device)
+    band = (idx[:, None] - idx[None, :]).abs() <= window_size
+    is_global = torch.zeros(seq_len, dtype=torch.bool, device=Q.device)
+    if len(global_tokens) > 0:
+        is_global[list(global_tokens)] = True
+    visible = (band | is_global[None, :] | is_global[:, None]) & (idx[None, :] <= idx[:, None])
+    scores = torch.einsum("bhqd,bhkd->bhqk", Q.float(), K.float()) * scale
+    scores = scores.masked_fill(~visible[None, None, :, :], float("-inf"))
+    return torch.einsum("bhqk,bhkd->bhqd", torch.softmax(scores, dim=-1), V.float())
+
+
 def _prepare(Q: torch.Tensor, window_size: int, global_tokens: Sequence[int], scale):
     if scale is None:
         scale = 1.0 / math.sqrt(Q.shape[-1])
@@ -72,6 +87,7 @@ def sliding_window_attention(
     scale: float | None = None,
     force_reference: bool = False,
     out_dtype: torch.dtype | None = None,
+    causal: bool = False,
 ) -> torch.Tensor:
     """Longformer-style sparse attention forward.
 
@@ -82,18 +98,21 @@ def sliding_window_attention(
     Returns a new fp32 tensor [batch, heads, seq_len, head_dim] on Q's device, computed
     on the current CUDA stream.  ``out_dtype`` (an addition; the reference always returns
     fp32) may be torch.float16 or torch.bfloat16: the same fp32-accumulated result,
-    rounded to that type by the kernel, with half the output bytes.
+    rounded to that type by the kernel, with half the output bytes.  ``causal=True`` (also
+    an addition) keeps only keys j <= i: the band becomes [i - window_size, i], a global
+    key is seen by the rows at or after it, a global row sees the keys up to itself.
     """
     if force_reference:
         if scale is None:
             scale = 1.0 / math.sqrt(Q.shape[-1])
-        out = _reference_sliding_window_attention(Q, K, V, window_size, global_tokens, scale)
+        dense = _dense_causal_attention if causal else _reference_sliding_window_attention
+        out = dense(Q, K, V, window_size, global_tokens, scale)
         return out if out_dtype in (None, torch.float32) else out.to(out_dtype)
     scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32):
+    if out_dtype in (None, torch.float32) and not causal:
         return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
-    return extension().sliding_window_attention_forward_typed(Q, K, V, window_size, tokens, scale, out_dtype,
-                                                              False)[0]
+    return extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
+                                                           out_dtype or torch.float32, bool(causal), False)[0]
 
 
 def sliding_window_attention_with_lse(
@@ -104,6 +123,7 @@ def sliding_window_attention_with_lse(
     global_tokens: Sequence[int] = (),
     scale: float | None = None,
     out_dtype: torch.dtype | None = None,
+    causal: bool = False,
 ):
     """As :func:`sliding_window_attention`, also returning the per-row log-sum-exp.
 
@@ -112,11 +132,11 @@ def sliding_window_attention_with_lse(
     or a cross-shard merge needs).  No counterpart in the reference.
     """
     scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32):
+    if out_dtype in (None, torch.float32) and not causal:
         out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
     else:
-        out, lse = extension().sliding_window_attention_forward_typed(Q, K, V, window_size, tokens, scale,
-                                                                      out_dtype, True)
+        out, lse = extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
+                                                                   out_dtype or torch.float32, bool(causal), True)
     return out, lse
 
 

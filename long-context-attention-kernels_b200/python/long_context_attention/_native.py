@@ -73,6 +73,7 @@ class CABI:
     DTYPE_F16 = 0
     DTYPE_BF16 = 1
     DTYPE_F32 = 2
+    FLAG_CAUSAL = 1
 
     def __init__(self, path: str = LIB_PATH):
         if not os.path.exists(path):
@@ -93,9 +94,9 @@ class CABI:
         lib.lca_swa_forward.restype = ctypes.c_int
         lib.lca_swa_forward.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64, ctypes.c_float,
                                         ctypes.POINTER(i64), i64, vp, sz, vp]
-        lib.lca_swa_forward_typed.restype = ctypes.c_int
-        lib.lca_swa_forward_typed.argtypes = [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, i64, i64, i64,
-                                              ctypes.c_float, ctypes.POINTER(i64), i64, vp, sz, vp]
+        lib.lca_swa_forward_ex.restype = ctypes.c_int
+        lib.lca_swa_forward_ex.argtypes = [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, i64, i64, i64,
+                                           ctypes.c_float, ctypes.c_int, ctypes.POINTER(i64), i64, vp, sz, vp]
         lib.lca_swa_forward_noalloc.restype = ctypes.c_int
         lib.lca_swa_forward_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64,
                                                 ctypes.c_float, ctypes.POINTER(i64), i64, vp]
@@ -151,13 +152,13 @@ class CABI:
         return self.lib.lca_swa_forward(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim,
                                         window, ctypes.c_float(scale), arr, n, ws_ptr, ws_bytes, stream_ptr)
 
-    def forward_typed(self, q_ptr, k_ptr, v_ptr, o_ptr, out_dtype, lse_ptr, dtype, batch, heads, seq_len, head_dim,
-                      window, scale, tokens, ws_ptr, ws_bytes, stream_ptr) -> int:
+    def forward_ex(self, q_ptr, k_ptr, v_ptr, o_ptr, out_dtype, lse_ptr, dtype, batch, heads, seq_len, head_dim,
+                   window, scale, flags, tokens, ws_ptr, ws_bytes, stream_ptr) -> int:
         n = len(tokens)
         arr = (ctypes.c_int64 * max(n, 1))(*tokens)
-        return self.lib.lca_swa_forward_typed(q_ptr, k_ptr, v_ptr, o_ptr, out_dtype, lse_ptr, dtype, batch, heads,
-                                              seq_len, head_dim, window, ctypes.c_float(scale), arr, n, ws_ptr,
-                                              ws_bytes, stream_ptr)
+        return self.lib.lca_swa_forward_ex(q_ptr, k_ptr, v_ptr, o_ptr, out_dtype, lse_ptr, dtype, batch, heads,
+                                           seq_len, head_dim, window, ctypes.c_float(scale), flags, arr, n, ws_ptr,
+                                           ws_bytes, stream_ptr)
 
     def forward_noalloc(self, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim, window,
                         scale, tokens, stream_ptr) -> int:

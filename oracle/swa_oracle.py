@@ -18,7 +18,9 @@ row block by row block, so that it also runs at sequence lengths where the dense
   oracle defaults to fp64 so its own rounding sits far below the tolerances it checks.
 
 It additionally returns the natural-log log-sum-exp of each row's visible scaled scores
-(the reference computes it implicitly inside softmax).
+(the reference computes it implicitly inside softmax), and takes `causal=True` for the
+one-sided variant this package adds (no counterpart in the reference): the reference's
+mask intersected with j <= i (every row keeps at least its own key).
 
 Parity of this restatement is pinned against outputs of the reference itself: see
 tests/golden/make_golden.py (generates fixtures by importing the reference) and
@@ -43,8 +45,10 @@ def normalize_global_tokens(global_tokens: Sequence[int], seq_len: int) -> np.nd
     return np.asarray(sorted(out), dtype=np.int64)
 
 
-def visible_rows(rows: np.ndarray, seq_len: int, window_size: int, global_idx: np.ndarray) -> np.ndarray:
-    """Boolean [len(rows), seq_len] mask rows (python/long_context_attention/__init__.py:39-47)."""
+def visible_rows(rows: np.ndarray, seq_len: int, window_size: int, global_idx: np.ndarray,
+                 causal: bool = False) -> np.ndarray:
+    """Boolean [len(rows), seq_len] mask rows (python/long_context_attention/__init__.py:39-47),
+    intersected with j <= i when `causal`."""
     rows = np.asarray(rows, dtype=np.int64)
     keys = np.arange(seq_len, dtype=np.int64)
     mask = np.abs(rows[:, None] - keys[None, :]) <= window_size
@@ -53,11 +57,14 @@ def visible_rows(rows: np.ndarray, seq_len: int, window_size: int, global_idx: n
         is_global[global_idx] = True
     mask |= is_global[None, :]
     mask |= is_global[rows][:, None]
+    if causal:
+        mask &= keys[None, :] <= rows[:, None]
     return mask
 
 
 def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[int], scale: float,
-                             rows: Sequence[int] | None = None, dtype=np.float64, block_rows: int = 256):
+                             rows: Sequence[int] | None = None, dtype=np.float64, block_rows: int = 256,
+                             causal: bool = False):
     """Dense-mask attention on the CPU.
 
     Q, K, V: arrays [B, H, n, d] (any float dtype; converted to `dtype`).
@@ -80,7 +87,7 @@ def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[
                 r = rows[s:s + block_rows]
                 q = Q[b, h, r].astype(dtype, copy=False)
                 scores = (q @ k.T) * dtype(scale)
-                scores = np.where(visible_rows(r, n, window_size, g), scores, -np.inf)
+                scores = np.where(visible_rows(r, n, window_size, g, causal), scores, -np.inf)
                 m = scores.max(axis=1, keepdims=True)
                 p = np.exp(scores - m)
                 l = p.sum(axis=1, keepdims=True)

@@ -60,13 +60,16 @@ def test_typed_forward_validation_before_device_work():
 
     def typed(out_dtype, **kw):
         args = dict(q_ptr=None, k_ptr=None, v_ptr=None, o_ptr=None, out_dtype=out_dtype, lse_ptr=None,
-                    dtype=c.DTYPE_BF16, batch=1, heads=1, seq_len=128, head_dim=64, window=4, scale=0.125, tokens=[],
-                    ws_ptr=None, ws_bytes=0, stream_ptr=None)
+                    dtype=c.DTYPE_BF16, batch=1, heads=1, seq_len=128, head_dim=64, window=4, scale=0.125, flags=0,
+                    tokens=[], ws_ptr=None, ws_bytes=0, stream_ptr=None)
         args.update(kw)
-        return c.forward_typed(**args)
+        return c.forward_ex(**args)
 
     assert typed(7) == c.ERR_UNSUPPORTED
     assert "out_dtype" in c.last_error()
+    assert typed(c.DTYPE_F32, flags=2) == c.ERR_INVALID_ARGUMENT
+    assert "flags" in c.last_error()
     for dt in (c.DTYPE_F32, c.DTYPE_F16, c.DTYPE_BF16):
-        assert typed(dt, batch=0) == c.OK
-        assert typed(dt) == c.ERR_INVALID_ARGUMENT  # NULL tensors, before any launch
+        for flags in (0, c.FLAG_CAUSAL):
+            assert typed(dt, batch=0, flags=flags) == c.OK
+            assert typed(dt, flags=flags) == c.ERR_INVALID_ARGUMENT  # NULL tensors, before any launch

@@ -41,7 +41,7 @@ def test_out_dtype_matches_rounded_fp32(out_dtype, in_dtype, d, n, w, g):
 
 
 def test_out_dtype_through_c_abi():
-    """lca_swa_forward_typed with caller-owned buffers gives the same bits as the extension."""
+    """lca_swa_forward_ex with caller-owned buffers gives the same bits as the extension."""
     cabi = _native.cabi()
     B, H, n, d, w, g = 1, 3, 600, 64, 200, [7, 450]
     q, k, v = (t.cuda() for t in make_inputs(9, B, H, n, d, torch.bfloat16))
@@ -51,8 +51,8 @@ def test_out_dtype_through_c_abi():
     st, ws_bytes = cabi.workspace_size(B, H, n, d, w, len(gl), cabi.DTYPE_BF16)
     ws = torch.empty(max(ws_bytes, 1), device="cuda", dtype=torch.uint8)
     stream = torch.cuda.current_stream().cuda_stream
-    st = cabi.forward_typed(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), cabi.DTYPE_BF16, 0,
-                            cabi.DTYPE_BF16, B, H, n, d, w, 0.125, g, ws.data_ptr(), ws_bytes, stream)
+    st = cabi.forward_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), cabi.DTYPE_BF16, 0,
+                         cabi.DTYPE_BF16, B, H, n, d, w, 0.125, 0, g, ws.data_ptr(), ws_bytes, stream)
     assert st == cabi.OK, cabi.last_error()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)

@@ -88,3 +88,19 @@ def test_row_subset_equals_full():
     sub, ls = swa_oracle.sliding_window_attention(q, k, v, 20, [7, 299], 0.25, rows=rows)
     np.testing.assert_allclose(sub, full[:, :, rows], atol=1e-12)
     np.testing.assert_allclose(ls, lf[:, :, rows], atol=1e-12)
+
+
+def test_causal_oracle_is_the_dense_mask_with_the_upper_triangle_removed():
+    """The oracle's causal option against the dense torch definition of the package
+    (the reference's mask intersected with j <= i), on small shapes with global tokens."""
+    import torch
+
+    from long_context_attention import _dense_causal_attention
+    for n, w, g in [(64, 4, [0, 63]), (100, 200, [5]), (37, 0, [-1, 10])]:
+        gen = torch.Generator().manual_seed(n)
+        q, k, v = (torch.randn(1, 2, n, 16, generator=gen) for _ in range(3))
+        want = _dense_causal_attention(q, k, v, w, g, 0.3).numpy()
+        got, lse = swa_oracle.sliding_window_attention(q.numpy(), k.numpy(), v.numpy(), w, g, 0.3, causal=True)
+        assert np.abs(got - want).max() < 2e-6
+        # every row keeps at least its own key
+        assert np.isfinite(lse).all()
