@@ -130,20 +130,27 @@ enum {
     LCA_FLAG_CAUSAL = 1
 };
 
+/* Most heads that lca_swa_forward_ex accepts radii of their own for. */
+#define LCA_MAX_HEAD_WINDOWS 256
+
 /*
  * lca_swa_forward with options, none of which the reference has (its extension always
- * returns fp32 and has no causal mode, csrc/bindings.cpp:31-73):
+ * returns fp32, has no causal mode and one window for every head, csrc/bindings.cpp:31-73):
  *   out_dtype    type of `out` ([batch, heads, seq_len, head_dim], 16-byte aligned):
  *                LCA_DTYPE_F32, or LCA_DTYPE_F16 / LCA_DTYPE_BF16 -- the same fp32-accumulated
  *                result rounded to nearest, with half the output bytes.  `lse` stays fp32.
+ *   head_window_sizes  NULL, or a HOST array of `heads` band radii (each >= 0): head h of
+ *                every batch uses head_window_sizes[h] in place of window_size (which is then
+ *                ignored).  At most LCA_MAX_HEAD_WINDOWS heads.
  *   flags        0 or LCA_FLAG_CAUSAL.
  * The other arguments are lca_swa_forward's; lca_swa_forward(...) is
- * lca_swa_forward_ex(..., LCA_DTYPE_F32, ..., 0, ...).
+ * lca_swa_forward_ex(..., LCA_DTYPE_F32, ..., NULL, ..., 0, ...).
  */
 LCA_API int lca_swa_forward_ex(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
                                int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
-                               int64_t window_size, float scale, int flags, const int64_t* global_tokens,
-                               int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream);
+                               int64_t window_size, const int64_t* head_window_sizes, float scale, int flags,
+                               const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /*
  * Bytes of the fixed device scratch array used by lca_swa_forward_noalloc.

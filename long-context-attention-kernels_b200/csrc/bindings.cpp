@@ -34,7 +34,7 @@ void raise_status(int st, const char* what) {
 std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Tensor& K, const torch::Tensor& V,
                                         int64_t window_size, const std::vector<int64_t>& globals, double scale,
                                         bool want_lse, c10::ScalarType out_type = torch::kFloat32,
-                                        bool causal = false) {
+                                        bool causal = false, const std::vector<int64_t>& head_windows = {}) {
     check_input(Q, "Q");
     check_input(K, "K");
     check_input(V, "V");
@@ -46,6 +46,9 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
     const int64_t batch = Q.size(0), heads = Q.size(1), seq_len = Q.size(2), head_dim = Q.size(3);
     TORCH_CHECK(head_dim == 64 || head_dim == 128, "head_dim must be 64 or 128 (got ", head_dim, ")");
     TORCH_CHECK(window_size >= 0, "window_size must be >= 0 (got ", window_size, ")");
+    TORCH_CHECK(head_windows.empty() || (int64_t)head_windows.size() == Q.size(1),
+                "window_size per head needs one radius per head (got ", head_windows.size(), " for ", Q.size(1),
+                " heads)");
     TORCH_CHECK(out_type == torch::kFloat32 || out_type == torch::kFloat16 || out_type == torch::kBFloat16,
                 "out_dtype must be float32, float16 or bfloat16");
 
@@ -60,7 +63,9 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
     raise_status(lca_normalize_global_tokens(globals.data(), (int64_t)globals.size(), seq_len, norm.data(), &G),
                  "global_tokens");
     size_t ws_bytes = 0;
-    raise_status(lca_swa_workspace_size(batch, heads, seq_len, head_dim, window_size, G, dtype, &ws_bytes),
+    int64_t wmax = window_size;
+    for (int64_t hw : head_windows) wmax = std::max(wmax, hw);
+    raise_status(lca_swa_workspace_size(batch, heads, seq_len, head_dim, wmax, G, dtype, &ws_bytes),
                  "workspace size");
     torch::Tensor ws;
     void* ws_ptr = nullptr;
@@ -73,7 +78,8 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
                           : (out_type == torch::kBFloat16 ? LCA_DTYPE_BF16 : LCA_DTYPE_F16);
     const int st = lca_swa_forward_ex(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), out_dtype,
                                       want_lse ? L.data_ptr<float>() : nullptr, dtype, batch, heads, seq_len, head_dim,
-                                      window_size, static_cast<float>(scale), causal ? LCA_FLAG_CAUSAL : 0,
+                                      window_size, head_windows.empty() ? nullptr : head_windows.data(),
+                                      static_cast<float>(scale), causal ? LCA_FLAG_CAUSAL : 0,
                                       globals.data(), (int64_t)globals.size(), ws_ptr, ws_bytes,
                                       static_cast<void*>(stream));
     raise_status(st, "sliding_window_attention_forward");
@@ -109,8 +115,8 @@ std::vector<torch::Tensor> sliding_window_attention_forward_lse(torch::Tensor Q,
 std::vector<torch::Tensor> sliding_window_attention_forward_ex(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
                                                                int64_t window_size, std::vector<int64_t> global_tokens,
                                                                double scale, c10::ScalarType out_dtype, bool causal,
-                                                               bool want_lse) {
-    return forward_impl(Q, K, V, window_size, global_tokens, scale, want_lse, out_dtype, causal);
+                                                               bool want_lse, std::vector<int64_t> head_windows) {
+    return forward_impl(Q, K, V, window_size, global_tokens, scale, want_lse, out_dtype, causal, head_windows);
 }
 
 int device_error() {
@@ -135,7 +141,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "Forward with the output in out_dtype (float32, float16 or bfloat16), optionally causal (keys j <= i); "
           "returns [O] or [O, LSE]",
           py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("window_size"), py::arg("global_tokens"),
-          py::arg("scale"), py::arg("out_dtype"), py::arg("causal"), py::arg("want_lse"));
+          py::arg("scale"), py::arg("out_dtype"), py::arg("causal"), py::arg("want_lse"),
+          py::arg("head_windows") = std::vector<int64_t>{});
     m.def("device_error", &device_error, "Read and clear the device-side error word (synchronises)");
     m.attr("abi_version") = lca_abi_version();
 }

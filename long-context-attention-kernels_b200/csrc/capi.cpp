@@ -125,6 +125,7 @@ struct Problem {
     int dtype = LCA_DTYPE_BF16;
     int out_dtype = LCA_DTYPE_F32;  // type of out (16-bit only through lca_swa_forward_ex)
     bool causal = false;            // LCA_FLAG_CAUSAL (whole-sequence problems only)
+    std::vector<int> head_window;   // a radius per head (whole-sequence problems), else empty
     float scale = 1.f;
     std::vector<int32_t> gl;  // sorted unique global indices (absolute)
     int64_t halo() const { return sharded && world > 1 ? window : 0; }
@@ -620,6 +621,8 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     p.timeout_ns = wait_timeout_ns();
     p.out16 = P.out_dtype == LCA_DTYPE_F32 ? 0 : (P.out_dtype == LCA_DTYPE_BF16 ? lca::kOut16BF16 : lca::kOut16F16);
     p.causal = P.causal ? 1 : 0;
+    p.n_head_windows = (int)P.head_window.size();
+    for (size_t h = 0; h < P.head_window.size(); ++h) p.head_window[h] = P.head_window[h];
     if (P.G > 0) {
         p.g_tiles = L.g_tiles;
         p.n_splits = L.n_splits;
@@ -772,21 +775,42 @@ int lca_swa_forward(const void* q, const void* k, const void* v, float* out, flo
                     float scale, const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
                     size_t workspace_bytes, void* stream_ptr) {
     return lca_swa_forward_ex(q, k, v, out, LCA_DTYPE_F32, lse, dtype, batch, heads, seq_len, head_dim, window_size,
-                              scale, 0, global_tokens, num_global_tokens, workspace, workspace_bytes, stream_ptr);
+                              nullptr, scale, 0, global_tokens, num_global_tokens, workspace, workspace_bytes,
+                              stream_ptr);
 }
 
 int lca_swa_forward_ex(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse, int dtype,
                        int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size,
-                       float scale, int flags, const int64_t* global_tokens, int64_t num_global_tokens,
-                       void* workspace, size_t workspace_bytes, void* stream_ptr) {
+                       const int64_t* head_window_sizes, float scale, int flags, const int64_t* global_tokens,
+                       int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream_ptr) {
     g_last_error.clear();
     if (out_dtype != LCA_DTYPE_F32 && out_dtype != LCA_DTYPE_F16 && out_dtype != LCA_DTYPE_BF16)
         return fail(LCA_ERR_UNSUPPORTED, "out_dtype %d is not supported (fp32, fp16 or bf16)", out_dtype);
     if ((flags & ~LCA_FLAG_CAUSAL) != 0) return fail(LCA_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    std::vector<int> head_window;
+    if (head_window_sizes != nullptr) {
+        // one radius per head: the largest sizes the workspace, each head's own drives its units
+        if (heads > LCA_MAX_HEAD_WINDOWS)
+            return fail(LCA_ERR_UNSUPPORTED, "radii of their own for %lld heads (at most %d)", (long long)heads,
+                        LCA_MAX_HEAD_WINDOWS);
+        int64_t wmax = 0;
+        bool uniform = true;
+        for (int64_t h = 0; h < heads; ++h) {
+            if (head_window_sizes[h] < 0)
+                return fail(LCA_ERR_INVALID_ARGUMENT, "head_window_sizes[%lld] = %lld must be >= 0", (long long)h,
+                            (long long)head_window_sizes[h]);
+            wmax = std::max(wmax, head_window_sizes[h]);
+            uniform = uniform && head_window_sizes[h] == head_window_sizes[0];
+        }
+        window_size = wmax;
+        if (!uniform)
+            for (int64_t h = 0; h < heads; ++h) head_window.push_back((int)std::min(head_window_sizes[h], seq_len));
+    }
     Problem P;
     int st = parse_common(P, dtype, batch, heads, seq_len, head_dim, window_size, scale, global_tokens,
                           num_global_tokens);
     if (st != LCA_OK) return st;
+    P.head_window = std::move(head_window);
     P.out_dtype = out_dtype;
     P.causal = (flags & LCA_FLAG_CAUSAL) != 0;
     if (P.bh == 0 || P.n == 0) return LCA_OK;  // nothing to compute

@@ -201,6 +201,7 @@ struct Unit {
     int num_band;     // band: issued band tiles
     int split;        // grow: split index
     int k0;           // grow: first key of the split
+    int w;            // band: the head's radius
 };
 
 struct Tile {
@@ -229,6 +230,7 @@ __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
         un.active[0] = true;
         un.active[1] = un.ntiles >= 2;
         un.kstart = un.p_lo = un.nA = un.num_band = 0;
+        un.w = 0;
     } else {
         un.grow = false;
         un.split = un.k0 = 0;
@@ -239,9 +241,12 @@ __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
         un.qrow[1] = q0 + BM;
         un.active[0] = true;
         un.active[1] = q0 + BM < p.n;
-        un.kstart = p.q_off + q0 - p.lead;
+        // the head's own radius, which is also its lead, when heads have radii of their own
+        un.w = p.n_head_windows > 0 ? p.head_window[un.bh % p.n_head_windows] : p.window;
+        const int lead = p.n_head_windows > 0 ? un.w : p.lead;
+        un.kstart = p.q_off + q0 - lead;
         // causal: A's rows [q0, q0 + 127] need keys up to q0 + 127 only
-        un.nA = p.causal ? (p.lead + BM - 1) / BN + 1 : (p.lead + p.window + BM + BN - 1) / BN;
+        un.nA = p.causal ? (lead + BM - 1) / BN + 1 : (lead + un.w + BM + BN - 1) / BN;
         const int p_first = un.kstart < p.key_lo ? (p.key_lo - un.kstart) / BN : 0;
         int p_last = un.active[1] ? un.nA : un.nA - 1;
         const int p_overlap_last = (p.key_hi - 1 - un.kstart) / BN;
@@ -702,8 +707,9 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                     if (g_tok < jhi) jhi = g_tok;
                 }
             } else {
-                jlo = qa - p.window > 0 ? qa - p.window : 0;
-                jhi = (qa + p.window < p.n_total - 1) ? qa + p.window : p.n_total - 1;
+                const int w = un.w;
+                jlo = qa - w > 0 ? qa - w : 0;
+                jhi = (qa + w < p.n_total - 1) ? qa + w : p.n_total - 1;
                 if (p.causal && qa < jhi) jhi = qa;  // causal band [i - w, i]
                 if (p.g_tiles > 0) {
                     // first global at or after the band's start, then the run inside the band
@@ -712,11 +718,11 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                     int a = 0, b = p.num_global;
                     while (a < b) {
                         const int mid = (a + b) >> 1;
-                        if (gl[mid] < qa - p.window) a = mid + 1; else b = mid;
+                        if (gl[mid] < qa - w) a = mid + 1; else b = mid;
                     }
                     g_lo = a;
                     int scan = 0;
-                    while (a < p.num_global && scan < 4 && gl[a] <= qa + p.window) {
+                    while (a < p.num_global && scan < 4 && gl[a] <= qa + w) {
                         ++a;
                         ++scan;
                     }
@@ -724,7 +730,7 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                         b = p.num_global;
                         while (a < b) {
                             const int mid = (a + b) >> 1;
-                            if (gl[mid] <= qa + p.window) a = mid + 1; else b = mid;
+                            if (gl[mid] <= qa + w) a = mid + 1; else b = mid;
                         }
                     }
                     g_hi = a;

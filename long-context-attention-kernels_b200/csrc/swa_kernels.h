@@ -28,6 +28,7 @@ struct PeerSignals {
     unsigned int ticket;            // merge blocks done in the current step
 };
 constexpr int kGatherChunk = 1024;    // global indices passed per gather launch
+constexpr int kMaxHeadWindows = 256;  // heads with a radius of their own (kernel parameter space)
 
 struct TensorMaps {
     CUtensorMap q, k, v;     // inputs [bh][n][d] (bf16 / f16), box 64 x 128 rows, 128B swizzle
@@ -82,6 +83,11 @@ struct MainParams {
     int out16;        // band rows' output type: 0 fp32, kOut16F16 fp16, kOut16BF16 bf16
     int causal;       // only keys j <= i (whole-sequence problems): band [i - w, i], global keys
                       // before the band, global rows up to themselves
+    // A band radius per head (whole-sequence problems): head h of every batch uses
+    // head_window[h] (each <= window) in place of window, with lead = its own radius;
+    // n_head_windows = 0 means one radius for all.
+    int n_head_windows;  // = heads, or 0
+    int head_window[kMaxHeadWindows];
 };
 constexpr int kOut16F16 = 1;
 constexpr int kOut16BF16 = 2;

@@ -66,7 +66,31 @@ def _dense_causal_attention(Q, K, V, window_size, global_tokens, scale):
     return torch.einsum("bhqk,bhkd->bhqd", torch.softmax(scores, dim=-1), V.float())
 
 
-def _prepare(Q: torch.Tensor, window_size: int, global_tokens: Sequence[int], scale):
+def _head_windows(window_size, heads: int):
+    """(radius, per-head radii or []): an int applies to every head; a sequence (or 1-D
+    tensor) gives one radius per head."""
+    if isinstance(window_size, torch.Tensor):
+        window_size = window_size.tolist()
+    if isinstance(window_size, (list, tuple)):
+        radii = [int(w) for w in window_size]
+        if len(radii) != heads:
+            raise ValueError(f"window_size per head needs {heads} radii, got {len(radii)}")
+        return max(radii, default=0), radii
+    return int(window_size), []
+
+
+def _dense(Q, K, V, window_size, global_tokens, scale, causal: bool):
+    """The dense definitions for ``force_reference=True``: the reference's (or its causal
+    restriction), head by head when the heads have radii of their own."""
+    dense = _dense_causal_attention if causal else _reference_sliding_window_attention
+    _, radii = _head_windows(window_size, Q.shape[1])
+    if not radii:
+        return dense(Q, K, V, int(window_size), global_tokens, scale)
+    return torch.cat([dense(Q[:, h:h + 1], K[:, h:h + 1], V[:, h:h + 1], radii[h], global_tokens, scale)
+                      for h in range(Q.shape[1])], dim=1)
+
+
+def _prepare(Q: torch.Tensor, window_size, global_tokens: Sequence[int], scale):
     if scale is None:
         scale = 1.0 / math.sqrt(Q.shape[-1])
     if not Q.is_cuda:
@@ -75,7 +99,8 @@ def _prepare(Q: torch.Tensor, window_size: int, global_tokens: Sequence[int], sc
             "pass force_reference=True for the dense CPU definition"
         )
     tokens = [int(t) for t in global_tokens]
-    return float(scale), int(window_size), tokens
+    window, radii = _head_windows(window_size, Q.shape[1])
+    return float(scale), window, tokens, radii
 
 
 def sliding_window_attention(
@@ -92,7 +117,8 @@ def sliding_window_attention(
     """Longformer-style sparse attention forward.
 
     Q, K, V: [batch, heads, seq_len, head_dim], fp16 or bf16, CUDA, contiguous,
-    head_dim 64 or 128.  window_size: band radius (|i - j| <= window_size is visible).
+    head_dim 64 or 128.  window_size: band radius (|i - j| <= window_size is visible), or one
+    radius per head (a sequence of ``heads`` ints; an addition to the reference's int).
     global_tokens: token indices with full rows and columns (negative indices count from
     the end; duplicates are harmless).  scale defaults to 1/sqrt(head_dim).
     Returns a new fp32 tensor [batch, heads, seq_len, head_dim] on Q's device, computed
@@ -105,14 +131,14 @@ def sliding_window_attention(
     if force_reference:
         if scale is None:
             scale = 1.0 / math.sqrt(Q.shape[-1])
-        dense = _dense_causal_attention if causal else _reference_sliding_window_attention
-        out = dense(Q, K, V, window_size, global_tokens, scale)
+        out = _dense(Q, K, V, window_size, global_tokens, scale, causal)
         return out if out_dtype in (None, torch.float32) else out.to(out_dtype)
-    scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32) and not causal:
+    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
+    if out_dtype in (None, torch.float32) and not causal and not radii:
         return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
     return extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
-                                                           out_dtype or torch.float32, bool(causal), False)[0]
+                                                           out_dtype or torch.float32, bool(causal), False,
+                                                           radii)[0]
 
 
 def sliding_window_attention_with_lse(
@@ -131,12 +157,13 @@ def sliding_window_attention_with_lse(
     sum of exp(scale * q.k) over each row's visible keys (the quantity a backward pass
     or a cross-shard merge needs).  No counterpart in the reference.
     """
-    scale, window_size, tokens = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32) and not causal:
+    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
+    if out_dtype in (None, torch.float32) and not causal and not radii:
         out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
     else:
         out, lse = extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
-                                                                   out_dtype or torch.float32, bool(causal), True)
+                                                                   out_dtype or torch.float32, bool(causal), True,
+                                                                   radii)
     return out, lse
 
 

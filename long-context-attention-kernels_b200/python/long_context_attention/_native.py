@@ -96,7 +96,8 @@ class CABI:
                                         ctypes.POINTER(i64), i64, vp, sz, vp]
         lib.lca_swa_forward_ex.restype = ctypes.c_int
         lib.lca_swa_forward_ex.argtypes = [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, i64, i64, i64,
-                                           ctypes.c_float, ctypes.c_int, ctypes.POINTER(i64), i64, vp, sz, vp]
+                                           ctypes.POINTER(i64), ctypes.c_float, ctypes.c_int, ctypes.POINTER(i64), i64,
+                                           vp, sz, vp]
         lib.lca_swa_forward_noalloc.restype = ctypes.c_int
         lib.lca_swa_forward_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64,
                                                 ctypes.c_float, ctypes.POINTER(i64), i64, vp]
@@ -153,12 +154,13 @@ class CABI:
                                         window, ctypes.c_float(scale), arr, n, ws_ptr, ws_bytes, stream_ptr)
 
     def forward_ex(self, q_ptr, k_ptr, v_ptr, o_ptr, out_dtype, lse_ptr, dtype, batch, heads, seq_len, head_dim,
-                   window, scale, flags, tokens, ws_ptr, ws_bytes, stream_ptr) -> int:
+                   window, scale, flags, tokens, ws_ptr, ws_bytes, stream_ptr, head_windows=None) -> int:
         n = len(tokens)
         arr = (ctypes.c_int64 * max(n, 1))(*tokens)
+        hw = None if head_windows is None else (ctypes.c_int64 * max(len(head_windows), 1))(*head_windows)
         return self.lib.lca_swa_forward_ex(q_ptr, k_ptr, v_ptr, o_ptr, out_dtype, lse_ptr, dtype, batch, heads,
-                                           seq_len, head_dim, window, ctypes.c_float(scale), flags, arr, n, ws_ptr,
-                                           ws_bytes, stream_ptr)
+                                           seq_len, head_dim, window, hw, ctypes.c_float(scale), flags, arr, n,
+                                           ws_ptr, ws_bytes, stream_ptr)
 
     def forward_noalloc(self, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len, head_dim, window,
                         scale, tokens, stream_ptr) -> int:

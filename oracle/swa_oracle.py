@@ -67,7 +67,9 @@ def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[
                              causal: bool = False):
     """Dense-mask attention on the CPU.
 
-    Q, K, V: arrays [B, H, n, d] (any float dtype; converted to `dtype`).
+    Q, K, V: arrays [B, H, n, d] (any float dtype; converted to `dtype`).  window_size: one
+    radius, or a sequence of H radii (head h uses window_size[h]; a per-head window has no
+    counterpart in the reference).
     rows: query rows to compute (default: all).  Returns (O, LSE) with O [B, H, len(rows), d]
     and LSE [B, H, len(rows)] in `dtype`.
     """
@@ -79,6 +81,8 @@ def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[
     rows = np.arange(n, dtype=np.int64) if rows is None else np.asarray(rows, dtype=np.int64)
     out = np.empty((B, H, rows.size, d), dtype=dtype)
     lse = np.empty((B, H, rows.size), dtype=dtype)
+    windows = [int(window_size)] * H if np.isscalar(window_size) else [int(x) for x in window_size]
+    assert len(windows) == H, "one radius per head"
     for b in range(B):
         for h in range(H):
             k = K[b, h].astype(dtype, copy=False)
@@ -87,7 +91,7 @@ def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[
                 r = rows[s:s + block_rows]
                 q = Q[b, h, r].astype(dtype, copy=False)
                 scores = (q @ k.T) * dtype(scale)
-                scores = np.where(visible_rows(r, n, window_size, g, causal), scores, -np.inf)
+                scores = np.where(visible_rows(r, n, windows[h], g, causal), scores, -np.inf)
                 m = scores.max(axis=1, keepdims=True)
                 p = np.exp(scores - m)
                 l = p.sum(axis=1, keepdims=True)

@@ -73,3 +73,16 @@ def test_typed_forward_validation_before_device_work():
         for flags in (0, c.FLAG_CAUSAL):
             assert typed(dt, batch=0, flags=flags) == c.OK
             assert typed(dt, flags=flags) == c.ERR_INVALID_ARGUMENT  # NULL tensors, before any launch
+
+
+def test_head_window_validation_before_device_work():
+    c = _native.cabi()
+
+    def ex(head_windows, heads):
+        return c.forward_ex(None, None, None, None, c.DTYPE_F32, None, c.DTYPE_BF16, 1, heads, 128, 64, 4, 0.125, 0,
+                            [], None, 0, None, head_windows=head_windows)
+
+    assert ex([3, -1], 2) == c.ERR_INVALID_ARGUMENT
+    assert "head_window_sizes[1]" in c.last_error()
+    assert ex([1] * 257, 257) == c.ERR_UNSUPPORTED
+    assert ex([1, 2], 2) == c.ERR_INVALID_ARGUMENT  # NULL tensors, after the radii checked out

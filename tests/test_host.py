@@ -97,3 +97,27 @@ def test_header_documents_reference_interfaces():
     hdr = open(os.path.join(REPO, "include", "lca.h")).read()
     # the forward entry point cites the reference binding it replaces
     assert "csrc/bindings.cpp:31-73" in hdr
+
+
+def test_window_per_head_argument_and_oracle():
+    """One radius per head: the Python argument checks, and the oracle's per-head radii
+    against running it head by head with one radius each."""
+    import numpy as np
+    import pytest
+    import torch
+
+    from long_context_attention import _head_windows
+    from oracle import swa_oracle
+    assert _head_windows(5, 3) == (5, [])
+    assert _head_windows([1, 7, 2], 3) == (7, [1, 7, 2])
+    assert _head_windows(torch.tensor([4, 0]), 2) == (4, [4, 0])
+    with pytest.raises(ValueError):
+        _head_windows([1, 2], 3)
+    rng = np.random.default_rng(0)
+    q, k, v = (rng.standard_normal((1, 3, 80, 8)) for _ in range(3))
+    radii = [0, 9, 100]
+    got, lse = swa_oracle.sliding_window_attention(q, k, v, radii, [4, 70], 0.5)
+    for h, w in enumerate(radii):
+        want, want_lse = swa_oracle.sliding_window_attention(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], w, [4, 70],
+                                                             0.5)
+        assert np.array_equal(got[:, h:h + 1], want) and np.array_equal(lse[:, h:h + 1], want_lse)
