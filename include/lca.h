@@ -152,6 +152,46 @@ LCA_API int lca_swa_forward_ex(const void* q, const void* k, const void* v, void
                                const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* Most sequences one lca_swa_forward_varlen call takes. */
+#define LCA_MAX_SEQUENCES 512
+
+/*
+ * Packed variable-length sequences (no counterpart in the reference, which takes one
+ * length per call).  q, k, v, out: [1, heads, total_len, head_dim] with sequence s in
+ * rows [cu_seqlens[s], cu_seqlens[s + 1]) (num_seqs + 1 host offsets from 0 to total_len,
+ * non-decreasing, at most LCA_MAX_SEQUENCES sequences); lse: [1, heads, total_len] or NULL.
+ * Every sequence is its own problem: its bands, global keys and global rows stay inside
+ * it.  The global-token list applies to every non-empty sequence, indexed within it as the
+ * reference indexes one sequence (negative from its end; an index outside it returns
+ * LCA_ERR_INDEX).  Workspace: lca_swa_workspace_size(1, heads, total_len, head_dim,
+ * window, num_seqs * num_global_tokens, dtype) bytes (an upper bound).  The other arguments
+ * are lca_swa_forward_ex's.
+ */
+LCA_API int lca_swa_forward_varlen(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
+                                   int dtype, int64_t heads, int64_t total_len, int64_t head_dim, int64_t window_size,
+                                   const int64_t* head_window_sizes, float scale, int flags,
+                                   const int64_t* cu_seqlens, int64_t num_seqs, const int64_t* global_tokens,
+                                   int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Dilated sliding window (no counterpart in the reference; its README lists dilated windows
+ * as future work): key j is visible to query i iff |i - j| <= window_size * dilation and
+ * (i - j) is a multiple of dilation, or j or i is a global token.  seq_len must be a
+ * multiple of dilation; the causal flag is not supported with dilation > 1.  The forward
+ * reorders Q, K, V into residue order (row r + dilation * t to r * (seq_len / dilation) + t)
+ * inside the workspace, runs the banded kernels with each residue class as its own segment,
+ * and writes out / lse back in sequence order.  Workspace: lca_swa_dilated_workspace_size
+ * bytes, 256-byte aligned.  dilation == 1 is lca_swa_forward_ex.
+ */
+LCA_API int lca_swa_dilated_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                                           int64_t window_size, int64_t dilation, int64_t num_unique_global,
+                                           int dtype, int out_dtype, size_t* out_bytes);
+LCA_API int lca_swa_forward_dilated(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
+                                    int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                                    int64_t window_size, const int64_t* head_window_sizes, int64_t dilation,
+                                    float scale, int flags, const int64_t* global_tokens, int64_t num_global_tokens,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
 /*
  * Bytes of the fixed device scratch array used by lca_swa_forward_noalloc.
  */

@@ -34,7 +34,8 @@ void raise_status(int st, const char* what) {
 std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Tensor& K, const torch::Tensor& V,
                                         int64_t window_size, const std::vector<int64_t>& globals, double scale,
                                         bool want_lse, c10::ScalarType out_type = torch::kFloat32,
-                                        bool causal = false, const std::vector<int64_t>& head_windows = {}) {
+                                        bool causal = false, const std::vector<int64_t>& head_windows = {},
+                                        int64_t dilation = 1, const std::vector<int64_t>& cu_seqlens = {}) {
     check_input(Q, "Q");
     check_input(K, "K");
     check_input(V, "V");
@@ -60,13 +61,30 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
     const int dtype = Q.scalar_type() == torch::kBFloat16 ? LCA_DTYPE_BF16 : LCA_DTYPE_F16;
     std::vector<int32_t> norm(globals.size() + 1);
     int64_t G = 0;
-    raise_status(lca_normalize_global_tokens(globals.data(), (int64_t)globals.size(), seq_len, norm.data(), &G),
-                 "global_tokens");
+    if (cu_seqlens.empty())
+        raise_status(lca_normalize_global_tokens(globals.data(), (int64_t)globals.size(), seq_len, norm.data(), &G),
+                     "global_tokens");
     size_t ws_bytes = 0;
     int64_t wmax = window_size;
     for (int64_t hw : head_windows) wmax = std::max(wmax, hw);
-    raise_status(lca_swa_workspace_size(batch, heads, seq_len, head_dim, wmax, G, dtype, &ws_bytes),
-                 "workspace size");
+    TORCH_CHECK(dilation >= 1, "dilation must be >= 1");
+    TORCH_CHECK(cu_seqlens.empty() || (batch == 1 && dilation == 1),
+                "packed sequences take Q of shape [1, heads, total_len, head_dim] and no dilation");
+    const int out_dtype = out_type == torch::kFloat32 ? LCA_DTYPE_F32
+                          : (out_type == torch::kBFloat16 ? LCA_DTYPE_BF16 : LCA_DTYPE_F16);
+    if (!cu_seqlens.empty()) {
+        const int64_t nseq = (int64_t)cu_seqlens.size() - 1;
+        G = nseq * (int64_t)globals.size();  // an upper bound on the unique global rows
+        raise_status(lca_swa_workspace_size(1, heads, seq_len, head_dim, wmax, G, dtype, &ws_bytes),
+                     "workspace size");
+    } else if (dilation > 1) {
+        raise_status(lca_swa_dilated_workspace_size(batch, heads, seq_len, head_dim, wmax, dilation, G, dtype,
+                                                    out_dtype, &ws_bytes),
+                     "workspace size");
+    } else {
+        raise_status(lca_swa_workspace_size(batch, heads, seq_len, head_dim, wmax, G, dtype, &ws_bytes),
+                     "workspace size");
+    }
     torch::Tensor ws;
     void* ws_ptr = nullptr;
     if (ws_bytes > 0) {
@@ -74,14 +92,21 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
         ws_ptr = ws.data_ptr();
     }
     cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-    const int out_dtype = out_type == torch::kFloat32 ? LCA_DTYPE_F32
-                          : (out_type == torch::kBFloat16 ? LCA_DTYPE_BF16 : LCA_DTYPE_F16);
-    const int st = lca_swa_forward_ex(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), out_dtype,
-                                      want_lse ? L.data_ptr<float>() : nullptr, dtype, batch, heads, seq_len, head_dim,
-                                      window_size, head_windows.empty() ? nullptr : head_windows.data(),
-                                      static_cast<float>(scale), causal ? LCA_FLAG_CAUSAL : 0,
-                                      globals.data(), (int64_t)globals.size(), ws_ptr, ws_bytes,
-                                      static_cast<void*>(stream));
+    const int64_t* hw = head_windows.empty() ? nullptr : head_windows.data();
+    const int flags = causal ? LCA_FLAG_CAUSAL : 0;
+    float* lse_ptr = want_lse ? L.data_ptr<float>() : nullptr;
+    void* sp = static_cast<void*>(stream);
+    int st;
+    if (!cu_seqlens.empty())
+        st = lca_swa_forward_varlen(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), out_dtype, lse_ptr, dtype,
+                                    heads, seq_len, head_dim, window_size, hw, static_cast<float>(scale), flags,
+                                    cu_seqlens.data(), (int64_t)cu_seqlens.size() - 1, globals.data(),
+                                    (int64_t)globals.size(), ws_ptr, ws_bytes, sp);
+    else
+        st = lca_swa_forward_dilated(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), out_dtype, lse_ptr, dtype,
+                                     batch, heads, seq_len, head_dim, window_size, hw, dilation,
+                                     static_cast<float>(scale), flags, globals.data(), (int64_t)globals.size(), ws_ptr,
+                                     ws_bytes, sp);
     raise_status(st, "sliding_window_attention_forward");
     if (want_lse) return {O, L};
     return {O};
@@ -115,8 +140,10 @@ std::vector<torch::Tensor> sliding_window_attention_forward_lse(torch::Tensor Q,
 std::vector<torch::Tensor> sliding_window_attention_forward_ex(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
                                                                int64_t window_size, std::vector<int64_t> global_tokens,
                                                                double scale, c10::ScalarType out_dtype, bool causal,
-                                                               bool want_lse, std::vector<int64_t> head_windows) {
-    return forward_impl(Q, K, V, window_size, global_tokens, scale, want_lse, out_dtype, causal, head_windows);
+                                                               bool want_lse, std::vector<int64_t> head_windows,
+                                                               int64_t dilation, std::vector<int64_t> cu_seqlens) {
+    return forward_impl(Q, K, V, window_size, global_tokens, scale, want_lse, out_dtype, causal, head_windows,
+                        dilation, cu_seqlens);
 }
 
 int device_error() {
@@ -142,7 +169,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "returns [O] or [O, LSE]",
           py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("window_size"), py::arg("global_tokens"),
           py::arg("scale"), py::arg("out_dtype"), py::arg("causal"), py::arg("want_lse"),
-          py::arg("head_windows") = std::vector<int64_t>{});
+          py::arg("head_windows") = std::vector<int64_t>{}, py::arg("dilation") = 1,
+          py::arg("cu_seqlens") = std::vector<int64_t>{});
     m.def("device_error", &device_error, "Read and clear the device-side error word (synchronises)");
     m.attr("abi_version") = lca_abi_version();
 }

@@ -126,6 +126,9 @@ struct Problem {
     int out_dtype = LCA_DTYPE_F32;  // type of out (16-bit only through lca_swa_forward_ex)
     bool causal = false;            // LCA_FLAG_CAUSAL (whole-sequence problems only)
     std::vector<int> head_window;   // a radius per head (whole-sequence problems), else empty
+    int seg_mode = lca::kSegNone;   // band clipped to segments (lca::MainParams::seg_mode)
+    int64_t seg_len = 0;            // kSegEqual: tokens per segment
+    std::vector<int> seg_start;     // kSegVarlen: segment starts, then the total
     float scale = 1.f;
     std::vector<int32_t> gl;  // sorted unique global indices (absolute)
     int64_t halo() const { return sharded && world > 1 ? window : 0; }
@@ -623,6 +626,10 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     p.causal = P.causal ? 1 : 0;
     p.n_head_windows = (int)P.head_window.size();
     for (size_t h = 0; h < P.head_window.size(); ++h) p.head_window[h] = P.head_window[h];
+    p.seg_mode = P.seg_mode;
+    p.seg_len = (int)P.seg_len;
+    p.n_segs = P.seg_start.empty() ? 0 : (int)P.seg_start.size() - 1;
+    for (size_t i = 0; i < P.seg_start.size(); ++i) p.seg_start[i] = P.seg_start[i];
     if (P.G > 0) {
         p.g_tiles = L.g_tiles;
         p.n_splits = L.n_splits;
@@ -688,6 +695,40 @@ int enqueue_combine_splits(const Problem& P, const Layout& L, void* out, float* 
     }
     cudaError_t e = lca::launch_combine((int)P.d, cp, stream);
     if (e != cudaSuccess) return fail_cuda(e, "combine launch");
+    return LCA_OK;
+}
+
+int run_problem(const Problem& P, const void* q, const void* k, const void* v, void* out, float* lse, void* workspace,
+                size_t workspace_bytes, void* stream_ptr);
+
+int check_out_flags(int out_dtype, int flags) {
+    if (out_dtype != LCA_DTYPE_F32 && out_dtype != LCA_DTYPE_F16 && out_dtype != LCA_DTYPE_BF16)
+        return fail(LCA_ERR_UNSUPPORTED, "out_dtype %d is not supported (fp32, fp16 or bf16)", out_dtype);
+    if ((flags & ~LCA_FLAG_CAUSAL) != 0) return fail(LCA_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    return LCA_OK;
+}
+
+// One radius per head: the largest becomes *window_size (it sizes the workspace); the
+// per-head list is kept unless all radii are equal.
+int parse_head_windows(int64_t heads, int64_t seq_len, const int64_t* head_window_sizes, int64_t* window_size,
+                       std::vector<int>& out) {
+    out.clear();
+    if (head_window_sizes == nullptr) return LCA_OK;
+    if (heads > LCA_MAX_HEAD_WINDOWS)
+        return fail(LCA_ERR_UNSUPPORTED, "radii of their own for %lld heads (at most %d)", (long long)heads,
+                    LCA_MAX_HEAD_WINDOWS);
+    int64_t wmax = 0;
+    bool uniform = true;
+    for (int64_t h = 0; h < heads; ++h) {
+        if (head_window_sizes[h] < 0)
+            return fail(LCA_ERR_INVALID_ARGUMENT, "head_window_sizes[%lld] = %lld must be >= 0", (long long)h,
+                        (long long)head_window_sizes[h]);
+        wmax = std::max(wmax, head_window_sizes[h]);
+        uniform = uniform && head_window_sizes[h] == head_window_sizes[0];
+    }
+    *window_size = wmax;
+    if (!uniform)
+        for (int64_t h = 0; h < heads; ++h) out.push_back((int)std::min(head_window_sizes[h], seq_len));
     return LCA_OK;
 }
 
@@ -784,35 +825,192 @@ int lca_swa_forward_ex(const void* q, const void* k, const void* v, void* out, i
                        const int64_t* head_window_sizes, float scale, int flags, const int64_t* global_tokens,
                        int64_t num_global_tokens, void* workspace, size_t workspace_bytes, void* stream_ptr) {
     g_last_error.clear();
-    if (out_dtype != LCA_DTYPE_F32 && out_dtype != LCA_DTYPE_F16 && out_dtype != LCA_DTYPE_BF16)
-        return fail(LCA_ERR_UNSUPPORTED, "out_dtype %d is not supported (fp32, fp16 or bf16)", out_dtype);
-    if ((flags & ~LCA_FLAG_CAUSAL) != 0) return fail(LCA_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    int st = check_out_flags(out_dtype, flags);
+    if (st != LCA_OK) return st;
     std::vector<int> head_window;
-    if (head_window_sizes != nullptr) {
-        // one radius per head: the largest sizes the workspace, each head's own drives its units
-        if (heads > LCA_MAX_HEAD_WINDOWS)
-            return fail(LCA_ERR_UNSUPPORTED, "radii of their own for %lld heads (at most %d)", (long long)heads,
-                        LCA_MAX_HEAD_WINDOWS);
-        int64_t wmax = 0;
-        bool uniform = true;
-        for (int64_t h = 0; h < heads; ++h) {
-            if (head_window_sizes[h] < 0)
-                return fail(LCA_ERR_INVALID_ARGUMENT, "head_window_sizes[%lld] = %lld must be >= 0", (long long)h,
-                            (long long)head_window_sizes[h]);
-            wmax = std::max(wmax, head_window_sizes[h]);
-            uniform = uniform && head_window_sizes[h] == head_window_sizes[0];
-        }
-        window_size = wmax;
-        if (!uniform)
-            for (int64_t h = 0; h < heads; ++h) head_window.push_back((int)std::min(head_window_sizes[h], seq_len));
-    }
+    st = parse_head_windows(heads, seq_len, head_window_sizes, &window_size, head_window);
+    if (st != LCA_OK) return st;
     Problem P;
-    int st = parse_common(P, dtype, batch, heads, seq_len, head_dim, window_size, scale, global_tokens,
-                          num_global_tokens);
+    st = parse_common(P, dtype, batch, heads, seq_len, head_dim, window_size, scale, global_tokens,
+                      num_global_tokens);
     if (st != LCA_OK) return st;
     P.head_window = std::move(head_window);
     P.out_dtype = out_dtype;
     P.causal = (flags & LCA_FLAG_CAUSAL) != 0;
+    return run_problem(P, q, k, v, out, lse, workspace, workspace_bytes, stream_ptr);
+}
+
+// ------------------------------------------------------------------ packed sequences
+
+int lca_swa_forward_varlen(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
+                           int dtype, int64_t heads, int64_t total_len, int64_t head_dim, int64_t window_size,
+                           const int64_t* head_window_sizes, float scale, int flags, const int64_t* cu_seqlens,
+                           int64_t num_seqs, const int64_t* global_tokens, int64_t num_global_tokens,
+                           void* workspace, size_t workspace_bytes, void* stream_ptr) {
+    g_last_error.clear();
+    int st = check_out_flags(out_dtype, flags);
+    if (st != LCA_OK) return st;
+    if (cu_seqlens == nullptr || num_seqs < 1)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "cu_seqlens needs num_seqs + 1 >= 2 offsets");
+    if (num_seqs > LCA_MAX_SEQUENCES)
+        return fail(LCA_ERR_UNSUPPORTED, "%lld sequences in one call (at most %d)", (long long)num_seqs,
+                    LCA_MAX_SEQUENCES);
+    if (cu_seqlens[0] != 0 || cu_seqlens[num_seqs] != total_len)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "cu_seqlens must run from 0 to total_len (%lld)", (long long)total_len);
+    for (int64_t i = 0; i < num_seqs; ++i)
+        if (cu_seqlens[i + 1] < cu_seqlens[i])
+            return fail(LCA_ERR_INVALID_ARGUMENT, "cu_seqlens must not decrease (at %lld)", (long long)i);
+    if (num_global_tokens < 0 || (num_global_tokens > 0 && global_tokens == nullptr))
+        return fail(LCA_ERR_INVALID_ARGUMENT, "bad global token list");
+    std::vector<int> head_window;
+    if ((st = parse_head_windows(heads, total_len, head_window_sizes, &window_size, head_window)) != LCA_OK)
+        return st;
+    Problem P;
+    if ((st = parse_common(P, dtype, 1, heads, total_len, head_dim, window_size, scale, nullptr, 0)) != LCA_OK)
+        return st;
+    // the token list applies to every non-empty sequence, indexed within it the way the
+    // reference indexes one sequence (negative from its end; outside it is an error)
+    std::vector<int32_t> norm((size_t)num_global_tokens + 1);
+    for (int64_t sq = 0; sq < num_seqs; ++sq) {
+        const int64_t len = cu_seqlens[sq + 1] - cu_seqlens[sq];
+        if (len == 0 || num_global_tokens == 0) continue;
+        int64_t G = 0;
+        if ((st = lca_normalize_global_tokens(global_tokens, num_global_tokens, len, norm.data(), &G)) != LCA_OK) {
+            const std::string why = lca_last_error();
+            return fail(st, "sequence %lld (length %lld): %s", (long long)sq, (long long)len, why.c_str());
+        }
+        for (int64_t i = 0; i < G; ++i) P.gl.push_back((int32_t)(cu_seqlens[sq] + norm[(size_t)i]));
+    }
+    std::sort(P.gl.begin(), P.gl.end());
+    P.G = (int64_t)P.gl.size();
+    P.head_window = std::move(head_window);
+    P.out_dtype = out_dtype;
+    P.causal = (flags & LCA_FLAG_CAUSAL) != 0;
+    if (num_seqs > 1) {
+        P.seg_mode = lca::kSegVarlen;
+        for (int64_t i = 0; i <= num_seqs; ++i) P.seg_start.push_back((int)cu_seqlens[i]);
+    }
+    return run_problem(P, q, k, v, out, lse, workspace, workspace_bytes, stream_ptr);
+}
+
+// ------------------------------------------------------------------ dilated windows
+
+}  // extern "C"
+
+namespace {
+
+// Bytes of the residue-order copies a dilated forward keeps ahead of the problem's own
+// workspace: Q, K, V, O and LSE, each region 1024-byte aligned.
+size_t dilated_prefix_bytes(int64_t bh, int64_t n, int64_t d, int out_dtype) {
+    const size_t plane = (size_t)bh * n * d;
+    const size_t osize = out_dtype == LCA_DTYPE_F32 ? 4 : 2;
+    return 3 * align_up(plane * 2, kAlign) + align_up(plane * osize, kAlign) + align_up((size_t)bh * n * 4, kAlign);
+}
+
+int permute(const void* src, void* dst, int64_t planes, int64_t n, int64_t dil, int64_t row_bytes, bool to_residue,
+            cudaStream_t stream) {
+    lca::PermuteParams pp;
+    pp.src = static_cast<const uint8_t*>(src);
+    pp.dst = static_cast<uint8_t*>(dst);
+    pp.planes = planes;
+    pp.n = (int)n;
+    pp.dil = (int)dil;
+    pp.row_bytes = (int)row_bytes;
+    pp.to_residue = to_residue ? 1 : 0;
+    cudaError_t e = lca::launch_permute_rows(pp, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "residue-order copy launch");
+    return LCA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lca_swa_dilated_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                                   int64_t window_size, int64_t dilation, int64_t num_unique_global, int dtype,
+                                   int out_dtype, size_t* out_bytes) {
+    if (out_bytes == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "out_bytes is NULL");
+    if (dilation < 1) return fail(LCA_ERR_INVALID_ARGUMENT, "dilation must be >= 1");
+    int st = check_out_flags(out_dtype, 0);
+    if (st != LCA_OK) return st;
+    size_t inner = 0;
+    if ((st = lca::workspace_bytes(batch, heads, seq_len, head_dim, window_size, num_unique_global, dtype, true,
+                                   &inner)) != LCA_OK)
+        return st;
+    *out_bytes = dilation == 1 ? inner : dilated_prefix_bytes(batch * heads, seq_len, head_dim, out_dtype) + inner;
+    return LCA_OK;
+}
+
+int lca_swa_forward_dilated(const void* q, const void* k, const void* v, void* out, int out_dtype, float* lse,
+                            int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                            int64_t window_size, const int64_t* head_window_sizes, int64_t dilation, float scale,
+                            int flags, const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
+                            size_t workspace_bytes, void* stream_ptr) {
+    g_last_error.clear();
+    if (dilation < 1) return fail(LCA_ERR_INVALID_ARGUMENT, "dilation must be >= 1 (got %lld)", (long long)dilation);
+    if (dilation == 1)
+        return lca_swa_forward_ex(q, k, v, out, out_dtype, lse, dtype, batch, heads, seq_len, head_dim, window_size,
+                                  head_window_sizes, scale, flags, global_tokens, num_global_tokens, workspace,
+                                  workspace_bytes, stream_ptr);
+    int st = check_out_flags(out_dtype, flags);
+    if (st != LCA_OK) return st;
+    if (flags & LCA_FLAG_CAUSAL)
+        return fail(LCA_ERR_UNSUPPORTED, "the causal variant has no dilated form in this build");
+    if (seq_len % dilation != 0)
+        return fail(LCA_ERR_UNSUPPORTED, "seq_len %lld is not a multiple of the dilation %lld", (long long)seq_len,
+                    (long long)dilation);
+    std::vector<int> head_window;
+    if ((st = parse_head_windows(heads, seq_len, head_window_sizes, &window_size, head_window)) != LCA_OK) return st;
+    Problem P;
+    if ((st = parse_common(P, dtype, batch, heads, seq_len, head_dim, window_size, scale, global_tokens,
+                           num_global_tokens)) != LCA_OK)
+        return st;
+    if (P.bh == 0 || P.n == 0) return LCA_OK;
+    if ((st = check_io(q, k, v, out, lse)) != LCA_OK) return st;
+    // The band of row i = r + dilation * t (residue r) is the keys r + dilation * t' with
+    // |t - t'| <= w: in residue order (row r * m + t, m = n / dilation) that is an ordinary
+    // band of radius w inside segment r of m tokens.  Global tokens move to their residue-order
+    // positions and keep seeing, and being seen by, every row.
+    const int64_t m = seq_len / dilation;
+    for (auto& g : P.gl) g = (int32_t)((g % dilation) * m + g / dilation);
+    std::sort(P.gl.begin(), P.gl.end());
+    P.head_window = std::move(head_window);
+    P.out_dtype = out_dtype;
+    P.seg_mode = lca::kSegEqual;
+    P.seg_len = m;
+    const size_t prefix = dilated_prefix_bytes(P.bh, P.n, P.d, out_dtype);
+    if (workspace == nullptr || workspace_bytes < prefix || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+        return fail(LCA_ERR_WORKSPACE, "a dilated forward needs lca_swa_dilated_workspace_size bytes, 256-byte aligned");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const size_t plane = (size_t)P.bh * P.n * P.d;
+    const size_t osize = out_dtype == LCA_DTYPE_F32 ? 4 : 2;
+    uint8_t* rq = ws;
+    uint8_t* rk = rq + align_up(plane * 2, kAlign);
+    uint8_t* rv = rk + align_up(plane * 2, kAlign);
+    uint8_t* ro = rv + align_up(plane * 2, kAlign);
+    float* rl = reinterpret_cast<float*>(ro + align_up(plane * osize, kAlign));
+    const int64_t row = P.d * 2;
+    if ((st = permute(q, rq, P.bh, P.n, dilation, row, true, stream)) != LCA_OK) return st;
+    if ((st = permute(k, rk, P.bh, P.n, dilation, row, true, stream)) != LCA_OK) return st;
+    if ((st = permute(v, rv, P.bh, P.n, dilation, row, true, stream)) != LCA_OK) return st;
+    if ((st = run_problem(P, rq, rk, rv, ro, lse != nullptr ? rl : nullptr, ws + prefix, workspace_bytes - prefix,
+                          stream_ptr)) != LCA_OK)
+        return st;
+    if ((st = permute(ro, out, P.bh, P.n, dilation, P.d * (int64_t)osize, false, stream)) != LCA_OK) return st;
+    if (lse != nullptr && (st = permute(rl, lse, P.bh, P.n, dilation, 4, false, stream)) != LCA_OK) return st;
+    return LCA_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Checks the buffers and enqueues one whole-sequence problem: gather of the global rows,
+// (fp16 copy of V), the main kernel, merge of the global-row splits.
+int run_problem(const Problem& P, const void* q, const void* k, const void* v, void* out, float* lse, void* workspace,
+                size_t workspace_bytes, void* stream_ptr) {
+    int st;
     if (P.bh == 0 || P.n == 0) return LCA_OK;  // nothing to compute
     if ((st = check_io(q, k, v, out, lse)) != LCA_OK) return st;
     int dev = 0;
@@ -833,6 +1031,10 @@ int lca_swa_forward_ex(const void* q, const void* k, const void* v, void* out, i
     if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16, fast)) != LCA_OK) return st;
     return enqueue_combine_splits(P, L, out, lse, ws, stream);
 }
+
+}  // namespace
+
+extern "C" {
 
 // ------------------------------------------------------------------ sequence shards
 

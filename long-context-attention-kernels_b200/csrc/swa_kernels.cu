@@ -213,7 +213,11 @@ struct Tile {
 
 // Units [0, n_grow_units) are global-row units and the rest band units when grow_first,
 // else band units come first: the longer kind goes first, so the short ones fill the tail.
+// EXT: the extended masks (causal, radius per head, segments) are compiled in; the plain
+// build leaves them out, so the common case carries none of their state.
+template <bool EXT>
 __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
+    const int n_hw = EXT ? p.n_head_windows : 0;
     Unit un;
     const bool grow = p.grow_first ? (u < p.n_grow_units) : (u >= p.n_band_units);
     const int t = grow ? (p.grow_first ? u : u - p.n_band_units) : (p.grow_first ? u - p.n_grow_units : u);
@@ -242,11 +246,11 @@ __device__ __forceinline__ Unit decode_unit(const MainParams& p, int u) {
         un.active[0] = true;
         un.active[1] = q0 + BM < p.n;
         // the head's own radius, which is also its lead, when heads have radii of their own
-        un.w = p.n_head_windows > 0 ? p.head_window[un.bh % p.n_head_windows] : p.window;
-        const int lead = p.n_head_windows > 0 ? un.w : p.lead;
+        un.w = n_hw > 0 ? p.head_window[un.bh % n_hw] : p.window;
+        const int lead = n_hw > 0 ? un.w : p.lead;
         un.kstart = p.q_off + q0 - lead;
         // causal: A's rows [q0, q0 + 127] need keys up to q0 + 127 only
-        un.nA = p.causal ? (lead + BM - 1) / BN + 1 : (lead + un.w + BM + BN - 1) / BN;
+        un.nA = (EXT && p.causal) ? (lead + BM - 1) / BN + 1 : (lead + un.w + BM + BN - 1) / BN;
         const int p_first = un.kstart < p.key_lo ? (p.key_lo - un.kstart) / BN : 0;
         int p_last = un.active[1] ? un.nA : un.nA - 1;
         const int p_overlap_last = (p.key_hi - 1 - un.kstart) / BN;
@@ -286,6 +290,33 @@ __device__ __forceinline__ Tile tile_of(const MainParams& p, const Unit& un, int
     return t;
 }
 
+// First index of the sorted list gl[0, count) whose value is >= key (count if none).
+__device__ __forceinline__ int lower_index(const int* gl, int count, int key) {
+    int a = 0, b = count;
+    while (a < b) {
+        const int mid = (a + b) >> 1;
+        if (gl[mid] < key) a = mid + 1; else b = mid;
+    }
+    return a;
+}
+
+// The segment [s_lo, s_hi) holding absolute token `x`: equal segments of seg_len tokens, or
+// the packed sequences of seg_start.
+__device__ __forceinline__ void segment_of(const MainParams& p, int x, int& s_lo, int& s_hi) {
+    if (p.seg_mode == kSegEqual) {
+        s_lo = (x / p.seg_len) * p.seg_len;
+        s_hi = s_lo + p.seg_len;
+        return;
+    }
+    int a = 0, b = p.n_segs;  // last segment whose start is <= x
+    while (b - a > 1) {
+        const int mid = (a + b) >> 1;
+        if (p.seg_start[mid] <= x) a = mid; else b = mid;
+    }
+    s_lo = p.seg_start[a];
+    s_hi = p.seg_start[a + 1];
+}
+
 // All 32 lanes wait; the warp proceeds only if every lane saw the phase complete, so
 // warp-collective tcgen05 instructions that follow are never reached divergently.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
@@ -308,7 +339,7 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk16) {
 
 // The main kernel's body: tensor maps by reference to the kernel's __grid_constant__
 // parameters (TMA reads them where they lie).
-template <int D, bool BF16, bool V16>
+template <int D, bool BF16, bool V16, bool EXT>
 __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                               const CUtensorMap& tm_kh, const CUtensorMap& tm_vh,
                                               const CUtensorMap& tm_qg, const CUtensorMap& tm_kg,
@@ -334,6 +365,8 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
     volatile int* abort_flag = &ctl->abort_flag;
     const int n_units = p.n_grow_units + p.n_band_units;
     const uint64_t tmo = p.timeout_ns;
+    const bool causal = EXT && p.causal;
+    const int seg_mode = EXT ? p.seg_mode : kSegNone;
 
     if (threadIdx.x == 0) {
         for (int x = 0; x < 2; ++x) {
@@ -404,7 +437,7 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                     ctl->unit_ring[us] = u;
                     ptx::mbar_arrive(&ctl->unit_full[us]);
                     if (u >= n_units) break;
-                    const Unit un = decode_unit(p, u);
+                    const Unit un = decode_unit<EXT>(p, u);
                     const CUtensorMap* mq = un.grow ? &tm_qg : &tm_q;
                     for (int x = 0; x < 2 && ok; ++x) {
                         // the compact global rows are [G][3][bh][d]: their maps index (col, bh, row)
@@ -548,7 +581,7 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                     const int u = *reinterpret_cast<volatile int*>(&ctl->unit_ring[us]);
                     ptx::mbar_arrive(&ctl->unit_empty[us]);
                     if (u >= n_units) break;
-                    const Unit un = decode_unit(p, u);
+                    const Unit un = decode_unit<EXT>(p, u);
                     const bool act = X ? un.active[1] : un.active[0];
                     if (!W(&ctl->q_full[X], qn)) break;
                     ++qn;
@@ -687,7 +720,7 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&ctl->unit_empty[us]);
             if (u >= n_units) break;
-            const Unit un = decode_unit(p, u);
+            const Unit un = decode_unit<EXT>(p, u);
             LCA_TRACE_LANE0(trace::EV_UNIT_DECODED);
             const bool active_x = X ? un.active[1] : un.active[0];
             if (!active_x) continue;
@@ -698,42 +731,50 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
             const bool warp_live = __any_sync(0xffffffffu, live);
             // row's visible keys in band / split tiles: [jlo, jhi] (absolute key index)
             int jlo = p.gk_lo, jhi = p.gk_lo + p.gk_n - 1;
-            // run [g_lo, g_hi) of sorted global indices inside the row's band (band units)
-            int g_lo = 0, g_hi = 0;
+            // band units: run [g_lo, g_hi) of sorted global indices inside the row's band, and
+            // the compact columns [gv_lo, gv_hi) of the global keys the row may see at all
+            int g_lo = 0, g_hi = 0, gv_lo = 0, gv_hi = p.num_global;
+            const int* gl = gidx_in_smem ? sGidx : p.gidx;
             if (un.grow) {
-                // causal: a global row sees the keys up to its own token
-                if (p.causal && qi < p.num_global) {
-                    const int g_tok = (gidx_in_smem ? sGidx : p.gidx)[qi];
-                    if (g_tok < jhi) jhi = g_tok;
+                if (qi < p.num_global && (causal || seg_mode == kSegVarlen)) {
+                    const int g_tok = gl[qi];
+                    if (causal && g_tok < jhi) jhi = g_tok;  // causal: keys up to the row's own token
+                    if (seg_mode == kSegVarlen) {           // packed sequences: keys of its own sequence
+                        int s_lo, s_hi;
+                        segment_of(p, g_tok, s_lo, s_hi);
+                        if (s_lo > jlo) jlo = s_lo;
+                        if (s_hi - 1 < jhi) jhi = s_hi - 1;
+                    }
                 }
             } else {
                 const int w = un.w;
                 jlo = qa - w > 0 ? qa - w : 0;
                 jhi = (qa + w < p.n_total - 1) ? qa + w : p.n_total - 1;
-                if (p.causal && qa < jhi) jhi = qa;  // causal band [i - w, i]
+                int s_lo = 0, s_hi = p.n_total;
+                if (seg_mode != kSegNone) {  // the band stops at the row's segment
+                    segment_of(p, qa, s_lo, s_hi);
+                    if (s_lo > jlo) jlo = s_lo;
+                    if (s_hi - 1 < jhi) jhi = s_hi - 1;
+                }
+                if (causal && qa < jhi) jhi = qa;  // causal band [i - w, i]
                 if (p.g_tiles > 0) {
                     // first global at or after the band's start, then the run inside the band
                     // (a few entries at most unless globals are dense: then a second search)
-                    const int* gl = gidx_in_smem ? sGidx : p.gidx;
-                    int a = 0, b = p.num_global;
-                    while (a < b) {
-                        const int mid = (a + b) >> 1;
-                        if (gl[mid] < qa - w) a = mid + 1; else b = mid;
-                    }
-                    g_lo = a;
-                    int scan = 0;
-                    while (a < p.num_global && scan < 4 && gl[a] <= qa + w) {
+                    g_lo = lower_index(gl, p.num_global, jlo);
+                    int a = g_lo, scan = 0;
+                    while (a < p.num_global && scan < 4 && gl[a] <= jhi) {
                         ++a;
                         ++scan;
                     }
-                    if (scan == 4) {
-                        b = p.num_global;
-                        while (a < b) {
-                            const int mid = (a + b) >> 1;
-                            if (gl[mid] <= qa + w) a = mid + 1; else b = mid;
-                        }
+                    g_hi = scan == 4 ? lower_index(gl, p.num_global, jhi + 1) : a;
+                    if (seg_mode == kSegVarlen) {  // packed sequences: the globals of the row's own
+                        gv_lo = lower_index(gl, p.num_global, s_lo);
+                        gv_hi = lower_index(gl, p.num_global, s_hi);
                     }
-                    g_hi = a;
+                    if (causal) {  // only the globals before the band: the rest are in it or after i
+                        gv_hi = g_lo;
+                        g_hi = g_lo;
+                    }
                 }
             }
             LCA_TRACE_LANE0(trace::EV_UNIT_READY);
@@ -757,14 +798,10 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                         // visible columns of this row in this tile: [lo, hi] minus the hole [h_lo, h_hi)
                         int lo, hi, h_lo = 0, h_hi = 0;
                         if (t.global_key) {
-                            lo = 0;
-                            hi = p.num_global - 1 - col0;
+                            lo = gv_lo - col0;
+                            hi = gv_hi - 1 - col0;
                             h_lo = g_lo - col0;
                             h_hi = g_hi - col0;
-                            if (p.causal) {  // only the globals before the band: the rest are in it or after i
-                                hi = g_lo - 1 - col0;
-                                h_lo = h_hi = 0;
-                            }
                         } else {
                             lo = jlo - col0;
                             hi = jhi - col0;
@@ -1068,23 +1105,23 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
 #define LCA_MAIN_ARGS tm_q, tm_k, tm_v, tm_kh, tm_vh, tm_qg, tm_kg, tm_vg, tm_o, tm_po, tm_v16, tm_vg16, tm_vh16, p
 
 // fp16 inputs (fp16 P), or bf16 inputs without the fp16 copy of V (bf16 P split into hi + lo)
-template <int D, bool BF16>
+template <int D, bool BF16, bool EXT>
 __global__ void __launch_bounds__(Cfg<D, BF16, false>::kThreads, 1) lca_swa_main(LCA_MAIN_PARAMS) {
-    swa_main_body<D, BF16, false>(LCA_MAIN_ARGS);
+    swa_main_body<D, BF16, false, EXT>(LCA_MAIN_ARGS);
 }
 
 // bf16 inputs with the fp16 copy of V: one launch that reads the word lca_convert_v16 set and
 // runs fp16 P with one P*V per tile from the copy when every value of V fitted fp16, else the
 // split bf16 P (no host synchronisation, so the choice stays capturable in a graph)
-template <int D>
+template <int D, bool EXT>
 __global__ void __launch_bounds__(Cfg<D, true, true>::kThreads, 1) lca_swa_main_v16(LCA_MAIN_PARAMS) {
     static_assert(Cfg<D, true, true>::kSmemBytes == Cfg<D, true, false>::kSmemBytes &&
                       Cfg<D, true, true>::kThreads == Cfg<D, true, false>::kThreads,
                   "both paths share one launch configuration");
     if (*reinterpret_cast<const volatile int*>(p.v16_bad) == 0)
-        swa_main_body<D, true, true>(LCA_MAIN_ARGS);
+        swa_main_body<D, true, true, EXT>(LCA_MAIN_ARGS);
     else
-        swa_main_body<D, true, false>(LCA_MAIN_ARGS);
+        swa_main_body<D, true, false, EXT>(LCA_MAIN_ARGS);
 }
 
 // ------------------------------------------------------------------------ gather
@@ -1184,6 +1221,33 @@ __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
         float m = 0.f;
         for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, s_max[i]);
         if (blk_bad || (blk_inexact && m < 0.0625f)) *cp.any_bad = 1;
+    }
+}
+
+// ------------------------------------------------------------------------ residue order
+
+// Rows of [planes][n][row_bytes] between the sequence order and the residue order of `dil`
+// (m = n / dil): residue-order row r * m + t is sequence row r + dil * t.  One thread per
+// 16-byte chunk (4-byte word for rows of 4 bytes).
+__global__ void __launch_bounds__(256) lca_permute_rows(PermuteParams pp) {
+    const int unit = (pp.row_bytes % 16 == 0) ? 16 : 4;
+    const long long per_row = pp.row_bytes / unit;
+    const long long total = pp.planes * pp.n * per_row;
+    const int m = pp.n / pp.dil;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long c = i % per_row;
+        const long long rest = i / per_row;
+        const int row = (int)(rest % pp.n);
+        const long long plane = rest / pp.n;
+        // the output row `row` reads input row `from`
+        const int from = pp.to_residue ? (row / m) + pp.dil * (row % m) : (row % pp.dil) * m + row / pp.dil;
+        const uint8_t* src = pp.src + (plane * pp.n + from) * pp.row_bytes + c * unit;
+        uint8_t* dst = pp.dst + (plane * pp.n + row) * pp.row_bytes + c * unit;
+        if (unit == 16)
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        else
+            *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
     }
 }
 
@@ -1361,9 +1425,9 @@ __global__ void __launch_bounds__(256) lca_peer_put(PeerPutParams pp) {
 
 // ------------------------------------------------------------------------ launchers
 
-template <int D, bool BF16, bool V16 = false>
+template <int D, bool BF16, bool V16, bool EXT>
 static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int grid, cudaStream_t stream) {
-    auto kern = V16 ? lca_swa_main_v16<D> : lca_swa_main<D, BF16>;
+    auto kern = V16 ? lca_swa_main_v16<D, EXT> : lca_swa_main<D, BF16, EXT>;
     const int smem = Cfg<D, BF16, V16>::kSmemBytes;
     // the shared-memory attribute is set once per device (it persists in the context)
     constexpr int kDevices = 64;
@@ -1381,14 +1445,25 @@ static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int 
     return cudaGetLastError();
 }
 
+template <bool EXT>
+static cudaError_t launch_main_v(int head_dim, bool bf16, const TensorMaps& tm, const MainParams& p, int grid,
+                                 cudaStream_t stream, bool v16) {
+    if (bf16 && v16)  // one launch; it picks fp16 P or the split on the device (p.v16_bad)
+        return head_dim == 64 ? launch_main_t<64, true, true, EXT>(tm, p, grid, stream)
+                              : launch_main_t<128, true, true, EXT>(tm, p, grid, stream);
+    if (head_dim == 64)
+        return bf16 ? launch_main_t<64, true, false, EXT>(tm, p, grid, stream)
+                    : launch_main_t<64, false, false, EXT>(tm, p, grid, stream);
+    return bf16 ? launch_main_t<128, true, false, EXT>(tm, p, grid, stream)
+                : launch_main_t<128, false, false, EXT>(tm, p, grid, stream);
+}
+
 cudaError_t launch_main(int head_dim, bool bf16, const TensorMaps& tm, const MainParams& p, int grid,
                         cudaStream_t stream, bool v16) {
     if (head_dim != 64 && head_dim != 128) return cudaErrorInvalidValue;
-    if (bf16 && v16)  // one launch; it picks fp16 P or the split on the device (p.v16_bad)
-        return head_dim == 64 ? launch_main_t<64, true, true>(tm, p, grid, stream)
-                              : launch_main_t<128, true, true>(tm, p, grid, stream);
-    if (head_dim == 64) return bf16 ? launch_main_t<64, true>(tm, p, grid, stream) : launch_main_t<64, false>(tm, p, grid, stream);
-    return bf16 ? launch_main_t<128, true>(tm, p, grid, stream) : launch_main_t<128, false>(tm, p, grid, stream);
+    // the extended masks only when a call uses them
+    if (p.causal || p.seg_mode != kSegNone || p.n_head_windows > 0) return launch_main_v<true>(head_dim, bf16, tm, p, grid, stream, v16);
+    return launch_main_v<false>(head_dim, bf16, tm, p, grid, stream, v16);
 }
 
 cudaError_t launch_gather(int head_dim, const void* q, const void* k, const void* v, const GatherParams& gp,
@@ -1441,6 +1516,15 @@ cudaError_t launch_halo_pack(const HaloPackParams& hp, cudaStream_t stream) {
     if (chunks <= 0) return cudaSuccess;
     const long long blocks = std::min<long long>((chunks + 255) / 256, 148ll * 16);
     lca_pack_halo<<<(unsigned)blocks, 256, 0, stream>>>(hp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_permute_rows(const PermuteParams& pp, cudaStream_t stream) {
+    if (pp.row_bytes % 4 != 0 || pp.dil < 1 || pp.n % pp.dil != 0) return cudaErrorInvalidValue;
+    const long long units = pp.planes * pp.n * (pp.row_bytes % 16 == 0 ? pp.row_bytes / 16 : pp.row_bytes / 4);
+    if (units <= 0) return cudaSuccess;
+    const long long blocks = std::min<long long>((units + 255) / 256, 148ll * 16);
+    lca_permute_rows<<<(unsigned)blocks, 256, 0, stream>>>(pp);
     return cudaGetLastError();
 }
 

@@ -29,6 +29,7 @@ struct PeerSignals {
 };
 constexpr int kGatherChunk = 1024;    // global indices passed per gather launch
 constexpr int kMaxHeadWindows = 256;  // heads with a radius of their own (kernel parameter space)
+constexpr int kMaxSegments = 512;     // packed sequences of one varlen call (kernel parameter space)
 
 struct TensorMaps {
     CUtensorMap q, k, v;     // inputs [bh][n][d] (bf16 / f16), box 64 x 128 rows, 128B swizzle
@@ -88,7 +89,19 @@ struct MainParams {
     // n_head_windows = 0 means one radius for all.
     int n_head_windows;  // = heads, or 0
     int head_window[kMaxHeadWindows];
+    // Segments (whole-sequence problems): the band of a row stops at the row's segment.
+    // kSegEqual: segments of seg_len tokens, every global key visible to every row and every
+    // global row over all keys (the dilated window, run on a residue-permuted sequence).
+    // kSegVarlen: n_segs packed sequences [seg_start[s], seg_start[s + 1]); global keys and
+    // global rows stay inside their own sequence.
+    int seg_mode;
+    int seg_len;
+    int n_segs;
+    int seg_start[kMaxSegments + 1];
 };
+constexpr int kSegNone = 0;
+constexpr int kSegEqual = 1;
+constexpr int kSegVarlen = 2;
 constexpr int kOut16F16 = 1;
 constexpr int kOut16BF16 = 2;
 
@@ -185,6 +198,17 @@ struct PeerPutParams {
     int* err;
     unsigned long long timeout_ns;
 };
+
+// Rows of [planes][n][row_bytes] (row_bytes a multiple of 4, n a multiple of dil) moved
+// into the residue order of `dil` (to_residue) or back: residue-order row r * (n / dil) + t
+// is sequence row r + dil * t.
+struct PermuteParams {
+    const uint8_t* src;
+    uint8_t* dst;
+    long long planes;
+    int n, dil, row_bytes, to_residue;
+};
+cudaError_t launch_permute_rows(const PermuteParams& pp, cudaStream_t stream);
 
 cudaError_t launch_peer_put(const PeerPutParams& pp, int blocks, cudaStream_t stream);
 

@@ -20,7 +20,7 @@ import torch
 
 from ._native import extension, native_error
 
-__all__ = ["sliding_window_attention", "sliding_window_attention_with_lse"]
+__all__ = ["sliding_window_attention", "sliding_window_attention_with_lse", "sliding_window_attention_varlen"]
 
 
 def _reference_sliding_window_attention(
@@ -51,16 +51,22 @@ def _reference_sliding_window_attention(
     return torch.einsum("bhqk,bhkd->bhqd", torch.softmax(scores, dim=-1), V.float())
 
 
-def _dense_causal_attention(Q, K, V, window_size, global_tokens, scale):
+def _dense_causal_attention(Q, K, V, window_size, global_tokens, scale, dilation: int = 1, causal: bool = True):
     """The dense definition above intersected with j <= i (``causal=True`` together with
-    ``force_reference=True``): the reference's mask, then its upper triangle removed."""
+    ``force_reference=True``): the reference's mask, then its upper triangle removed; with
+    ``dilation`` > 1 the band keeps the keys i + dilation * t, |t| <= window_size."""
     seq_len = Q.shape[2]
     idx = torch.arange(seq_len, device=Q.device)
-    band = (idx[:, None] - idx[None, :]).abs() <= window_size
+    diff = idx[:, None] - idx[None, :]
+    band = diff.abs() <= window_size * dilation
+    if dilation > 1:
+        band &= diff % dilation == 0
     is_global = torch.zeros(seq_len, dtype=torch.bool, device=Q.device)
     if len(global_tokens) > 0:
         is_global[list(global_tokens)] = True
-    visible = (band | is_global[None, :] | is_global[:, None]) & (idx[None, :] <= idx[:, None])
+    visible = band | is_global[None, :] | is_global[:, None]
+    if causal:
+        visible &= idx[None, :] <= idx[:, None]
     scores = torch.einsum("bhqd,bhkd->bhqk", Q.float(), K.float()) * scale
     scores = scores.masked_fill(~visible[None, None, :, :], float("-inf"))
     return torch.einsum("bhqk,bhkd->bhqd", torch.softmax(scores, dim=-1), V.float())
@@ -79,10 +85,14 @@ def _head_windows(window_size, heads: int):
     return int(window_size), []
 
 
-def _dense(Q, K, V, window_size, global_tokens, scale, causal: bool):
-    """The dense definitions for ``force_reference=True``: the reference's (or its causal
-    restriction), head by head when the heads have radii of their own."""
-    dense = _dense_causal_attention if causal else _reference_sliding_window_attention
+def _dense(Q, K, V, window_size, global_tokens, scale, causal: bool, dilation: int = 1):
+    """The dense definitions for ``force_reference=True``: the reference's (or its causal or
+    dilated form), head by head when the heads have radii of their own."""
+    if causal or dilation > 1:
+        def dense(q, k, v, w, g, sc):
+            return _dense_causal_attention(q, k, v, w, g, sc, dilation=dilation, causal=causal)
+    else:
+        dense = _reference_sliding_window_attention
     _, radii = _head_windows(window_size, Q.shape[1])
     if not radii:
         return dense(Q, K, V, int(window_size), global_tokens, scale)
@@ -113,6 +123,7 @@ def sliding_window_attention(
     force_reference: bool = False,
     out_dtype: torch.dtype | None = None,
     causal: bool = False,
+    dilation: int = 1,
 ) -> torch.Tensor:
     """Longformer-style sparse attention forward.
 
@@ -127,18 +138,20 @@ def sliding_window_attention(
     rounded to that type by the kernel, with half the output bytes.  ``causal=True`` (also
     an addition) keeps only keys j <= i: the band becomes [i - window_size, i], a global
     key is seen by the rows at or after it, a global row sees the keys up to itself.
+    ``dilation`` > 1 (also an addition) keeps, of the band, the keys i + dilation * t with
+    |t| <= window_size (seq_len must be a multiple of the dilation; not with causal).
     """
     if force_reference:
         if scale is None:
             scale = 1.0 / math.sqrt(Q.shape[-1])
-        out = _dense(Q, K, V, window_size, global_tokens, scale, causal)
+        out = _dense(Q, K, V, window_size, global_tokens, scale, causal, int(dilation))
         return out if out_dtype in (None, torch.float32) else out.to(out_dtype)
     scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32) and not causal and not radii:
+    if out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1:
         return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
     return extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
                                                            out_dtype or torch.float32, bool(causal), False,
-                                                           radii)[0]
+                                                           radii, int(dilation))[0]
 
 
 def sliding_window_attention_with_lse(
@@ -150,6 +163,7 @@ def sliding_window_attention_with_lse(
     scale: float | None = None,
     out_dtype: torch.dtype | None = None,
     causal: bool = False,
+    dilation: int = 1,
 ):
     """As :func:`sliding_window_attention`, also returning the per-row log-sum-exp.
 
@@ -158,13 +172,41 @@ def sliding_window_attention_with_lse(
     or a cross-shard merge needs).  No counterpart in the reference.
     """
     scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32) and not causal and not radii:
+    if out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1:
         out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
     else:
         out, lse = extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
                                                                    out_dtype or torch.float32, bool(causal), True,
-                                                                   radii)
+                                                                   radii, int(dilation))
     return out, lse
+
+
+def sliding_window_attention_varlen(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    cu_seqlens: Sequence[int],
+    window_size,
+    global_tokens: Sequence[int] = (),
+    scale: float | None = None,
+    out_dtype: torch.dtype | None = None,
+    causal: bool = False,
+    return_lse: bool = False,
+):
+    """Packed variable-length sequences (no counterpart in the reference).
+
+    Q, K, V: [1, heads, total_len, head_dim] with sequence s in rows
+    ``[cu_seqlens[s], cu_seqlens[s + 1])`` (host offsets from 0 to total_len, at most 512
+    sequences).  Each sequence is attended on its own: its band, global keys and global
+    rows stay inside it, and ``global_tokens`` is indexed within each sequence as the
+    reference indexes one sequence.  Returns O (and LSE with ``return_lse``).
+    """
+    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
+    cu = [int(x) for x in (cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else cu_seqlens)]
+    res = extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
+                                                          out_dtype or torch.float32, bool(causal), bool(return_lse),
+                                                          radii, 1, cu)
+    return (res[0], res[1]) if return_lse else res[0]
 
 
 # Values of the device-side error word (include/lca.h, LCA_DEVERR_*).

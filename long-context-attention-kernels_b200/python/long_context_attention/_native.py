@@ -98,6 +98,17 @@ class CABI:
         lib.lca_swa_forward_ex.argtypes = [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, i64, i64, i64,
                                            ctypes.POINTER(i64), ctypes.c_float, ctypes.c_int, ctypes.POINTER(i64), i64,
                                            vp, sz, vp]
+        lib.lca_swa_forward_varlen.restype = ctypes.c_int
+        lib.lca_swa_forward_varlen.argtypes = [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, i64, i64,
+                                               ctypes.POINTER(i64), ctypes.c_float, ctypes.c_int, ctypes.POINTER(i64),
+                                               i64, ctypes.POINTER(i64), i64, vp, sz, vp]
+        lib.lca_swa_dilated_workspace_size.restype = ctypes.c_int
+        lib.lca_swa_dilated_workspace_size.argtypes = [i64, i64, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int,
+                                                       ctypes.POINTER(sz)]
+        lib.lca_swa_forward_dilated.restype = ctypes.c_int
+        lib.lca_swa_forward_dilated.argtypes = [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, i64, i64,
+                                                i64, ctypes.POINTER(i64), i64, ctypes.c_float, ctypes.c_int,
+                                                ctypes.POINTER(i64), i64, vp, sz, vp]
         lib.lca_swa_forward_noalloc.restype = ctypes.c_int
         lib.lca_swa_forward_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64,
                                                 ctypes.c_float, ctypes.POINTER(i64), i64, vp]

@@ -46,12 +46,16 @@ def normalize_global_tokens(global_tokens: Sequence[int], seq_len: int) -> np.nd
 
 
 def visible_rows(rows: np.ndarray, seq_len: int, window_size: int, global_idx: np.ndarray,
-                 causal: bool = False) -> np.ndarray:
+                 causal: bool = False, dilation: int = 1) -> np.ndarray:
     """Boolean [len(rows), seq_len] mask rows (python/long_context_attention/__init__.py:39-47),
-    intersected with j <= i when `causal`."""
+    intersected with j <= i when `causal`; with `dilation` > 1 the band keeps the keys
+    i + dilation * t, |t| <= window_size."""
     rows = np.asarray(rows, dtype=np.int64)
     keys = np.arange(seq_len, dtype=np.int64)
-    mask = np.abs(rows[:, None] - keys[None, :]) <= window_size
+    diff = rows[:, None] - keys[None, :]
+    mask = np.abs(diff) <= window_size * dilation
+    if dilation > 1:
+        mask &= diff % dilation == 0
     is_global = np.zeros(seq_len, dtype=bool)
     if global_idx.size:
         is_global[global_idx] = True
@@ -64,7 +68,7 @@ def visible_rows(rows: np.ndarray, seq_len: int, window_size: int, global_idx: n
 
 def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[int], scale: float,
                              rows: Sequence[int] | None = None, dtype=np.float64, block_rows: int = 256,
-                             causal: bool = False):
+                             causal: bool = False, dilation: int = 1):
     """Dense-mask attention on the CPU.
 
     Q, K, V: arrays [B, H, n, d] (any float dtype; converted to `dtype`).  window_size: one
@@ -91,10 +95,29 @@ def sliding_window_attention(Q, K, V, window_size: int, global_tokens: Sequence[
                 r = rows[s:s + block_rows]
                 q = Q[b, h, r].astype(dtype, copy=False)
                 scores = (q @ k.T) * dtype(scale)
-                scores = np.where(visible_rows(r, n, windows[h], g, causal), scores, -np.inf)
+                scores = np.where(visible_rows(r, n, windows[h], g, causal, dilation), scores, -np.inf)
                 m = scores.max(axis=1, keepdims=True)
                 p = np.exp(scores - m)
                 l = p.sum(axis=1, keepdims=True)
                 out[b, h, s:s + r.size] = (p @ v) / l
                 lse[b, h, s:s + r.size] = (m + np.log(l))[:, 0]
+    return out, lse
+
+
+def sliding_window_attention_varlen(Q, K, V, cu_seqlens: Sequence[int], window_size, global_tokens: Sequence[int],
+                                    scale: float, causal: bool = False, dtype=np.float64):
+    """Packed sequences: Q, K, V [1, H, total, d] with sequence s in rows
+    [cu_seqlens[s], cu_seqlens[s + 1]); each sequence is attended on its own by
+    :func:`sliding_window_attention`, the global-token list indexed within it.  Returns
+    (O [1, H, total, d], LSE [1, H, total])."""
+    Q, K, V = np.asarray(Q), np.asarray(K), np.asarray(V)
+    out = np.empty(Q.shape, dtype=dtype)
+    lse = np.empty(Q.shape[:3], dtype=dtype)
+    for s in range(len(cu_seqlens) - 1):
+        a, b = int(cu_seqlens[s]), int(cu_seqlens[s + 1])
+        if b == a:
+            continue
+        o, l = sliding_window_attention(Q[:, :, a:b], K[:, :, a:b], V[:, :, a:b], window_size, global_tokens, scale,
+                                        dtype=dtype, causal=causal)
+        out[:, :, a:b], lse[:, :, a:b] = o, l
     return out, lse

@@ -86,3 +86,36 @@ def test_head_window_validation_before_device_work():
     assert "head_window_sizes[1]" in c.last_error()
     assert ex([1] * 257, 257) == c.ERR_UNSUPPORTED
     assert ex([1, 2], 2) == c.ERR_INVALID_ARGUMENT  # NULL tensors, after the radii checked out
+
+
+def test_varlen_and_dilated_validation_before_device_work():
+    import ctypes
+    c = _native.cabi()
+    i64 = ctypes.c_int64
+
+    def varlen(cu, tokens=()):
+        arr = (i64 * len(cu))(*cu)
+        tok = (i64 * max(len(tokens), 1))(*tokens)
+        return c.lib.lca_swa_forward_varlen(None, None, None, None, c.DTYPE_F32, None, c.DTYPE_BF16, 1, cu[-1], 64, 8,
+                                            None, ctypes.c_float(0.1), 0, arr, len(cu) - 1, tok, len(tokens), None, 0,
+                                            None)
+
+    assert varlen([0, 10, 5]) == c.ERR_INVALID_ARGUMENT  # decreasing
+    assert varlen([1, 10]) == c.ERR_INVALID_ARGUMENT     # not from 0
+    assert varlen(list(range(0, 514))) == c.ERR_UNSUPPORTED  # 513 sequences
+    assert varlen([0, 100, 150], [60]) == c.ERR_INDEX    # index 60 is outside the second sequence
+    assert varlen([0, 100, 150], [40, -50]) == c.ERR_INVALID_ARGUMENT  # valid tokens, NULL tensors
+
+    def dilated(n, dil, flags=0):
+        return c.lib.lca_swa_forward_dilated(None, None, None, None, c.DTYPE_F32, None, c.DTYPE_BF16, 1, 1, n, 64, 8,
+                                             None, dil, ctypes.c_float(0.1), flags, None, 0, None, 0, None)
+
+    assert dilated(100, 0) == c.ERR_INVALID_ARGUMENT
+    assert dilated(100, 3) == c.ERR_UNSUPPORTED          # not a multiple
+    assert dilated(99, 3, c.FLAG_CAUSAL) == c.ERR_UNSUPPORTED
+    assert dilated(99, 3) == c.ERR_INVALID_ARGUMENT      # NULL tensors
+    size = ctypes.c_size_t(0)
+    assert c.lib.lca_swa_dilated_workspace_size(1, 2, 96, 64, 8, 3, 0, c.DTYPE_BF16, c.DTYPE_F32,
+                                                ctypes.byref(size)) == c.OK
+    base = c.workspace_size(1, 2, 96, 64, 8, 0, c.DTYPE_BF16)[1]
+    assert size.value >= base + 3 * 2 * 96 * 64 * 2 + 2 * 96 * 64 * 4

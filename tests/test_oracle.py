@@ -104,3 +104,24 @@ def test_causal_oracle_is_the_dense_mask_with_the_upper_triangle_removed():
         assert np.abs(got - want).max() < 2e-6
         # every row keeps at least its own key
         assert np.isfinite(lse).all()
+
+
+
+def test_dilated_and_varlen_oracle():
+    """The oracle's dilated band against the package's dense torch definition, and its packed
+    sequences against running each sequence alone."""
+    import torch
+
+    from long_context_attention import _dense_causal_attention
+    gen = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 2, 60, 8, generator=gen) for _ in range(3))
+    for w, dil, g in [(3, 2, [0]), (5, 3, [7, 59]), (100, 4, [])]:
+        want = _dense_causal_attention(q, k, v, w, g, 0.4, dilation=dil, causal=False).numpy()
+        got, _ = swa_oracle.sliding_window_attention(q.numpy(), k.numpy(), v.numpy(), w, g, 0.4, dilation=dil)
+        assert np.abs(got - want).max() < 2e-6
+    cu = [0, 25, 25, 60]
+    got, lse = swa_oracle.sliding_window_attention_varlen(q.numpy(), k.numpy(), v.numpy(), cu, 4, [0, -1], 0.4)
+    for a, b in [(0, 25), (25, 60)]:
+        want, want_lse = swa_oracle.sliding_window_attention(q[:, :, a:b].numpy(), k[:, :, a:b].numpy(),
+                                                             v[:, :, a:b].numpy(), 4, [0, -1], 0.4)
+        assert np.array_equal(got[:, :, a:b], want) and np.array_equal(lse[:, :, a:b], want_lse)
