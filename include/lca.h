@@ -127,7 +127,11 @@ enum {
     /* Causal (one-sided) variant: the mask above intersected with j <= i -- the band
      * becomes [i - window_size, i], a global key is visible to the rows at or after it,
      * and a global row sees the keys up to itself. */
-    LCA_FLAG_CAUSAL = 1
+    LCA_FLAG_CAUSAL = 1,
+    /* q, k, v and out are token-major, [batch, seq_len, heads, head_dim] (the layout of a
+     * fused QKV projection's output), read and written in place without a transpose; lse
+     * stays [batch, heads, seq_len].  Not with dilation. */
+    LCA_FLAG_TOKEN_MAJOR = 2
 };
 
 /* Most heads that lca_swa_forward_ex accepts radii of their own for. */
@@ -142,7 +146,7 @@ enum {
  *   head_window_sizes  NULL, or a HOST array of `heads` band radii (each >= 0): head h of
  *                every batch uses head_window_sizes[h] in place of window_size (which is then
  *                ignored).  At most LCA_MAX_HEAD_WINDOWS heads.
- *   flags        0 or LCA_FLAG_CAUSAL.
+ *   flags        LCA_FLAG_CAUSAL and / or LCA_FLAG_TOKEN_MAJOR, or 0.
  * The other arguments are lca_swa_forward's; lca_swa_forward(...) is
  * lca_swa_forward_ex(..., LCA_DTYPE_F32, ..., NULL, ..., 0, ...).
  */

@@ -35,26 +35,29 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
                                         int64_t window_size, const std::vector<int64_t>& globals, double scale,
                                         bool want_lse, c10::ScalarType out_type = torch::kFloat32,
                                         bool causal = false, const std::vector<int64_t>& head_windows = {},
-                                        int64_t dilation = 1, const std::vector<int64_t>& cu_seqlens = {}) {
+                                        int64_t dilation = 1, const std::vector<int64_t>& cu_seqlens = {},
+                                        bool token_major = false) {
     check_input(Q, "Q");
     check_input(K, "K");
     check_input(V, "V");
-    TORCH_CHECK(Q.dim() == 4, "Q must be [batch, heads, seq_len, head_dim]");
+    TORCH_CHECK(Q.dim() == 4, token_major ? "Q must be [batch, seq_len, heads, head_dim]"
+                                          : "Q must be [batch, heads, seq_len, head_dim]");
     TORCH_CHECK(K.sizes() == Q.sizes() && V.sizes() == Q.sizes(), "Q, K and V must have the same shape");
     TORCH_CHECK(K.scalar_type() == Q.scalar_type() && V.scalar_type() == Q.scalar_type(),
                 "Q, K and V must have the same dtype");
     TORCH_CHECK(K.device() == Q.device() && V.device() == Q.device(), "Q, K and V must be on the same device");
-    const int64_t batch = Q.size(0), heads = Q.size(1), seq_len = Q.size(2), head_dim = Q.size(3);
+    const int64_t batch = Q.size(0), heads = Q.size(token_major ? 2 : 1), seq_len = Q.size(token_major ? 1 : 2),
+                  head_dim = Q.size(3);
     TORCH_CHECK(head_dim == 64 || head_dim == 128, "head_dim must be 64 or 128 (got ", head_dim, ")");
     TORCH_CHECK(window_size >= 0, "window_size must be >= 0 (got ", window_size, ")");
-    TORCH_CHECK(head_windows.empty() || (int64_t)head_windows.size() == Q.size(1),
-                "window_size per head needs one radius per head (got ", head_windows.size(), " for ", Q.size(1),
+    TORCH_CHECK(head_windows.empty() || (int64_t)head_windows.size() == heads,
+                "window_size per head needs one radius per head (got ", head_windows.size(), " for ", heads,
                 " heads)");
     TORCH_CHECK(out_type == torch::kFloat32 || out_type == torch::kFloat16 || out_type == torch::kBFloat16,
                 "out_dtype must be float32, float16 or bfloat16");
 
     c10::cuda::CUDAGuard guard(Q.device());
-    auto O = torch::empty({batch, heads, seq_len, head_dim}, Q.options().dtype(out_type));
+    auto O = torch::empty(Q.sizes(), Q.options().dtype(out_type));  // the input's layout
     torch::Tensor L;
     if (want_lse) L = torch::empty({batch, heads, seq_len}, Q.options().dtype(torch::kFloat32));
 
@@ -93,7 +96,7 @@ std::vector<torch::Tensor> forward_impl(const torch::Tensor& Q, const torch::Ten
     }
     cudaStream_t stream = at::cuda::getCurrentCUDAStream();
     const int64_t* hw = head_windows.empty() ? nullptr : head_windows.data();
-    const int flags = causal ? LCA_FLAG_CAUSAL : 0;
+    const int flags = (causal ? LCA_FLAG_CAUSAL : 0) | (token_major ? LCA_FLAG_TOKEN_MAJOR : 0);
     float* lse_ptr = want_lse ? L.data_ptr<float>() : nullptr;
     void* sp = static_cast<void*>(stream);
     int st;
@@ -141,9 +144,10 @@ std::vector<torch::Tensor> sliding_window_attention_forward_ex(torch::Tensor Q, 
                                                                int64_t window_size, std::vector<int64_t> global_tokens,
                                                                double scale, c10::ScalarType out_dtype, bool causal,
                                                                bool want_lse, std::vector<int64_t> head_windows,
-                                                               int64_t dilation, std::vector<int64_t> cu_seqlens) {
+                                                               int64_t dilation, std::vector<int64_t> cu_seqlens,
+                                                               bool token_major) {
     return forward_impl(Q, K, V, window_size, global_tokens, scale, want_lse, out_dtype, causal, head_windows,
-                        dilation, cu_seqlens);
+                        dilation, cu_seqlens, token_major);
 }
 
 int device_error() {
@@ -170,7 +174,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("window_size"), py::arg("global_tokens"),
           py::arg("scale"), py::arg("out_dtype"), py::arg("causal"), py::arg("want_lse"),
           py::arg("head_windows") = std::vector<int64_t>{}, py::arg("dilation") = 1,
-          py::arg("cu_seqlens") = std::vector<int64_t>{});
+          py::arg("cu_seqlens") = std::vector<int64_t>{}, py::arg("token_major") = false);
     m.def("device_error", &device_error, "Read and clear the device-side error word (synchronises)");
     m.attr("abi_version") = lca_abi_version();
 }

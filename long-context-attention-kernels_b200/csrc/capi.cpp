@@ -114,6 +114,8 @@ int check_device(int* dev_out, int** err_word) {
 // shard of it.
 struct Problem {
     int64_t bh = 0;
+    int64_t heads = 1;     // heads per batch (bh = batch * heads)
+    bool tok_major = false;  // q, k, v, out are [batch][n][heads][d] (else [batch][heads][n][d])
     int64_t n_total = 0;   // sequence length
     int64_t n = 0;         // local rows of Q / K / V / O
     int64_t q_off = 0;     // absolute index of local row 0
@@ -132,6 +134,10 @@ struct Problem {
     float scale = 1.f;
     std::vector<int32_t> gl;  // sorted unique global indices (absolute)
     int64_t halo() const { return sharded && world > 1 ? window : 0; }
+    // element strides of q / k / v / out: batch, head, row
+    int64_t s_b() const { return tok_major ? n * heads * d : heads * n * d; }
+    int64_t s_h() const { return tok_major ? d : n * d; }
+    int64_t s_n() const { return tok_major ? heads * d : d; }
     int64_t lead() const {
         return sharded ? (window + lca::kTileRows - 1) / lca::kTileRows * lca::kTileRows : window;
     }
@@ -169,6 +175,7 @@ int parse_common(Problem& P, int dtype, int64_t batch, int64_t heads, int64_t se
     if (st != LCA_OK) return st;
     P.gl.resize((size_t)G);
     P.bh = bh;
+    P.heads = heads > 0 ? heads : 1;
     P.n_total = seq_len;
     P.n = seq_len;
     P.q_off = 0;
@@ -344,6 +351,24 @@ int encode_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* bas
     return LCA_OK;
 }
 
+// Token-major tensor [batch][n][heads][d] as the 4-D map {d, heads, n, batch} (strides in
+// increasing order), box box_x columns x 1 head x 128 rows x 1 batch: the box lands in shared
+// memory like a box_x x 128 box of a head-major tensor.
+int encode_tok(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t d, uint64_t heads,
+               uint64_t rows, uint64_t batch, uint32_t box_x, const char* name,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (enc == nullptr) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+    cuuint64_t dims[4] = {d, heads, rows, batch};
+    cuuint64_t strides[3] = {d * (uint64_t)esize, heads * d * (uint64_t)esize, rows * heads * d * (uint64_t)esize};
+    cuuint32_t box[4] = {box_x, 1, (cuuint32_t)lca::kTileRows, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
+    return LCA_OK;
+}
+
 // Compact global rows [G][3][bh][d] (16-bit): dims {d, bh, G} with the row stride of a
 // whole compact row, box 64 columns x 1 head x 128 rows (lands in shared memory exactly
 // like a 64 x 128 box of a [bh][n][d] tensor).
@@ -404,6 +429,10 @@ int enqueue_gather(const Problem& P, const Layout& L, const void* q, const void*
     for (int first = 0; first < (int)P.G; first += lca::kGatherChunk) {
         gp.n = (int)P.n;
         gp.q_off = (int)P.q_off;
+        gp.heads = (int)P.heads;
+        gp.s_b = P.s_b();
+        gp.s_h = P.s_h();
+        gp.s_n = P.s_n();
         gp.num_global = (int)P.G;
         gp.bh = (int)P.bh;
         gp.first = first;
@@ -435,8 +464,13 @@ int enqueue_convert_v16(const Problem& P, const Layout& L, const void* v, uint8_
         g.src_row = src_row;
         g.dst_plane = dst_plane;
         g.dst_row = dst_row;
+        g.heads = 1;
+        g.src_head = 0;
     };
-    add(static_cast<const uint16_t*>(v), reinterpret_cast<uint16_t*>(ws + L.off_v16), bh, P.n, P.n * d, d, P.n * d, d);
+    add(static_cast<const uint16_t*>(v), reinterpret_cast<uint16_t*>(ws + L.off_v16), bh, P.n, P.s_b(), P.s_n(), P.n * d,
+        d);
+    cv.seg[0].heads = (int)P.heads;  // the caller's V in its own layout
+    cv.seg[0].src_head = P.s_h();
     if (P.G > 0) {
         // compact rows [G][3][bh][d]: the v plane of row g starts 2 * bh * d elements in
         const uint16_t* vg = reinterpret_cast<const uint16_t*>(ws + L.off_globals) + 2 * bh * d;
@@ -470,7 +504,7 @@ struct MapKey {
     const void* out;
     const void* ws;
     int64_t n, n_total, q_off, d, bh, G, window, world;
-    int dtype, out_dtype, sharded, v16, n_splits, dev;
+    int dtype, out_dtype, sharded, v16, n_splits, dev, tok_major, heads;
 };
 constexpr int kMapCache = 4;
 thread_local MapKey g_map_key[kMapCache];
@@ -488,16 +522,24 @@ int encode_maps(const Problem& P, const Layout& L, const void* q, const void* k,
     const int halo = (int)P.halo();
     int st;
     memset(&tm, 0, sizeof(tm));
-    if ((st = encode_3d(&tm.q, tdt, 2, q, d, n, bh, 64, "q")) != LCA_OK) return st;
-    if ((st = encode_3d(&tm.k, tdt, 2, k, d, n, bh, 64, "k")) != LCA_OK) return st;
-    if ((st = encode_3d(&tm.v, tdt, 2, v, d, n, bh, 64, "v")) != LCA_OK) return st;
-    if (P.out_dtype == LCA_DTYPE_F32) {
-        if ((st = encode_3d(&tm.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, d, n, bh, 32, "out")) != LCA_OK) return st;
+    const CUtensorMapDataType odt = P.out_dtype == LCA_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : P.out_dtype == LCA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int osize = P.out_dtype == LCA_DTYPE_F32 ? 4 : 2;
+    // fp32 output in 32-column boxes of 128-byte swizzled rows; 16-bit output in 32-column
+    // boxes of 64-byte rows, unswizzled
+    const CUtensorMapSwizzle osw = P.out_dtype == LCA_DTYPE_F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    if (P.tok_major) {
+        const uint64_t H = (uint64_t)P.heads, B = bh / H;
+        if ((st = encode_tok(&tm.q, tdt, 2, q, d, H, n, B, 64, "q")) != LCA_OK) return st;
+        if ((st = encode_tok(&tm.k, tdt, 2, k, d, H, n, B, 64, "k")) != LCA_OK) return st;
+        if ((st = encode_tok(&tm.v, tdt, 2, v, d, H, n, B, 64, "v")) != LCA_OK) return st;
+        if ((st = encode_tok(&tm.o, odt, osize, out, d, H, n, B, 32, "out", osw)) != LCA_OK) return st;
     } else {
-        // 16-bit output: 32-column boxes of 64-byte rows, unswizzled
-        const CUtensorMapDataType odt =
-            P.out_dtype == LCA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-        if ((st = encode_3d(&tm.o, odt, 2, out, d, n, bh, 32, "out", CU_TENSOR_MAP_SWIZZLE_NONE)) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.q, tdt, 2, q, d, n, bh, 64, "q")) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.k, tdt, 2, k, d, n, bh, 64, "k")) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.v, tdt, 2, v, d, n, bh, 64, "v")) != LCA_OK) return st;
+        if ((st = encode_3d(&tm.o, odt, osize, out, d, n, bh, 32, "out", osw)) != LCA_OK) return st;
     }
     if (halo > 0) {
         // recv block [2 sides][2 (k, v)][bh][halo][d]: K planes at z = side * 2bh + b from
@@ -565,6 +607,8 @@ int cached_maps(const Problem& P, const Layout& L, int dev, const void* q, const
     key.world = P.world;
     key.dtype = P.dtype;
     key.out_dtype = P.out_dtype;
+    key.tok_major = P.tok_major ? 1 : 0;
+    key.heads = (int)P.heads;
     key.sharded = P.sharded ? 1 : 0;
     key.v16 = v16 ? 1 : 0;
     key.n_splits = L.n_splits;
@@ -626,6 +670,7 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     p.causal = P.causal ? 1 : 0;
     p.n_head_windows = (int)P.head_window.size();
     for (size_t h = 0; h < P.head_window.size(); ++h) p.head_window[h] = P.head_window[h];
+    p.heads4d = P.tok_major ? (int)P.heads : 0;
     p.seg_mode = P.seg_mode;
     p.seg_len = (int)P.seg_len;
     p.n_segs = P.seg_start.empty() ? 0 : (int)P.seg_start.size() - 1;
@@ -692,6 +737,10 @@ int enqueue_combine_splits(const Problem& P, const Layout& L, void* out, float* 
         cp.out16 = P.out_dtype == LCA_DTYPE_F32 ? 0 : (P.out_dtype == LCA_DTYPE_BF16 ? lca::kOut16BF16 : lca::kOut16F16);
         cp.n_rows = (int)P.n;
         cp.row_off = 0;
+        cp.heads = (int)P.heads;
+        cp.o_b = P.s_b();
+        cp.o_h = P.s_h();
+        cp.o_n = P.s_n();
     }
     cudaError_t e = lca::launch_combine((int)P.d, cp, stream);
     if (e != cudaSuccess) return fail_cuda(e, "combine launch");
@@ -704,7 +753,8 @@ int run_problem(const Problem& P, const void* q, const void* k, const void* v, v
 int check_out_flags(int out_dtype, int flags) {
     if (out_dtype != LCA_DTYPE_F32 && out_dtype != LCA_DTYPE_F16 && out_dtype != LCA_DTYPE_BF16)
         return fail(LCA_ERR_UNSUPPORTED, "out_dtype %d is not supported (fp32, fp16 or bf16)", out_dtype);
-    if ((flags & ~LCA_FLAG_CAUSAL) != 0) return fail(LCA_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    if ((flags & ~(LCA_FLAG_CAUSAL | LCA_FLAG_TOKEN_MAJOR)) != 0)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
     return LCA_OK;
 }
 
@@ -837,6 +887,7 @@ int lca_swa_forward_ex(const void* q, const void* k, const void* v, void* out, i
     P.head_window = std::move(head_window);
     P.out_dtype = out_dtype;
     P.causal = (flags & LCA_FLAG_CAUSAL) != 0;
+    P.tok_major = (flags & LCA_FLAG_TOKEN_MAJOR) != 0;
     return run_problem(P, q, k, v, out, lse, workspace, workspace_bytes, stream_ptr);
 }
 
@@ -886,6 +937,7 @@ int lca_swa_forward_varlen(const void* q, const void* k, const void* v, void* ou
     P.head_window = std::move(head_window);
     P.out_dtype = out_dtype;
     P.causal = (flags & LCA_FLAG_CAUSAL) != 0;
+    P.tok_major = (flags & LCA_FLAG_TOKEN_MAJOR) != 0;
     if (num_seqs > 1) {
         P.seg_mode = lca::kSegVarlen;
         for (int64_t i = 0; i <= num_seqs; ++i) P.seg_start.push_back((int)cu_seqlens[i]);
@@ -956,6 +1008,8 @@ int lca_swa_forward_dilated(const void* q, const void* k, const void* v, void* o
     if (st != LCA_OK) return st;
     if (flags & LCA_FLAG_CAUSAL)
         return fail(LCA_ERR_UNSUPPORTED, "the causal variant has no dilated form in this build");
+    if (flags & LCA_FLAG_TOKEN_MAJOR)
+        return fail(LCA_ERR_UNSUPPORTED, "the dilated window takes head-major tensors in this build");
     if (seq_len % dilation != 0)
         return fail(LCA_ERR_UNSUPPORTED, "seq_len %lld is not a multiple of the dilation %lld", (long long)seq_len,
                     (long long)dilation);
@@ -1148,6 +1202,10 @@ int lca_swa_shard_finish(const lca_shard_desc* desc, float* out, float* lse, con
     cp.part_lse = cp.part_o + (size_t)P.bh * P.G * P.d;
     cp.gidx = reinterpret_cast<const int*>(ws + L.off_gidx);
     cp.o = out;
+    cp.heads = (int)P.heads;
+    cp.o_b = P.s_b();
+    cp.o_h = P.s_h();
+    cp.o_n = P.s_n();
     cp.lse = lse;
     cp.n_rows = (int)P.n;
     cp.row_off = (int)P.q_off;
@@ -1334,6 +1392,10 @@ int lca_swa_shard_finish_peer(const lca_shard_desc* desc, float* out, float* lse
     cp.part_lse = cp.part_o + (size_t)P.bh * P.G * P.d;
     cp.gidx = reinterpret_cast<const int*>(at(peer_workspaces, rank, L.off_gidx));
     cp.o = out;
+    cp.heads = (int)P.heads;
+    cp.o_b = P.s_b();
+    cp.o_h = P.s_h();
+    cp.o_n = P.s_n();
     cp.lse = lse;
     cp.n_rows = (int)P.n;
     cp.row_off = (int)P.q_off;

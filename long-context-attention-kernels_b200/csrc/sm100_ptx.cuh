@@ -132,6 +132,26 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
         : "memory");
 }
 
+// 4-D tiled load (token-major [batch][n][heads][d] tensors mapped as {d, heads, n, batch}):
+// x = column (16-byte aligned, as above), h = head, y = row, b = batch.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int h, int y,
+                                            int b) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(h), "r"(y), "r"(b)
+        : "memory");
+}
+
+// 4-D tiled store shared -> global, coordinates as tma_load_4d.
+__device__ __forceinline__ void tma_store_4d(const void* tmap, const void* smem_src, int x, int h, int y, int b) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(tmap)),
+        "r"(smem_u32(smem_src)), "r"(x), "r"(h), "r"(y), "r"(b)
+        : "memory");
+}
+
 // 3-D tiled store shared -> global (rows outside the tensor are clipped by the TMA unit).
 __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_src, int x, int y, int z) {
     asm volatile(

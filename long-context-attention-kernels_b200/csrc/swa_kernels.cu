@@ -450,9 +450,14 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                         }
                         ptx::mbar_arrive_expect_tx(&ctl->q_full[x], C::kTileBytes);
 #pragma unroll
-                        for (int pn = 0; pn < C::kPanels; ++pn)
-                            ptx::tma_load_3d(sQ + x * C::kTileBytes + pn * kPanelBytes, mq, &ctl->q_full[x],
-                                             pn * 64, qy, qz);
+                        for (int pn = 0; pn < C::kPanels; ++pn) {
+                            if (p.heads4d > 0 && !un.grow)  // token-major: (column, head, row, batch)
+                                ptx::tma_load_4d(sQ + x * C::kTileBytes + pn * kPanelBytes, mq, &ctl->q_full[x],
+                                                 pn * 64, qz % p.heads4d, qy, qz / p.heads4d);
+                            else
+                                ptx::tma_load_3d(sQ + x * C::kTileBytes + pn * kPanelBytes, mq, &ctl->q_full[x],
+                                                 pn * 64, qy, qz);
+                        }
                     }
                     if (!ok) break;
                     ++qn;
@@ -489,9 +494,16 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                             }
                             uint8_t* dst = sSlots + slot * C::kTileBytes;
                             ptx::mbar_arrive_expect_tx(&ctl->kv_full[slot], C::kTileBytes);
+                            // token-major K / V (not the fp16 copy of V, which is head-major)
+                            const bool four = p.heads4d > 0 && (m == &tm_k || m == &tm_v);
 #pragma unroll
-                            for (int pn = 0; pn < C::kPanels; ++pn)
-                                ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64, y, z);
+                            for (int pn = 0; pn < C::kPanels; ++pn) {
+                                if (four)
+                                    ptx::tma_load_4d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64,
+                                                     z % p.heads4d, y, z / p.heads4d);
+                                else
+                                    ptx::tma_load_3d(dst + pn * kPanelBytes, m, &ctl->kv_full[slot], pn * 64, y, z);
+                            }
                             ++L;
                         }
                     }
@@ -1066,7 +1078,10 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
                 ptx::fence_proxy_async_smem();
                 ptx::named_bar_sync(wg_bar, kWgThreads);
                 if (r == 0 && ok) {
-                    ptx::tma_store_3d(mo, panel, ocol, qrow_x, oz);
+                    if (p.heads4d > 0 && !un.grow)
+                        ptx::tma_store_4d(mo, panel, ocol, oz % p.heads4d, qrow_x, oz / p.heads4d);
+                    else
+                        ptx::tma_store_3d(mo, panel, ocol, qrow_x, oz);
                     ptx::tma_store_commit();
                 }
             }
@@ -1142,7 +1157,7 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
     const int src_row = src_abs - gp.q_off;
     if (bh == 0 && lane == 0) gp.gidx_out[g] = src_abs;
     if (src_row < 0 || src_row >= gp.n) return;  // owned by another shard
-    const size_t src_off = ((size_t)bh * gp.n + src_row) * D;
+    const size_t src_off = (size_t)(bh / gp.heads) * gp.s_b + (size_t)(bh % gp.heads) * gp.s_h + (size_t)src_row * gp.s_n;
     for (int c = lane; c < 3 * kChunks; c += 32) {
         const int which = c / kChunks;
         const int cc = c % kChunks;
@@ -1185,7 +1200,8 @@ __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
         const int c = (int)threadIdx.x + i * 256;
         if (c < total) {
             const long long r = r0 + c / kChunksPerRow;
-            in[i] = *reinterpret_cast<const uint4*>(sg.src + pl * sg.src_plane + r * sg.src_row +
+            in[i] = *reinterpret_cast<const uint4*>(sg.src + (long long)(pl / sg.heads) * sg.src_plane +
+                                                    (long long)(pl % sg.heads) * sg.src_head + r * sg.src_row +
                                                     (c % kChunksPerRow) * 8);
         }
     }
@@ -1359,7 +1375,7 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
     } else {
         const int orow = cp.gidx[g] - cp.row_off;
         if (orow >= 0 && orow < cp.n_rows) {  // else owned by another shard
-            out_idx = ((size_t)bh * cp.n_rows + orow) * D;
+            out_idx = (size_t)(bh / cp.heads) * cp.o_b + (size_t)(bh % cp.heads) * cp.o_h + (size_t)orow * cp.o_n;
             out16 = cp.out16;
             out_row = static_cast<float*>(cp.o) + (out16 ? 0 : out_idx);
             lse_out = cp.lse != nullptr ? cp.lse + (size_t)bh * cp.n_rows + orow : nullptr;

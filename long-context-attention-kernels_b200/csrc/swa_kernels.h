@@ -98,6 +98,10 @@ struct MainParams {
     int seg_len;
     int n_segs;
     int seg_start[kMaxSegments + 1];
+    // Token-major q, k, v and out ([batch][n][heads][d], whole-sequence problems): their maps
+    // (tm.q, tm.k, tm.v, tm.o) are 4-D {d, heads, n, batch} and take (column, head, row,
+    // batch); heads4d = heads, or 0 for the 3-D head-major maps.
+    int heads4d;
 };
 constexpr int kSegNone = 0;
 constexpr int kSegEqual = 1;
@@ -111,6 +115,8 @@ constexpr int kOut16BF16 = 2;
 struct GatherParams {
     int n, q_off;      // local rows of q / k / v and the absolute index of row 0
     int num_global, bh;
+    int heads;         // element offset of (bh, row): (bh / heads) * s_b + (bh % heads) * s_h + row * s_n
+    long long s_b, s_h, s_n;
     int first, count;  // compact rows [first, first + count) handled by this launch
     int* gidx_out;
     uint16_t* compact;
@@ -143,6 +149,8 @@ struct CombineParams {
     void* o;          // fp32, or 16-bit per out16
     float* lse;
     int out16;        // type of o: 0 fp32, kOut16F16, kOut16BF16
+    int heads;        // element offset of row (bh, r) of o: (bh / heads) * o_b + (bh % heads) * o_h + r * o_n
+    long long o_b, o_h, o_n;
     int n_rows, row_off;
     float* out_o;
     float* out_lse;
@@ -167,6 +175,8 @@ struct ConvertSegment {
     uint16_t* dst;
     int planes, rows;
     long long src_plane, src_row, dst_plane, dst_row;
+    int heads;            // source plane pl at (pl / heads) * src_plane + (pl % heads) * src_head
+    long long src_head;
 };
 struct ConvertParams {
     int n_segments;

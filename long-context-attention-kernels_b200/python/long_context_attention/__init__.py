@@ -100,7 +100,13 @@ def _dense(Q, K, V, window_size, global_tokens, scale, causal: bool, dilation: i
                       for h in range(Q.shape[1])], dim=1)
 
 
-def _prepare(Q: torch.Tensor, window_size, global_tokens: Sequence[int], scale):
+def _token_major(layout: str) -> bool:
+    if layout not in ("bhnd", "bnhd"):
+        raise ValueError(f"layout must be 'bhnd' or 'bnhd', got {layout!r}")
+    return layout == "bnhd"
+
+
+def _prepare(Q: torch.Tensor, window_size, global_tokens: Sequence[int], scale, token_major: bool = False):
     if scale is None:
         scale = 1.0 / math.sqrt(Q.shape[-1])
     if not Q.is_cuda:
@@ -109,7 +115,7 @@ def _prepare(Q: torch.Tensor, window_size, global_tokens: Sequence[int], scale):
             "pass force_reference=True for the dense CPU definition"
         )
     tokens = [int(t) for t in global_tokens]
-    window, radii = _head_windows(window_size, Q.shape[1])
+    window, radii = _head_windows(window_size, Q.shape[2] if token_major else Q.shape[1])
     return float(scale), window, tokens, radii
 
 
@@ -124,6 +130,7 @@ def sliding_window_attention(
     out_dtype: torch.dtype | None = None,
     causal: bool = False,
     dilation: int = 1,
+    layout: str = "bhnd",
 ) -> torch.Tensor:
     """Longformer-style sparse attention forward.
 
@@ -140,18 +147,26 @@ def sliding_window_attention(
     key is seen by the rows at or after it, a global row sees the keys up to itself.
     ``dilation`` > 1 (also an addition) keeps, of the band, the keys i + dilation * t with
     |t| <= window_size (seq_len must be a multiple of the dilation; not with causal).
+    ``layout="bnhd"`` (also an addition) takes Q, K, V as [batch, seq_len, heads, head_dim],
+    the layout of a fused QKV projection's output, without a transpose, and returns O in the
+    same layout (not with dilation).
     """
+    tm = _token_major(layout)
     if force_reference:
         if scale is None:
             scale = 1.0 / math.sqrt(Q.shape[-1])
+        if tm:
+            Q, K, V = (t.transpose(1, 2) for t in (Q, K, V))
         out = _dense(Q, K, V, window_size, global_tokens, scale, causal, int(dilation))
+        if tm:
+            out = out.transpose(1, 2).contiguous()
         return out if out_dtype in (None, torch.float32) else out.to(out_dtype)
-    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1:
+    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale, tm)
+    if out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1 and not tm:
         return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
     return extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
                                                            out_dtype or torch.float32, bool(causal), False,
-                                                           radii, int(dilation))[0]
+                                                           radii, int(dilation), [], tm)[0]
 
 
 def sliding_window_attention_with_lse(
@@ -164,6 +179,7 @@ def sliding_window_attention_with_lse(
     out_dtype: torch.dtype | None = None,
     causal: bool = False,
     dilation: int = 1,
+    layout: str = "bhnd",
 ):
     """As :func:`sliding_window_attention`, also returning the per-row log-sum-exp.
 
@@ -171,13 +187,14 @@ def sliding_window_attention_with_lse(
     sum of exp(scale * q.k) over each row's visible keys (the quantity a backward pass
     or a cross-shard merge needs).  No counterpart in the reference.
     """
-    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
-    if out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1:
+    tm = _token_major(layout)
+    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale, tm)
+    if out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1 and not tm:
         out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
     else:
         out, lse = extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
                                                                    out_dtype or torch.float32, bool(causal), True,
-                                                                   radii, int(dilation))
+                                                                   radii, int(dilation), [], tm)
     return out, lse
 
 
@@ -192,20 +209,22 @@ def sliding_window_attention_varlen(
     out_dtype: torch.dtype | None = None,
     causal: bool = False,
     return_lse: bool = False,
+    layout: str = "bhnd",
 ):
     """Packed variable-length sequences (no counterpart in the reference).
 
-    Q, K, V: [1, heads, total_len, head_dim] with sequence s in rows
-    ``[cu_seqlens[s], cu_seqlens[s + 1])`` (host offsets from 0 to total_len, at most 512
-    sequences).  Each sequence is attended on its own: its band, global keys and global
+    Q, K, V: [1, heads, total_len, head_dim] (or [1, total_len, heads, head_dim] with
+    ``layout="bnhd"``) with sequence s in rows ``[cu_seqlens[s], cu_seqlens[s + 1])`` (host
+    offsets from 0 to total_len, at most 512 sequences).  Each sequence is attended on its own: its band, global keys and global
     rows stay inside it, and ``global_tokens`` is indexed within each sequence as the
     reference indexes one sequence.  Returns O (and LSE with ``return_lse``).
     """
-    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
+    tm = _token_major(layout)
+    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale, tm)
     cu = [int(x) for x in (cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else cu_seqlens)]
     res = extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
                                                           out_dtype or torch.float32, bool(causal), bool(return_lse),
-                                                          radii, 1, cu)
+                                                          radii, 1, cu, tm)
     return (res[0], res[1]) if return_lse else res[0]
 
 

@@ -74,6 +74,7 @@ class CABI:
     DTYPE_BF16 = 1
     DTYPE_F32 = 2
     FLAG_CAUSAL = 1
+    FLAG_TOKEN_MAJOR = 2
 
     def __init__(self, path: str = LIB_PATH):
         if not os.path.exists(path):

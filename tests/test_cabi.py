@@ -67,10 +67,10 @@ def test_typed_forward_validation_before_device_work():
 
     assert typed(7) == c.ERR_UNSUPPORTED
     assert "out_dtype" in c.last_error()
-    assert typed(c.DTYPE_F32, flags=2) == c.ERR_INVALID_ARGUMENT
+    assert typed(c.DTYPE_F32, flags=4) == c.ERR_INVALID_ARGUMENT
     assert "flags" in c.last_error()
     for dt in (c.DTYPE_F32, c.DTYPE_F16, c.DTYPE_BF16):
-        for flags in (0, c.FLAG_CAUSAL):
+        for flags in (0, c.FLAG_CAUSAL, c.FLAG_TOKEN_MAJOR, c.FLAG_CAUSAL | c.FLAG_TOKEN_MAJOR):
             assert typed(dt, batch=0, flags=flags) == c.OK
             assert typed(dt, flags=flags) == c.ERR_INVALID_ARGUMENT  # NULL tensors, before any launch
 
@@ -113,6 +113,7 @@ def test_varlen_and_dilated_validation_before_device_work():
     assert dilated(100, 0) == c.ERR_INVALID_ARGUMENT
     assert dilated(100, 3) == c.ERR_UNSUPPORTED          # not a multiple
     assert dilated(99, 3, c.FLAG_CAUSAL) == c.ERR_UNSUPPORTED
+    assert dilated(99, 3, c.FLAG_TOKEN_MAJOR) == c.ERR_UNSUPPORTED
     assert dilated(99, 3) == c.ERR_INVALID_ARGUMENT      # NULL tensors
     size = ctypes.c_size_t(0)
     assert c.lib.lca_swa_dilated_workspace_size(1, 2, 96, 64, 8, 3, 0, c.DTYPE_BF16, c.DTYPE_F32,
