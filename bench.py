@@ -413,6 +413,11 @@ def run_ours(args):
     h2d_all, d2h_all = (h2d * world, d2h * world) if pg is None else _sum_over_ranks(pg, dev, [h2d, d2h])
     del q, k, v
 
+    others = None
+    if world == 1 and not args.no_sequence and w.name == "many_globals_64k":
+        others = {name: measure_one_gpu(WORKLOADS[name], dev, steps=min(args.steps, 100), warmup=args.warmup)
+                  for name in ("single_head_16k", "longformer_base_4k")}
+
     sequence = None
     if not args.no_sequence and w.name != SEQUENCE_WORKLOAD:
         sequence = measure_sequence(WORKLOADS[SEQUENCE_WORKLOAD], world, rank, local, dev, pg,
@@ -449,6 +454,8 @@ def run_ours(args):
         }
         if sequence is not None:
             line["sequence_128k"] = sequence
+        if others is not None:
+            line["other_configs"] = others
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
@@ -460,6 +467,58 @@ def _sum_over_ranks(pg, dev, values):
     t = torch.tensor([float(x) for x in values], device=dev, dtype=torch.float64)
     pg.all_reduce(t)
     return [int(x) for x in t.tolist()]
+
+
+def measure_one_gpu(w, dev, steps: int, warmup: int) -> dict:
+    """One workload whole on this GPU: a step is one replay of one forward captured as a
+    CUDA graph (inputs resident); the main kernel is timed by the library's events in eager
+    calls.  For the workloads the headline line does not carry (one 16K head in fp16, the
+    96-head 4K batch), so every configuration has a device measurement."""
+    import long_context_attention as lca
+    from long_context_attention import _native
+
+    cabi = _native.cabi()
+    q, k, v = w.inputs(device=dev)
+    g = w.global_tokens()
+
+    def fwd():
+        return lca.sliding_window_attention(q, k, v, w.window, g, w.scale)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, 3)):
+            out = fwd()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = fwd()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        graph.replay()
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    n_main = min(steps, 20)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_main)]
+    for a, b in ev:
+        a.record()
+        b.record()
+    for a, b in ev:
+        cabi.lib.lca_set_timing_events(a.cuda_event, b.cuda_event)
+        out = fwd()
+    cabi.lib.lca_set_timing_events(None, None)
+    torch.cuda.synchronize()
+    main_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    assert lca.device_error() == 0
+    del out, graph, q, k, v
+    rf = roofline(w.useful_flops(), w.io_bytes(), main_ms, None, "lca_swa_main")
+    return {"workload": w.name, "metric": metric_of(w), "value": w.tokens() / (ms * 1e-3), "unit": UNIT,
+            "ms_per_step": ms, "main_kernel_ms": main_ms, "useful_tflops": w.useful_flops() / (ms * 1e-3) / 1e12,
+            "config": config_of(w, 1, "one GPU"), "roofline": rf,
+            "step_timing": "replays of one forward captured as a CUDA graph"}
 
 
 def measure_sequence(w, world, rank, local, dev, pg, steps, warmup, exchange, e2e_steps, cpu, heads=None,
