@@ -449,7 +449,17 @@ int enqueue_gather(const Problem& P, const Layout& L, const void* q, const void*
 // The main kernel over band and global-row units.
 // fp16 copy of V (the optional workspace suffix): this rank's V rows, the compact global V
 // rows (complete once gathered, and for a shard once exchanged) and the received halos.
-int enqueue_convert_v16(const Problem& P, const Layout& L, const void* v, uint8_t* ws, cudaStream_t stream) {
+// Zeroes the words of the optional suffix that a forward starts from: the work-unit counter
+// and, with the fp16 copy of V, the word beside it that records a failed conversion.
+int clear_suffix_words(const Layout& L, uint8_t* ws, bool v16, cudaStream_t stream) {
+    cudaError_t e = v16 ? cudaMemsetAsync(ws + L.off_v16bad, 0, 2 * sizeof(int), stream)
+                        : cudaMemsetAsync(ws + L.off_counter, 0, sizeof(unsigned int), stream);
+    return e == cudaSuccess ? LCA_OK : fail_cuda(e, "workspace word reset");
+}
+
+// `clear`: zero the words first (else the caller has, earlier on the stream).
+int enqueue_convert_v16(const Problem& P, const Layout& L, const void* v, uint8_t* ws, cudaStream_t stream,
+                        bool clear = true) {
     lca::ConvertParams cv;
     memset(&cv, 0, sizeof(cv));
     const long long d = P.d, bh = P.bh;
@@ -486,9 +496,9 @@ int enqueue_convert_v16(const Problem& P, const Layout& L, const void* v, uint8_
         }
     }
     cv.any_bad = reinterpret_cast<int*>(ws + L.off_v16bad);
-    // clears the word and, next to it, the main kernel's work-unit counter
-    cudaError_t e = cudaMemsetAsync(cv.any_bad, 0, 2 * sizeof(int), stream);
-    if (e == cudaSuccess) e = lca::launch_convert_v16((int)P.d, cv, stream);
+    int st;
+    if (clear && (st = clear_suffix_words(L, ws, true, stream)) != LCA_OK) return st;
+    cudaError_t e = lca::launch_convert_v16((int)P.d, cv, stream);
     if (e != cudaSuccess) return fail_cuda(e, "fp16 V copy launch");
     return LCA_OK;
 }
@@ -631,7 +641,7 @@ int cached_maps(const Problem& P, const Layout& L, int dev, const void* q, const
 
 int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, const void* q, const void* k,
                  const void* v, void* out, float* lse, uint8_t* ws, cudaStream_t stream, bool v16 = false,
-                 bool dynamic_units = false) {
+                 bool dynamic_units = false, bool clear_counter = true) {
     const bool bf16 = P.dtype == LCA_DTYPE_BF16;
     const int n = (int)P.n;
     const int d = (int)P.d;
@@ -695,10 +705,8 @@ int enqueue_main(const Problem& P, const Layout& L, int dev, int* err_word, cons
     const int grid = (int)std::min<long long>(units, g_dev_sms[dev]);
     if (dynamic_units) {
         p.unit_counter = reinterpret_cast<unsigned int*>(ws + L.off_counter);
-        if (!v16) {  // (with the fp16 copy of V, the copy's memset cleared it)
-            cudaError_t me = cudaMemsetAsync(p.unit_counter, 0, sizeof(unsigned int), stream);
-            if (me != cudaSuccess) return fail_cuda(me, "unit counter reset");
-        }
+        // (with the fp16 copy of V, the copy's memset cleared it)
+        if (!v16 && clear_counter && (st = clear_suffix_words(L, ws, false, stream)) != LCA_OK) return st;
     }
     const bool timed = g_ev_before_main != nullptr && g_ev_after_main != nullptr;
     cudaError_t e;
@@ -1078,11 +1086,13 @@ int run_problem(const Problem& P, const void* q, const void* k, const void* v, v
     const bool fast = workspace != nullptr && workspace_bytes >= L.total_fast &&
                       reinterpret_cast<uintptr_t>(workspace) % 256 == 0;
     const bool v16 = fast && L.has_v16;
-    // 1. gather the global rows, (2. fp16 copy of V), 3. band + global-row units, 4. merge
-    //    the global-row splits
+    // 0. zero the suffix words, 1. gather the global rows, (2. fp16 copy of V), 3. band +
+    //    global-row units, 4. merge the global-row splits.  The words are cleared first so
+    //    that 1-4 are consecutive kernels, each launched to overlap the one before.
+    if (fast && (st = clear_suffix_words(L, ws, v16, stream)) != LCA_OK) return st;
     if ((st = enqueue_gather(P, L, q, k, v, ws, stream)) != LCA_OK) return st;
-    if (v16 && (st = enqueue_convert_v16(P, L, v, ws, stream)) != LCA_OK) return st;
-    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16, fast)) != LCA_OK) return st;
+    if (v16 && (st = enqueue_convert_v16(P, L, v, ws, stream, false)) != LCA_OK) return st;
+    if ((st = enqueue_main(P, L, dev, err_word, q, k, v, out, lse, ws, stream, v16, fast, false)) != LCA_OK) return st;
     return enqueue_combine_splits(P, L, out, lse, ws, stream);
 }
 

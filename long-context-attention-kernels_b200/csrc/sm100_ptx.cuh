@@ -56,6 +56,14 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Programmatic dependent launch.  griddep_wait blocks until the grids this one was
+// launched after (with the programmatic-serialisation attribute) have completed and their
+// memory is visible; without that attribute it returns at once.  griddep_launch lets the
+// next such grid start launching once every CTA of this one has called it (or exited).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

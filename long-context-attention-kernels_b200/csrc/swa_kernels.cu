@@ -61,6 +61,8 @@
 #include <cstdint>
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
+#include <utility>
 
 #include "sm100_ptx.cuh"
 #include "swa_kernels.h"
@@ -1122,6 +1124,8 @@ __device__ __forceinline__ void swa_main_body(const CUtensorMap& tm_q, const CUt
 // fp16 inputs (fp16 P), or bf16 inputs without the fp16 copy of V (bf16 P split into hi + lo)
 template <int D, bool BF16, bool EXT>
 __global__ void __launch_bounds__(Cfg<D, BF16, false>::kThreads, 1) lca_swa_main(LCA_MAIN_PARAMS) {
+    ptx::griddep_wait();  // the compact global rows and the unit counter are written before
+    ptx::griddep_launch();
     swa_main_body<D, BF16, false, EXT>(LCA_MAIN_ARGS);
 }
 
@@ -1133,6 +1137,8 @@ __global__ void __launch_bounds__(Cfg<D, true, true>::kThreads, 1) lca_swa_main_
     static_assert(Cfg<D, true, true>::kSmemBytes == Cfg<D, true, false>::kSmemBytes &&
                       Cfg<D, true, true>::kThreads == Cfg<D, true, false>::kThreads,
                   "both paths share one launch configuration");
+    ptx::griddep_wait();  // the fp16 copy, its word, the compact rows and the counter
+    ptx::griddep_launch();
     if (*reinterpret_cast<const volatile int*>(p.v16_bad) == 0)
         swa_main_body<D, true, true, EXT>(LCA_MAIN_ARGS);
     else
@@ -1147,6 +1153,7 @@ __global__ void __launch_bounds__(256) lca_gather_globals(const uint16_t* __rest
                                                           const uint16_t* __restrict__ v, GatherParams gp) {
     // one warp per (bh, compact row); 16-byte chunks
     constexpr int kChunks = D * 2 / 16;
+    ptx::griddep_launch();
     const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= (long long)gp.count * gp.bh) return;
@@ -1182,7 +1189,11 @@ __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
         if (blk < nb) break;
         blk -= nb;
     }
+    ptx::griddep_launch();
     if (si >= cp.n_segments) return;
+    // segment 0 is the caller's V, complete before this forward's first launch; the others
+    // (compact global rows, received halos) are written by the launch before this one
+    if (si > 0) ptx::griddep_wait();
     const ConvertSegment sg = cp.seg[si];
     const int per_plane = (sg.rows + 127) / 128;
     const int pl = (int)(blk / per_plane);
@@ -1236,6 +1247,7 @@ __global__ void __launch_bounds__(256) lca_convert_v16(ConvertParams cp) {
     if (threadIdx.x == 0) {
         float m = 0.f;
         for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, s_max[i]);
+        ptx::griddep_wait();  // the word is cleared before
         if (blk_bad || (blk_inexact && m < 0.0625f)) *cp.any_bad = 1;
     }
 }
@@ -1292,15 +1304,19 @@ __global__ void __launch_bounds__(256) lca_pack_halo(HaloPackParams hp) {
 // ------------------------------------------------------------------------ combine
 
 template <int D>
-__global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp) {
-    // One block per (bh, global row).  Each warp finds the largest log-sum-exp with its
-    // lanes spread over the partials, then sums a quarter of the partials (lane = kPer
-    // adjacent output columns, independent loads); the four warps' sums meet in shared
-    // memory.
-    constexpr int kWarps = 4;
-    constexpr int kPer = D / 32;
-    __shared__ float s_acc[kWarps][D];
-    __shared__ float s_w[kWarps];
+__global__ void __launch_bounds__(kCombineThreads) lca_combine_global_rows(CombineParams cp) {
+    // One block per (bh, global row).  The block's threads form groups of D / 4 lanes;
+    // group g reads partials g, g + kGroups, ... (lane = 4 adjacent output columns, one
+    // 16-byte load each), four of them in flight per thread, and folds them into its own
+    // running (max, sum, acc) with an online log-sum-exp.  The groups' results meet in
+    // shared memory.  The loads of a batch do not depend on one another, so a row's
+    // partials arrive in a few round trips to L2 however many splits there are.
+    constexpr int kLanes = D / 4;
+    constexpr int kGroups = kCombineThreads / kLanes;
+    constexpr int kBatch = 4;
+    __shared__ float4 s_acc[kGroups][kLanes];
+    __shared__ float s_m[kGroups], s_l[kGroups];
+    ptx::griddep_wait();  // the partials are written by the launch before this one
     const long long row = blockIdx.x;  // b * G + g
     if (row >= (long long)cp.num_global * cp.bh) {  // no global rows: only the epoch step below
         if (cp.epoch != nullptr && threadIdx.x == 0) {
@@ -1314,13 +1330,15 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
     }
     const int g = (int)(row % cp.num_global);
     const int bh = (int)(row / cp.num_global);
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
+    const int grp = (int)threadIdx.x / kLanes;
+    const int lane = (int)threadIdx.x % kLanes;
     if (cp.epoch != nullptr && ((*reinterpret_cast<volatile unsigned int*>(cp.epoch) + 1u) & 1u)) {
         cp.part_o += cp.parity_floats;
         cp.part_lse += cp.parity_floats;
     }
+    // a split past the end of the keys, or the odd half of a one-tile split, wrote nothing
     auto valid = [&](int part) {
+        if (part >= cp.n_parts) return false;
         if (cp.split_tiles == 0) return true;
         const int s = part >> 1;
         const int first_key = s * cp.split_tiles * 128;
@@ -1328,41 +1346,57 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
         if (tiles > cp.split_tiles) tiles = cp.split_tiles;
         return tiles > (part & 1);
     };
-    auto lse_of = [&](int part) {
-        return valid(part) ? __ldg(cp.part_lse + (size_t)part * cp.part_stride_lse + row) : -INFINITY;
-    };
-    float mx = -INFINITY;
-    for (int s = lane; s < cp.n_parts; s += 32) mx = fmaxf(mx, lse_of(s));
+    float m = -INFINITY, l = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int base = grp; base < cp.n_parts; base += kBatch * kGroups) {
+        float ls[kBatch];
+        float4 v[kBatch];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float acc[kPer];
+        for (int j = 0; j < kBatch; ++j) {
+            const int s = base + j * kGroups;
+            ls[j] = -INFINITY;
+            v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (valid(s)) {
+                ls[j] = __ldg(cp.part_lse + (size_t)s * cp.part_stride_lse + row);
+                v[j] = __ldg(reinterpret_cast<const float4*>(cp.part_o + (size_t)s * cp.part_stride_o + row * D) + lane);
+            }
+        }
 #pragma unroll
-    for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
-    float wsum = 0.f;
-#pragma unroll 4
-    for (int s = warp; s < cp.n_parts; s += kWarps) {
-        const float ls = lse_of(s);
-        if (ls == -INFINITY) continue;
-        const float wt = __expf(ls - mx);
-        const float* po = cp.part_o + (size_t)s * cp.part_stride_o + row * D + lane * kPer;
-        wsum += wt;
-        if constexpr (kPer == 2) {
-            const float2 v = __ldg(reinterpret_cast<const float2*>(po));
-            acc[0] += wt * v.x;
-            acc[1] += wt * v.y;
-        } else {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(po));
-            acc[0] += wt * v.x;
-            acc[1] += wt * v.y;
-            acc[2] += wt * v.z;
-            acc[3] += wt * v.w;
+        for (int j = 0; j < kBatch; ++j) {
+            if (ls[j] == -INFINITY) continue;
+            if (ls[j] > m) {
+                const float c = __expf(m - ls[j]);  // 0 while m is -inf (l and acc are 0)
+                l *= c;
+                acc.x *= c;
+                acc.y *= c;
+                acc.z *= c;
+                acc.w *= c;
+                m = ls[j];
+            }
+            const float wt = __expf(ls[j] - m);
+            l += wt;
+            acc.x += wt * v[j].x;
+            acc.y += wt * v[j].y;
+            acc.z += wt * v[j].z;
+            acc.w += wt * v[j].w;
         }
     }
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) s_acc[warp][lane * kPer + e] = acc[e];
-    if (lane == 0) s_w[warp] = wsum;
+    s_acc[grp][lane] = acc;
+    if (lane == 0) {
+        s_m[grp] = m;
+        s_l[grp] = l;
+    }
     __syncthreads();
-    const float wtot = (s_w[0] + s_w[1]) + (s_w[2] + s_w[3]);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) mx = fmaxf(mx, s_m[i]);
+    float wtot = 0.f;
+    float sc[kGroups];
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+        sc[i] = s_m[i] == -INFINITY ? 0.f : __expf(s_m[i] - mx);
+        wtot += sc[i] * s_l[i];
+    }
     const float inv = 1.f / wtot;
     const float lse = mx + __logf(wtot);
     float* out_row = nullptr;
@@ -1383,7 +1417,11 @@ __global__ void __launch_bounds__(128) lca_combine_global_rows(CombineParams cp)
     }
     if (out_row != nullptr) {
         for (int c = threadIdx.x; c < D; c += blockDim.x) {
-            const float val = ((s_acc[0][c] + s_acc[1][c]) + (s_acc[2][c] + s_acc[3][c])) * inv;
+            const float* col = reinterpret_cast<const float*>(&s_acc[0][0]) + c;
+            float a = 0.f;
+#pragma unroll
+            for (int i = 0; i < kGroups; ++i) a += sc[i] * col[i * D];
+            const float val = a * inv;
             if (out16 == kOut16BF16)
                 static_cast<__nv_bfloat16*>(cp.o)[out_idx + c] = __float2bfloat16_rn(val);
             else if (out16 == kOut16F16)
@@ -1441,6 +1479,35 @@ __global__ void __launch_bounds__(256) lca_peer_put(PeerPutParams pp) {
 
 // ------------------------------------------------------------------------ launchers
 
+// Launch with programmatic stream serialisation: the kernel may start while the previous
+// kernel of the stream is still running, and waits for it on the device (griddep_wait)
+// before it reads what that kernel writes.  The kernels launched this way are exactly the
+// ones that call griddep_wait first.  LCA_PDL=0 in the environment launches them in plain
+// stream order instead.
+static bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("LCA_PDL");
+        return !(e != nullptr && e[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_after_prev(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                                     cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <int D, bool BF16, bool V16, bool EXT>
 static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int grid, cudaStream_t stream) {
     auto kern = V16 ? lca_swa_main_v16<D, EXT> : lca_swa_main<D, BF16, EXT>;
@@ -1456,9 +1523,8 @@ static cudaError_t launch_main_t(const TensorMaps& tm, const MainParams& p, int 
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < kDevices) attr_set[dev] = true;
     }
-    kern<<<grid, Cfg<D, BF16, V16>::kThreads, smem, stream>>>(tm.q, tm.k, tm.v, tm.kh, tm.vh, tm.qg, tm.kg, tm.vg,
-                                                              tm.o, tm.po, tm.v16, tm.vg16, tm.vh16, p);
-    return cudaGetLastError();
+    return launch_after_prev(kern, (unsigned)grid, Cfg<D, BF16, V16>::kThreads, smem, stream, tm.q, tm.k, tm.v, tm.kh,
+                             tm.vh, tm.qg, tm.kg, tm.vg, tm.o, tm.po, tm.v16, tm.vg16, tm.vh16, p);
 }
 
 template <bool EXT>
@@ -1504,13 +1570,9 @@ cudaError_t launch_combine(int head_dim, const CombineParams& cp, cudaStream_t s
     if (rows <= 0 && cp.epoch == nullptr) return cudaSuccess;
     if (rows > INT_MAX) return cudaErrorInvalidValue;
     const unsigned grid = rows > 0 ? (unsigned)rows : 1u;  // one block for the epoch step alone
-    if (head_dim == 64)
-        lca_combine_global_rows<64><<<grid, 128, 0, stream>>>(cp);
-    else if (head_dim == 128)
-        lca_combine_global_rows<128><<<grid, 128, 0, stream>>>(cp);
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (head_dim == 64) return launch_after_prev(lca_combine_global_rows<64>, grid, kCombineThreads, 0, stream, cp);
+    if (head_dim == 128) return launch_after_prev(lca_combine_global_rows<128>, grid, kCombineThreads, 0, stream, cp);
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_convert_v16(int head_dim, const ConvertParams& cp, cudaStream_t stream) {
@@ -1518,13 +1580,9 @@ cudaError_t launch_convert_v16(int head_dim, const ConvertParams& cp, cudaStream
     for (int i = 0; i < cp.n_segments; ++i) blocks += (long long)cp.seg[i].planes * ((cp.seg[i].rows + 127) / 128);
     if (blocks <= 0) return cudaSuccess;
     if (blocks > INT_MAX) return cudaErrorInvalidValue;
-    if (head_dim == 64)
-        lca_convert_v16<64><<<(unsigned)blocks, 256, 0, stream>>>(cp);
-    else if (head_dim == 128)
-        lca_convert_v16<128><<<(unsigned)blocks, 256, 0, stream>>>(cp);
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (head_dim == 64) return launch_after_prev(lca_convert_v16<64>, (unsigned)blocks, 256, 0, stream, cp);
+    if (head_dim == 128) return launch_after_prev(lca_convert_v16<128>, (unsigned)blocks, 256, 0, stream, cp);
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_halo_pack(const HaloPackParams& hp, cudaStream_t stream) {

@@ -28,6 +28,7 @@ struct PeerSignals {
     unsigned int ticket;            // merge blocks done in the current step
 };
 constexpr int kGatherChunk = 1024;    // global indices passed per gather launch
+constexpr int kCombineThreads = 256;  // threads of one global-row merge block
 constexpr int kMaxHeadWindows = 256;  // heads with a radius of their own (kernel parameter space)
 constexpr int kMaxSegments = 512;     // packed sequences of one varlen call (kernel parameter space)
 
