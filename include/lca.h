@@ -52,7 +52,8 @@ enum {
     LCA_DEVERR_TIMEOUT_MMA = 2,      /* main kernel: an MMA issuer waited for data or P */
     LCA_DEVERR_TIMEOUT_SOFTMAX = 3,  /* main kernel: a softmax warp waited for S or O */
     LCA_DEVERR_TIMEOUT_DRAIN = 4,    /* main kernel: waiting for its own copies at exit */
-    LCA_DEVERR_TIMEOUT_PEER = 5      /* peer exchange: another rank's data did not arrive */
+    LCA_DEVERR_TIMEOUT_PEER = 5,     /* peer exchange: another rank's data did not arrive */
+    LCA_DEVERR_TIMEOUT_BACKWARD = 6  /* backward kernel: waited for a tile or an MMA */
 };
 
 /* Element types: Q, K, V share LCA_DTYPE_F16 or LCA_DTYPE_BF16; the output is fp32
@@ -333,6 +334,28 @@ LCA_API int lca_swa_shard_exchange_peer(const lca_shard_desc* desc, const int64_
 LCA_API int lca_swa_shard_finish_peer(const lca_shard_desc* desc, float* out, float* lse,
                                       const int64_t* global_tokens, int64_t num_global_tokens,
                                       void* const* peer_workspaces, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward pass (no counterpart in the reference, whose roadmap lists it first:
+ * README.md:113).  Gradients of the attention of lca_swa_forward with respect to Q, K and
+ * V, for the same q, k, v, dtype, shape, window_size, scale and global tokens:
+ *   o    : the forward's fp32 output  [batch][heads][seq_len][head_dim]
+ *   lse  : the forward's natural-log LSE  [batch][heads][seq_len]
+ *   dout : the gradient of the loss with respect to o (fp32, o's shape)
+ *   dq, dk, dv : fp32 outputs, q's shape (every element is written)
+ * P is recomputed from lse; dO, P and the score gradient enter the tensor-core products in
+ * the inputs' 16-bit type (fp32 accumulation).  Head-major layout, no causal / per-head
+ * radius / packed-sequence options.  The workspace (lca_swa_backward_workspace_size bytes,
+ * 256-byte aligned) is scratch: the call may overwrite all of it.
+ */
+LCA_API int lca_swa_backward_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                                            int64_t window_size, int64_t num_unique_global, int dtype,
+                                            size_t* out_bytes);
+LCA_API int lca_swa_backward(const void* q, const void* k, const void* v, const float* o, const float* lse,
+                             const float* dout, float* dq, float* dk, float* dv, int dtype, int64_t batch,
+                             int64_t heads, int64_t seq_len, int64_t head_dim, int64_t window_size, float scale,
+                             const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /*
  * Measurement hook (no counterpart in the reference): when both events are non-NULL,

@@ -30,8 +30,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CABI_SOURCES = ["swa_kernels.cu", "capi.cpp", "noalloc.cu"]
-CABI_HEADERS = ["sm100_ptx.cuh", "swa_kernels.h", "trace.cuh"]
+CABI_SOURCES = ["swa_kernels.cu", "swa_backward.cu", "capi.cpp", "noalloc.cu"]
+CABI_HEADERS = ["sm100_ptx.cuh", "swa_kernels.h", "swa_backward.h", "trace.cuh"]
 LIB_NAME = "liblca_b200.so"
 TRACE_LIB_NAME = "liblca_b200_trace.so"  # -DLCA_TRACE: in-kernel event trace (trace.cuh)
 EXT_NAME = "long_context_attention_kernels"

@@ -150,6 +150,58 @@ std::vector<torch::Tensor> sliding_window_attention_forward_ex(torch::Tensor Q, 
                         dilation, cu_seqlens, token_major);
 }
 
+// Gradients of the forward (include/lca.h lca_swa_backward): dQ, dK, dV in fp32, from the
+// forward's fp32 O and LSE and the fp32 gradient dO of O.  No counterpart in the reference.
+std::vector<torch::Tensor> sliding_window_attention_backward(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                                                             torch::Tensor O, torch::Tensor LSE, torch::Tensor dO,
+                                                             int64_t window_size,
+                                                             std::vector<int64_t> global_tokens, double scale) {
+    check_input(Q, "Q");
+    check_input(K, "K");
+    check_input(V, "V");
+    TORCH_CHECK(Q.dim() == 4, "Q must be [batch, heads, seq_len, head_dim]");
+    TORCH_CHECK(K.sizes() == Q.sizes() && V.sizes() == Q.sizes(), "Q, K and V must have the same shape");
+    TORCH_CHECK(K.scalar_type() == Q.scalar_type() && V.scalar_type() == Q.scalar_type(),
+                "Q, K and V must have the same dtype");
+    for (const torch::Tensor* t : {&O, &dO}) {
+        TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous() &&
+                        t->sizes() == Q.sizes(),
+                    "O and dO must be contiguous fp32 CUDA tensors of Q's shape");
+    }
+    const int64_t batch = Q.size(0), heads = Q.size(1), seq_len = Q.size(2), head_dim = Q.size(3);
+    TORCH_CHECK(LSE.is_cuda() && LSE.scalar_type() == torch::kFloat32 && LSE.is_contiguous() &&
+                    LSE.numel() == batch * heads * seq_len,
+                "LSE must be a contiguous fp32 CUDA tensor [batch, heads, seq_len]");
+    TORCH_CHECK(head_dim == 64 || head_dim == 128, "head_dim must be 64 or 128 (got ", head_dim, ")");
+    TORCH_CHECK(window_size >= 0, "window_size must be >= 0 (got ", window_size, ")");
+    c10::cuda::CUDAGuard guard(Q.device());
+    const int dtype = Q.scalar_type() == torch::kBFloat16 ? LCA_DTYPE_BF16 : LCA_DTYPE_F16;
+    std::vector<int32_t> norm(global_tokens.size() + 1);
+    int64_t G = 0;
+    raise_status(lca_normalize_global_tokens(global_tokens.data(), (int64_t)global_tokens.size(), seq_len, norm.data(),
+                                             &G),
+                 "global_tokens");
+    size_t ws_bytes = 0;
+    raise_status(lca_swa_backward_workspace_size(batch, heads, seq_len, head_dim, window_size, G, dtype, &ws_bytes),
+                 "backward workspace size");
+    torch::Tensor ws;
+    void* ws_ptr = nullptr;
+    if (ws_bytes > 0) {
+        ws = torch::empty({(int64_t)ws_bytes}, Q.options().dtype(torch::kUInt8));
+        ws_ptr = ws.data_ptr();
+    }
+    auto f32 = Q.options().dtype(torch::kFloat32);
+    auto dQ = torch::empty(Q.sizes(), f32), dK = torch::empty(Q.sizes(), f32), dV = torch::empty(Q.sizes(), f32);
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+    const int st = lca_swa_backward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr<float>(),
+                                    LSE.data_ptr<float>(), dO.data_ptr<float>(), dQ.data_ptr<float>(),
+                                    dK.data_ptr<float>(), dV.data_ptr<float>(), dtype, batch, heads, seq_len, head_dim,
+                                    window_size, static_cast<float>(scale), global_tokens.data(),
+                                    (int64_t)global_tokens.size(), ws_ptr, ws_bytes, static_cast<void*>(stream));
+    raise_status(st, "sliding_window_attention_backward");
+    return {dQ, dK, dV};
+}
+
 int device_error() {
     int code = 0;
     raise_status(lca_device_error(&code), "device_error");
@@ -175,6 +227,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("scale"), py::arg("out_dtype"), py::arg("causal"), py::arg("want_lse"),
           py::arg("head_windows") = std::vector<int64_t>{}, py::arg("dilation") = 1,
           py::arg("cu_seqlens") = std::vector<int64_t>{}, py::arg("token_major") = false);
+    m.def("sliding_window_attention_backward", &sliding_window_attention_backward,
+          "Gradients (dQ, dK, dV), fp32, of the forward from its O and LSE and the gradient dO of O",
+          py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("O"), py::arg("LSE"), py::arg("dO"),
+          py::arg("window_size"), py::arg("global_tokens"), py::arg("scale"));
     m.def("device_error", &device_error, "Read and clear the device-side error word (synchronises)");
     m.attr("abi_version") = lca_abi_version();
 }

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "swa_kernels.h"
+#include "swa_backward.h"
 
 namespace {
 
@@ -1438,6 +1439,233 @@ int lca_device_error(int* code) {
     e = cudaMemcpy(err_word, &zero, sizeof(int), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return fail_cuda(e, "clear error word");
     *code = val;
+    return LCA_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ backward pass
+
+namespace {
+
+// Workspace of the backward: the 16-bit dO, per-row stats, the global index list, the
+// compact global rows ([G][4 (q, k, v, dO16)][bh][d]) with their stats, and the split
+// partials of the global-row and global-key units.
+struct BwdLayout {
+    int n_tiles = 0, g_tiles = 0, split_tiles = 0, n_splits = 0;
+    size_t off_dout16 = 0, off_lse2 = 0, off_dvec = 0, off_gidx = 0, off_compact = 0, off_lse2g = 0, off_dg = 0;
+    size_t off_pq = 0, off_pk = 0, off_pv = 0, total = 0;
+};
+
+BwdLayout make_bwd_layout(const Problem& P) {
+    BwdLayout B;
+    const size_t bh = (size_t)P.bh, n = (size_t)P.n, d = (size_t)P.d, G = (size_t)P.G;
+    B.n_tiles = (int)((P.n + lca::kTileRows - 1) / lca::kTileRows);
+    if (G > 0) {
+        B.g_tiles = (int)((P.G + lca::kTileRows - 1) / lca::kTileRows);
+        // a split is about twice a band unit's inner tiles
+        const int64_t band_tiles = (2 * P.window + 2 * lca::kTileRows - 1) / lca::kTileRows + B.g_tiles;
+        B.split_tiles = (int)std::max<int64_t>(8, std::min<int64_t>(64, 2 * band_tiles));
+        B.n_splits = (B.n_tiles + B.split_tiles - 1) / B.split_tiles;
+    }
+    size_t off = 0;
+    auto take = [&](size_t& at, size_t bytes) {
+        at = off;
+        off = align_up(off + bytes, kAlign);
+    };
+    take(B.off_dout16, bh * n * d * 2);
+    take(B.off_lse2, bh * n * 4);
+    take(B.off_dvec, bh * n * 4);
+    if (G > 0) {
+        take(B.off_gidx, G * 4);
+        take(B.off_compact, G * 4 * bh * d * 2);
+        take(B.off_lse2g, bh * G * 4);
+        take(B.off_dg, bh * G * 4);
+        const size_t part = (size_t)B.n_splits * bh * G * d * 4;
+        take(B.off_pq, part);
+        take(B.off_pk, part);
+        take(B.off_pv, part);
+    }
+    B.total = off;
+    return B;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lca_swa_backward_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                                    int64_t window_size, int64_t num_unique_global, int dtype, size_t* out_bytes) {
+    g_last_error.clear();
+    if (out_bytes == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "out_bytes is NULL");
+    if (batch < 0 || heads < 0 || seq_len < 0 || num_unique_global < 0)
+        return fail(LCA_ERR_INVALID_ARGUMENT, "negative size");
+    int st = check_dtype_dim(dtype, head_dim);
+    if (st != LCA_OK) return st;
+    if (window_size < 0) return fail(LCA_ERR_INVALID_ARGUMENT, "window_size must be >= 0");
+    Problem P;
+    P.bh = batch * heads;
+    P.n_total = P.n = seq_len;
+    P.d = head_dim;
+    P.window = std::min(window_size, seq_len);
+    P.G = std::min(num_unique_global, seq_len);
+    P.dtype = dtype;
+    *out_bytes = make_bwd_layout(P).total;
+    return LCA_OK;
+}
+
+int lca_swa_backward(const void* q, const void* k, const void* v, const float* o, const float* lse,
+                     const float* dout, float* dq, float* dk, float* dv, int dtype, int64_t batch, int64_t heads,
+                     int64_t seq_len, int64_t head_dim, int64_t window_size, float scale,
+                     const int64_t* global_tokens, int64_t num_global_tokens, void* workspace,
+                     size_t workspace_bytes, void* stream_ptr) {
+    g_last_error.clear();
+    Problem P;
+    int st = parse_common(P, dtype, batch, heads, seq_len, head_dim, window_size, scale, global_tokens,
+                          num_global_tokens);
+    if (st != LCA_OK) return st;
+    if (P.bh == 0 || P.n == 0) return LCA_OK;
+    const void* ptrs[9] = {q, k, v, o, lse, dout, dq, dk, dv};
+    for (const void* x : ptrs)
+        if (x == nullptr) return fail(LCA_ERR_INVALID_ARGUMENT, "q, k, v, o, lse, dout, dq, dk and dv must be non-NULL");
+    for (int i = 0; i < 9; ++i)
+        if (i != 4 && !aligned16(ptrs[i]))
+            return fail(LCA_ERR_INVALID_ARGUMENT, "q, k, v, o, dout, dq, dk and dv must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(lse) & 3u) return fail(LCA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
+    if (P.bh * (int64_t)((P.n + lca::kTileRows - 1) / lca::kTileRows) > INT_MAX / 2)
+        return fail(LCA_ERR_UNSUPPORTED, "problem too large for the backward");
+    int dev = 0;
+    int* err_word = nullptr;
+    if ((st = check_device(&dev, &err_word)) != LCA_OK) return st;
+    const BwdLayout B = make_bwd_layout(P);
+    if (workspace_bytes < B.total)
+        return fail(LCA_ERR_WORKSPACE, "backward workspace needs %zu bytes, got %zu", B.total, workspace_bytes);
+    if (B.total > 0 && (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) % 256) != 0))
+        return fail(LCA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const bool bf16 = P.dtype == LCA_DTYPE_BF16;
+    const int d = (int)P.d;
+    const int G = (int)P.G;
+    int* gidx = G > 0 ? reinterpret_cast<int*>(ws + B.off_gidx) : nullptr;
+    cudaError_t e;
+
+    // 1. the sorted global indices
+    for (int first = 0; first < G; first += lca::kBwdIndexChunk) {
+        static thread_local lca::BwdIndexParams ip;
+        ip.dst = gidx + first;
+        ip.count = std::min(lca::kBwdIndexChunk, G - first);
+        for (int i = 0; i < ip.count; ++i) ip.idx[i] = P.gl[(size_t)first + i];
+        if ((e = lca::launch_bwd_indices(ip, stream)) != cudaSuccess) return fail_cuda(e, "backward index launch");
+    }
+    // 2. per-row preparation
+    lca::BwdPrepParams pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.q = q;
+    pp.k = k;
+    pp.v = v;
+    pp.o = o;
+    pp.dout = dout;
+    pp.lse = lse;
+    pp.dout16 = ws + B.off_dout16;
+    pp.lse2 = reinterpret_cast<float*>(ws + B.off_lse2);
+    pp.dvec = reinterpret_cast<float*>(ws + B.off_dvec);
+    if (G > 0) {
+        pp.compact = ws + B.off_compact;
+        pp.lse2g = reinterpret_cast<float*>(ws + B.off_lse2g);
+        pp.dg = reinterpret_cast<float*>(ws + B.off_dg);
+    }
+    pp.gidx = gidx;
+    pp.num_global = G;
+    pp.n = (int)P.n;
+    pp.bh = (int)P.bh;
+    pp.bf16 = bf16 ? 1 : 0;
+    if ((e = lca::launch_bwd_prep(d, pp, stream)) != cudaSuccess) return fail_cuda(e, "backward prep launch");
+
+    // 3. tensor maps: the inputs, the 16-bit dO and the compact planes
+    const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap mq, mk, mv, mdo, mqg, mkg, mvg, mdog;
+    const uint64_t rows = (uint64_t)P.n, planes = (uint64_t)P.bh;
+    if ((st = encode_3d(&mq, dt, 2, q, d, rows, planes, 64, "q")) != LCA_OK) return st;
+    if ((st = encode_3d(&mk, dt, 2, k, d, rows, planes, 64, "k")) != LCA_OK) return st;
+    if ((st = encode_3d(&mv, dt, 2, v, d, rows, planes, 64, "v")) != LCA_OK) return st;
+    if ((st = encode_3d(&mdo, dt, 2, ws + B.off_dout16, d, rows, planes, 64, "dout16")) != LCA_OK) return st;
+    if (G > 0) {
+        const uint8_t* cb = ws + B.off_compact;
+        const size_t plane_bytes = (size_t)P.bh * d * 2;
+        if ((st = encode_compact(&mqg, dt, cb, d, planes, G, "q global rows", 4)) != LCA_OK) return st;
+        if ((st = encode_compact(&mkg, dt, cb + plane_bytes, d, planes, G, "k global rows", 4)) != LCA_OK) return st;
+        if ((st = encode_compact(&mvg, dt, cb + 2 * plane_bytes, d, planes, G, "v global rows", 4)) != LCA_OK)
+            return st;
+        if ((st = encode_compact(&mdog, dt, cb + 3 * plane_bytes, d, planes, G, "dout16 global rows", 4)) != LCA_OK)
+            return st;
+    } else {  // never loaded without global tokens
+        mqg = mq;
+        mkg = mk;
+        mvg = mv;
+        mdog = mdo;
+    }
+
+    // 4. the dQ kernel and the dK / dV kernel
+    lca::BwdParams bp;
+    memset(&bp, 0, sizeof(bp));
+    bp.n = (int)P.n;
+    bp.bh = (int)P.bh;
+    bp.window = (int)P.window;
+    bp.num_global = G;
+    bp.g_tiles = B.g_tiles;
+    bp.n_tiles = B.n_tiles;
+    bp.split_tiles = B.split_tiles;
+    bp.n_splits = B.n_splits;
+    bp.n_band_units = (int)(P.bh * B.n_tiles);
+    const long long units = (long long)bp.n_band_units + (long long)P.bh * B.g_tiles * B.n_splits;
+    if (units > INT_MAX) return fail(LCA_ERR_UNSUPPORTED, "problem too large (%lld backward units)", units);
+    bp.n_units = (int)units;
+    bp.scale = scale;
+    bp.scale_log2 = scale * 1.4426950408889634f;
+    bp.gidx = gidx;
+    bp.lse2 = pp.lse2;
+    bp.dvec = pp.dvec;
+    bp.lse2g = pp.lse2g;
+    bp.dg = pp.dg;
+    bp.err = err_word;
+    bp.timeout_ns = wait_timeout_ns();
+    float* pq = G > 0 ? reinterpret_cast<float*>(ws + B.off_pq) : nullptr;
+    float* pk = G > 0 ? reinterpret_cast<float*>(ws + B.off_pk) : nullptr;
+    float* pv = G > 0 ? reinterpret_cast<float*>(ws + B.off_pv) : nullptr;
+
+    lca::BwdMaps mqk{mq, mdo, mk, mv, mqg, mdog, mkg, mvg};  // outer (Q, dO16), inner (K, V)
+    lca::BwdParams bq = bp;
+    bq.out_a = dq;
+    bq.part_a = pq;
+    if ((e = lca::launch_bwd_main(d, bf16, false, mqk, bq, stream)) != cudaSuccess)
+        return fail_cuda(e, "backward dQ kernel launch");
+    lca::BwdMaps mkv{mk, mv, mq, mdo, mkg, mvg, mqg, mdog};  // outer (K, V), inner (Q, dO16)
+    lca::BwdParams bk = bp;
+    bk.out_a = dv;
+    bk.out_b = dk;
+    bk.part_a = pv;
+    bk.part_b = pk;
+    if ((e = lca::launch_bwd_main(d, bf16, true, mkv, bk, stream)) != cudaSuccess)
+        return fail_cuda(e, "backward dK/dV kernel launch");
+
+    // 5. the global tokens' rows
+    if (G > 0) {
+        lca::BwdReduceParams rp;
+        memset(&rp, 0, sizeof(rp));
+        rp.part_q = pq;
+        rp.part_k = pk;
+        rp.part_v = pv;
+        rp.dq = dq;
+        rp.dk = dk;
+        rp.dv = dv;
+        rp.gidx = gidx;
+        rp.splits_q = rp.splits_k = B.n_splits;
+        rp.num_global = G;
+        rp.n = (int)P.n;
+        rp.bh = (int)P.bh;
+        if ((e = lca::launch_bwd_reduce(d, rp, stream)) != cudaSuccess) return fail_cuda(e, "backward reduce launch");
+    }
     return LCA_OK;
 }
 

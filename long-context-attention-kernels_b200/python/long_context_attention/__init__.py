@@ -20,7 +20,8 @@ import torch
 
 from ._native import extension, native_error
 
-__all__ = ["sliding_window_attention", "sliding_window_attention_with_lse", "sliding_window_attention_varlen"]
+__all__ = ["sliding_window_attention", "sliding_window_attention_with_lse", "sliding_window_attention_varlen",
+           "sliding_window_attention_backward"]
 
 
 def _reference_sliding_window_attention(
@@ -162,11 +163,64 @@ def sliding_window_attention(
             out = out.transpose(1, 2).contiguous()
         return out if out_dtype in (None, torch.float32) else out.to(out_dtype)
     scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale, tm)
-    if out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1 and not tm:
+    base = out_dtype in (None, torch.float32) and not causal and not radii and dilation == 1 and not tm
+    if torch.is_grad_enabled() and (Q.requires_grad or K.requires_grad or V.requires_grad):
+        if not base:
+            raise NotImplementedError(
+                "long_context_attention: the backward covers fp32 output, one radius, no causal mask, no "
+                "dilation and the [batch, heads, seq_len, head_dim] layout")
+        return _SlidingWindowAttentionFn.apply(Q, K, V, window_size, tokens, scale)
+    if base:
         return extension().sliding_window_attention_forward_list(Q, K, V, window_size, tokens, scale)
     return extension().sliding_window_attention_forward_ex(Q, K, V, window_size, tokens, scale,
                                                            out_dtype or torch.float32, bool(causal), False,
                                                            radii, int(dilation), [], tm)[0]
+
+
+class _SlidingWindowAttentionFn(torch.autograd.Function):
+    """Forward through the sm_100a kernels keeping O and LSE; backward through
+    lca_swa_backward (gradients computed in fp32, returned in the inputs' types)."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, window_size, tokens, scale):
+        out, lse = extension().sliding_window_attention_forward_lse(Q, K, V, window_size, tokens, scale)
+        ctx.save_for_backward(Q, K, V, out, lse)
+        ctx.args = (window_size, tokens, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, out, lse = ctx.saved_tensors
+        window_size, tokens, scale = ctx.args
+        dq, dk, dv = extension().sliding_window_attention_backward(
+            Q, K, V, out, lse, dO.to(torch.float32).contiguous(), window_size, tokens, scale)
+        return dq.to(Q.dtype), dk.to(K.dtype), dv.to(V.dtype), None, None, None
+
+
+def sliding_window_attention_backward(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    O: torch.Tensor,
+    LSE: torch.Tensor,
+    dO: torch.Tensor,
+    window_size: int,
+    global_tokens: Sequence[int] = (),
+    scale: float | None = None,
+):
+    """Gradients ``(dQ, dK, dV)`` (fp32, Q's shape) of the attention with respect to Q, K, V.
+
+    O and LSE are what :func:`sliding_window_attention_with_lse` returned for the same
+    arguments, dO the gradient of the loss with respect to O.  No counterpart in the
+    reference (its roadmap's first open item, README.md:113).  ``sliding_window_attention``
+    calls this through autograd when Q, K or V requires grad.
+    """
+    scale, window_size, tokens, radii = _prepare(Q, window_size, global_tokens, scale)
+    if radii:
+        raise NotImplementedError("long_context_attention: the backward takes one radius")
+    dq, dk, dv = extension().sliding_window_attention_backward(Q, K, V, O, LSE, dO.to(torch.float32).contiguous(),
+                                                               window_size, tokens, scale)
+    return dq, dk, dv
 
 
 def sliding_window_attention_with_lse(
@@ -235,6 +289,7 @@ DEVICE_ERRORS = {
     3: "main kernel: a softmax warp waited too long for S or O",
     4: "main kernel: waiting for its own copies at exit took too long",
     5: "peer exchange: another rank's halos, global rows or row partials did not arrive in time",
+    6: "backward kernel: waited too long for a tile or an MMA",
 }
 
 

@@ -113,6 +113,11 @@ class CABI:
         lib.lca_swa_forward_noalloc.restype = ctypes.c_int
         lib.lca_swa_forward_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64,
                                                 ctypes.c_float, ctypes.POINTER(i64), i64, vp]
+        lib.lca_swa_backward_workspace_size.restype = ctypes.c_int
+        lib.lca_swa_backward_workspace_size.argtypes = [i64, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.POINTER(sz)]
+        lib.lca_swa_backward.restype = ctypes.c_int
+        lib.lca_swa_backward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, i64, i64,
+                                         ctypes.c_float, ctypes.POINTER(i64), i64, vp, sz, vp]
         dp, lp = ctypes.POINTER(ShardDesc), ctypes.POINTER(ShardLayout)
         lib.lca_swa_shard_layout.restype = ctypes.c_int
         lib.lca_swa_shard_layout.argtypes = [dp, i64, lp]
@@ -180,6 +185,20 @@ class CABI:
         arr = (ctypes.c_int64 * max(n, 1))(*tokens)
         return self.lib.lca_swa_forward_noalloc(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dtype, batch, heads, seq_len,
                                                 head_dim, window, ctypes.c_float(scale), arr, n, stream_ptr)
+
+    def backward_workspace_size(self, batch, heads, seq_len, head_dim, window, num_unique_global,
+                                dtype) -> tuple[int, int]:
+        out = ctypes.c_size_t(0)
+        st = self.lib.lca_swa_backward_workspace_size(batch, heads, seq_len, head_dim, window, num_unique_global,
+                                                      dtype, ctypes.byref(out))
+        return st, out.value
+
+    def backward(self, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dout_ptr, dq_ptr, dk_ptr, dv_ptr, dtype, batch, heads,
+                 seq_len, head_dim, window, scale, tokens, ws_ptr, ws_bytes, stream_ptr) -> int:
+        arr, n = self._tokens(tokens)
+        return self.lib.lca_swa_backward(q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, dout_ptr, dq_ptr, dk_ptr, dv_ptr, dtype,
+                                         batch, heads, seq_len, head_dim, window, ctypes.c_float(scale), arr, n,
+                                         ws_ptr, ws_bytes, stream_ptr)
 
     @staticmethod
     def _tokens(tokens):

@@ -121,3 +121,41 @@ def sliding_window_attention_varlen(Q, K, V, cu_seqlens: Sequence[int], window_s
                                         dtype=dtype, causal=causal)
         out[:, :, a:b], lse[:, :, a:b] = o, l
     return out, lse
+
+
+def sliding_window_attention_backward(Q, K, V, dO, window_size: int, global_tokens: Sequence[int], scale: float,
+                                      dtype=np.float64, block_rows: int = 256):
+    """Gradients (dQ, dK, dV) of sum(O * dO) for O = :func:`sliding_window_attention`.
+
+    The reference is forward only (its roadmap lists the backward first, README.md:113);
+    this restates the gradient of its dense-mask definition
+    (python/long_context_attention/__init__.py:24-53): with P the row softmax over visible
+    keys, D_i = sum_c dO[i][c] O[i][c], dP = dO V^T, dS = P (dP - D) on visible pairs,
+    dQ = scale dS K, dK = scale dS^T Q, dV = P^T dO.  Row-blocked like the forward; all
+    arrays [B, H, n, d], results in `dtype`.
+    """
+    Q, K, V, dO = (np.asarray(x) for x in (Q, K, V, dO))
+    B, H, n, d = Q.shape
+    g = normalize_global_tokens(global_tokens, n)
+    dQ = np.zeros((B, H, n, d), dtype=dtype)
+    dK = np.zeros((B, H, n, d), dtype=dtype)
+    dV = np.zeros((B, H, n, d), dtype=dtype)
+    for b in range(B):
+        for h in range(H):
+            k = K[b, h].astype(dtype, copy=False)
+            v = V[b, h].astype(dtype, copy=False)
+            for s in range(0, n, block_rows):
+                r = np.arange(s, min(n, s + block_rows), dtype=np.int64)
+                q = Q[b, h, r].astype(dtype, copy=False)
+                do = dO[b, h, r].astype(dtype, copy=False)
+                scores = np.where(visible_rows(r, n, int(window_size), g), (q @ k.T) * dtype(scale), -np.inf)
+                m = scores.max(axis=1, keepdims=True)
+                p = np.exp(scores - m)
+                p /= p.sum(axis=1, keepdims=True)
+                o = p @ v
+                dvec = (do * o).sum(axis=1, keepdims=True)
+                ds = p * (do @ v.T - dvec)
+                dQ[b, h, r] = dtype(scale) * (ds @ k)
+                dK[b, h] += dtype(scale) * (ds.T @ q)
+                dV[b, h] += p.T @ do
+    return dQ, dK, dV

@@ -120,3 +120,35 @@ def test_varlen_and_dilated_validation_before_device_work():
                                                 ctypes.byref(size)) == c.OK
     base = c.workspace_size(1, 2, 96, 64, 8, 0, c.DTYPE_BF16)[1]
     assert size.value >= base + 3 * 2 * 96 * 64 * 2 + 2 * 96 * 64 * 4
+
+
+def _bwd(c, **kw):
+    args = dict(q_ptr=None, k_ptr=None, v_ptr=None, o_ptr=None, lse_ptr=None, dout_ptr=None, dq_ptr=None,
+                dk_ptr=None, dv_ptr=None, dtype=c.DTYPE_BF16, batch=1, heads=1, seq_len=128, head_dim=64, window=4,
+                scale=0.125, tokens=[], ws_ptr=None, ws_bytes=0, stream_ptr=None)
+    args.update(kw)
+    return c.backward(**args)
+
+
+def test_backward_validation_before_device_work():
+    c = _native.cabi()
+    assert _bwd(c, dtype=7) == c.ERR_UNSUPPORTED
+    assert _bwd(c, head_dim=96) == c.ERR_UNSUPPORTED
+    assert _bwd(c, window=-1) == c.ERR_INVALID_ARGUMENT
+    assert _bwd(c, tokens=[128]) == c.ERR_INDEX
+    assert _bwd(c, batch=0) == c.OK
+    assert _bwd(c, seq_len=0) == c.OK
+    assert _bwd(c) == c.ERR_INVALID_ARGUMENT
+    assert "non-NULL" in c.last_error()
+
+
+def test_backward_workspace_size():
+    c = _native.cabi()
+    st, none = c.backward_workspace_size(1, 2, 1000, 64, 16, 0, c.DTYPE_BF16)
+    assert st == c.OK
+    # at least the 16-bit dO and the two per-row statistics
+    assert none >= 2 * 1000 * 64 * 2 + 2 * 2 * 1000 * 4
+    st, some = c.backward_workspace_size(1, 2, 1000, 64, 16, 3, c.DTYPE_BF16)
+    assert st == c.OK and some > none  # compact global rows and split partials
+    assert c.backward_workspace_size(1, 2, 1000, 96, 16, 3, c.DTYPE_BF16)[0] == c.ERR_UNSUPPORTED
+    assert c.backward_workspace_size(1, 2, 1000, 64, -1, 3, c.DTYPE_BF16)[0] == c.ERR_INVALID_ARGUMENT

@@ -125,3 +125,42 @@ def test_dilated_and_varlen_oracle():
         want, want_lse = swa_oracle.sliding_window_attention(q[:, :, a:b].numpy(), k[:, :, a:b].numpy(),
                                                              v[:, :, a:b].numpy(), 4, [0, -1], 0.4)
         assert np.array_equal(got[:, :, a:b], want) and np.array_equal(lse[:, :, a:b], want_lse)
+
+
+@pytest.mark.parametrize("B,H,n,d,w,g", [(1, 2, 37, 8, 3, [0, 5, -1]), (2, 1, 64, 16, 0, []),
+                                         (1, 1, 50, 4, 100, [7, 7]), (1, 2, 130, 8, 9, [129, 0, 64])])
+def test_backward_oracle_matches_autograd_of_the_reference_definition(B, H, n, d, w, g):
+    """The oracle's backward is pinned to torch autograd through the reference's own dense
+    definition (python/long_context_attention/__init__.py:24-53, restated under the same
+    name in this package), which computes in fp32."""
+    import long_context_attention as lca
+    gen = torch.Generator().manual_seed(n * 31 + d)
+    Q, K, V, dO = (torch.randn(B, H, n, d, generator=gen, dtype=torch.float64) for _ in range(4))
+    Qr, Kr, Vr = (x.clone().requires_grad_() for x in (Q, K, V))
+    out = lca._reference_sliding_window_attention(Qr, Kr, Vr, w, g, 0.3)
+    want = torch.autograd.grad((out * dO).sum(), (Qr, Kr, Vr))
+    got = swa_oracle.sliding_window_attention_backward(Q.numpy(), K.numpy(), V.numpy(), dO.numpy(), w, g, 0.3,
+                                                       block_rows=16)
+    for a, b in zip(got, want):
+        assert max_abs(a, b.numpy()) < 2e-6
+
+
+def test_backward_oracle_matches_finite_differences():
+    """fp64 central differences of sum(O * dO) against the oracle's gradient."""
+    rng = np.random.default_rng(5)
+    B, H, n, d, w, g, scale = 1, 1, 12, 3, 2, [4], 0.7
+    Q, K, V, dO = (rng.standard_normal((B, H, n, d)) for _ in range(4))
+    dq, dk, dv = swa_oracle.sliding_window_attention_backward(Q, K, V, dO, w, g, scale)
+
+    def loss(q, k, v):
+        return float((swa_oracle.sliding_window_attention(q, k, v, w, g, scale)[0] * dO).sum())
+
+    eps = 1e-6
+    for which, grad in ((0, dq), (1, dk), (2, dv)):
+        for idx in [(0, 0, 0, 0), (0, 0, 4, 1), (0, 0, 11, 2), (0, 0, 7, 0)]:
+            args = [Q.copy(), K.copy(), V.copy()]
+            args[which][idx] += eps
+            up = loss(*args)
+            args[which][idx] -= 2 * eps
+            down = loss(*args)
+            assert abs((up - down) / (2 * eps) - grad[idx]) < 1e-6
