@@ -339,12 +339,12 @@ Layout make_layout(const Problem& P) {
 
 int encode_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t d, uint64_t rows,
               uint64_t planes, uint32_t box_x, const char* name,
-              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B, uint32_t box_rows = lca::kTileRows) {
     EncodeTiledFn enc = get_encode_fn();
     if (enc == nullptr) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
     cuuint64_t dims[3] = {d, rows, planes};
     cuuint64_t strides[2] = {d * (uint64_t)esize, d * rows * (uint64_t)esize};
-    cuuint32_t box[3] = {box_x, (cuuint32_t)lca::kTileRows, 1};
+    cuuint32_t box[3] = {box_x, box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -374,12 +374,12 @@ int encode_tok(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* ba
 // whole compact row, box 64 columns x 1 head x 128 rows (lands in shared memory exactly
 // like a 64 x 128 box of a [bh][n][d] tensor).
 int encode_compact(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d, uint64_t bh, uint64_t G,
-                   const char* name, uint64_t planes_per_row = 3) {
+                   const char* name, uint64_t planes_per_row = 3, uint32_t box_rows = lca::kTileRows) {
     EncodeTiledFn enc = get_encode_fn();
     if (enc == nullptr) return fail(LCA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
     cuuint64_t dims[3] = {d, bh, G};
     cuuint64_t strides[2] = {d * 2, planes_per_row * bh * d * 2};
-    cuuint32_t box[3] = {64, 1, (cuuint32_t)lca::kTileRows};
+    cuuint32_t box[3] = {64, 1, box_rows};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1451,9 +1451,13 @@ namespace {
 // Workspace of the backward: the 16-bit dO, per-row stats, the global index list, the
 // compact global rows ([G][4 (q, k, v, dO16)][bh][d]) with their stats, and the split
 // partials of the global-row and global-key units.
+constexpr int kBwdInnerRows = 64;  // rows of an inner tile of the backward kernels
+
 struct BwdLayout {
-    int n_tiles = 0, g_tiles = 0, split_tiles = 0, n_splits = 0;
-    size_t off_dout16 = 0, off_lse2 = 0, off_dvec = 0, off_gidx = 0, off_compact = 0, off_lse2g = 0, off_dg = 0;
+    int n_tiles = 0, g_tiles = 0, gi_tiles = 0, split_tiles = 0, n_splits = 0;
+    size_t off_dout16 = 0, off_lse2 = 0, off_dvec = 0, off_gidx = 0, off_bitmap = 0, off_compact = 0, off_lse2g = 0,
+           off_dg = 0;
+    int bitmap_words = 0;
     size_t off_pq = 0, off_pk = 0, off_pv = 0, total = 0;
 };
 
@@ -1463,10 +1467,12 @@ BwdLayout make_bwd_layout(const Problem& P) {
     B.n_tiles = (int)((P.n + lca::kTileRows - 1) / lca::kTileRows);
     if (G > 0) {
         B.g_tiles = (int)((P.G + lca::kTileRows - 1) / lca::kTileRows);
+        B.gi_tiles = (int)((P.G + kBwdInnerRows - 1) / kBwdInnerRows);
         // a split is about twice a band unit's inner tiles
-        const int64_t band_tiles = (2 * P.window + 2 * lca::kTileRows - 1) / lca::kTileRows + B.g_tiles;
-        B.split_tiles = (int)std::max<int64_t>(8, std::min<int64_t>(64, 2 * band_tiles));
-        B.n_splits = (B.n_tiles + B.split_tiles - 1) / B.split_tiles;
+        const int64_t band_tiles = (2 * P.window + lca::kTileRows + 2 * kBwdInnerRows - 1) / kBwdInnerRows + B.gi_tiles;
+        B.split_tiles = (int)std::max<int64_t>(16, std::min<int64_t>(128, 2 * band_tiles));
+        const int64_t inner_tiles = (P.n + kBwdInnerRows - 1) / kBwdInnerRows;
+        B.n_splits = (int)((inner_tiles + B.split_tiles - 1) / B.split_tiles);
     }
     size_t off = 0;
     auto take = [&](size_t& at, size_t bytes) {
@@ -1478,6 +1484,8 @@ BwdLayout make_bwd_layout(const Problem& P) {
     take(B.off_dvec, bh * n * 4);
     if (G > 0) {
         take(B.off_gidx, G * 4);
+        B.bitmap_words = (int)((n + 31) / 32 + 3);
+        take(B.off_bitmap, (size_t)B.bitmap_words * 4);
         take(B.off_compact, G * 4 * bh * d * 2);
         take(B.off_lse2g, bh * G * 4);
         take(B.off_dg, bh * G * 4);
@@ -1554,6 +1562,9 @@ int lca_swa_backward(const void* q, const void* k, const void* v, const float* o
     for (int first = 0; first < G; first += lca::kBwdIndexChunk) {
         static thread_local lca::BwdIndexParams ip;
         ip.dst = gidx + first;
+        ip.bitmap = reinterpret_cast<uint32_t*>(ws + B.off_bitmap);
+        ip.bitmap_words = B.bitmap_words;
+        ip.clear_bitmap = first == 0 ? 1 : 0;
         ip.count = std::min(lca::kBwdIndexChunk, G - first);
         for (int i = 0; i < ip.count; ++i) ip.idx[i] = P.gl[(size_t)first + i];
         if ((e = lca::launch_bwd_indices(ip, stream)) != cudaSuccess) return fail_cuda(e, "backward index launch");
@@ -1576,6 +1587,7 @@ int lca_swa_backward(const void* q, const void* k, const void* v, const float* o
         pp.dg = reinterpret_cast<float*>(ws + B.off_dg);
     }
     pp.gidx = gidx;
+    pp.gbitmap = G > 0 ? reinterpret_cast<const uint32_t*>(ws + B.off_bitmap) : nullptr;
     pp.num_global = G;
     pp.n = (int)P.n;
     pp.bh = (int)P.bh;
@@ -1584,26 +1596,32 @@ int lca_swa_backward(const void* q, const void* k, const void* v, const float* o
 
     // 3. tensor maps: the inputs, the 16-bit dO and the compact planes
     const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap mq, mk, mv, mdo, mqg, mkg, mvg, mdog;
+    // [0] outer tiles (128-row boxes), [1] inner tiles (64-row boxes)
+    CUtensorMap mq[2], mk[2], mv[2], mdo[2], mqg[2], mkg[2], mvg[2], mdog[2];
     const uint64_t rows = (uint64_t)P.n, planes = (uint64_t)P.bh;
-    if ((st = encode_3d(&mq, dt, 2, q, d, rows, planes, 64, "q")) != LCA_OK) return st;
-    if ((st = encode_3d(&mk, dt, 2, k, d, rows, planes, 64, "k")) != LCA_OK) return st;
-    if ((st = encode_3d(&mv, dt, 2, v, d, rows, planes, 64, "v")) != LCA_OK) return st;
-    if ((st = encode_3d(&mdo, dt, 2, ws + B.off_dout16, d, rows, planes, 64, "dout16")) != LCA_OK) return st;
-    if (G > 0) {
-        const uint8_t* cb = ws + B.off_compact;
-        const size_t plane_bytes = (size_t)P.bh * d * 2;
-        if ((st = encode_compact(&mqg, dt, cb, d, planes, G, "q global rows", 4)) != LCA_OK) return st;
-        if ((st = encode_compact(&mkg, dt, cb + plane_bytes, d, planes, G, "k global rows", 4)) != LCA_OK) return st;
-        if ((st = encode_compact(&mvg, dt, cb + 2 * plane_bytes, d, planes, G, "v global rows", 4)) != LCA_OK)
-            return st;
-        if ((st = encode_compact(&mdog, dt, cb + 3 * plane_bytes, d, planes, G, "dout16 global rows", 4)) != LCA_OK)
-            return st;
-    } else {  // never loaded without global tokens
-        mqg = mq;
-        mkg = mk;
-        mvg = mv;
-        mdog = mdo;
+    const void* dout16 = ws + B.off_dout16;
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t br = i == 0 ? lca::kTileRows : kBwdInnerRows;
+        const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+        if ((st = encode_3d(&mq[i], dt, 2, q, d, rows, planes, 64, "q", sw, br)) != LCA_OK) return st;
+        if ((st = encode_3d(&mk[i], dt, 2, k, d, rows, planes, 64, "k", sw, br)) != LCA_OK) return st;
+        if ((st = encode_3d(&mv[i], dt, 2, v, d, rows, planes, 64, "v", sw, br)) != LCA_OK) return st;
+        if ((st = encode_3d(&mdo[i], dt, 2, dout16, d, rows, planes, 64, "dout16", sw, br)) != LCA_OK) return st;
+        if (G > 0) {
+            const uint8_t* cb = ws + B.off_compact;
+            const size_t pb = (size_t)P.bh * d * 2;
+            if ((st = encode_compact(&mqg[i], dt, cb, d, planes, G, "q global rows", 4, br)) != LCA_OK) return st;
+            if ((st = encode_compact(&mkg[i], dt, cb + pb, d, planes, G, "k global rows", 4, br)) != LCA_OK) return st;
+            if ((st = encode_compact(&mvg[i], dt, cb + 2 * pb, d, planes, G, "v global rows", 4, br)) != LCA_OK)
+                return st;
+            if ((st = encode_compact(&mdog[i], dt, cb + 3 * pb, d, planes, G, "dout16 global rows", 4, br)) != LCA_OK)
+                return st;
+        } else {  // never loaded without global tokens
+            mqg[i] = mq[i];
+            mkg[i] = mk[i];
+            mvg[i] = mv[i];
+            mdog[i] = mdo[i];
+        }
     }
 
     // 4. the dQ kernel and the dK / dV kernel
@@ -1614,6 +1632,7 @@ int lca_swa_backward(const void* q, const void* k, const void* v, const float* o
     bp.window = (int)P.window;
     bp.num_global = G;
     bp.g_tiles = B.g_tiles;
+    bp.gi_tiles = B.gi_tiles;
     bp.n_tiles = B.n_tiles;
     bp.split_tiles = B.split_tiles;
     bp.n_splits = B.n_splits;
@@ -1624,6 +1643,7 @@ int lca_swa_backward(const void* q, const void* k, const void* v, const float* o
     bp.scale = scale;
     bp.scale_log2 = scale * 1.4426950408889634f;
     bp.gidx = gidx;
+    bp.gbitmap = G > 0 ? reinterpret_cast<const uint32_t*>(ws + B.off_bitmap) : nullptr;
     bp.lse2 = pp.lse2;
     bp.dvec = pp.dvec;
     bp.lse2g = pp.lse2g;
@@ -1634,13 +1654,13 @@ int lca_swa_backward(const void* q, const void* k, const void* v, const float* o
     float* pk = G > 0 ? reinterpret_cast<float*>(ws + B.off_pk) : nullptr;
     float* pv = G > 0 ? reinterpret_cast<float*>(ws + B.off_pv) : nullptr;
 
-    lca::BwdMaps mqk{mq, mdo, mk, mv, mqg, mdog, mkg, mvg};  // outer (Q, dO16), inner (K, V)
+    lca::BwdMaps mqk{mq[0], mdo[0], mk[1], mv[1], mqg[0], mdog[0], mkg[1], mvg[1]};  // outer (Q, dO16), inner (K, V)
     lca::BwdParams bq = bp;
     bq.out_a = dq;
     bq.part_a = pq;
     if ((e = lca::launch_bwd_main(d, bf16, false, mqk, bq, stream)) != cudaSuccess)
         return fail_cuda(e, "backward dQ kernel launch");
-    lca::BwdMaps mkv{mk, mv, mq, mdo, mkg, mvg, mqg, mdog};  // outer (K, V), inner (Q, dO16)
+    lca::BwdMaps mkv{mk[0], mv[0], mq[1], mdo[1], mkg[0], mvg[0], mqg[1], mdog[1]};  // outer (K, V), inner (Q, dO16)
     lca::BwdParams bk = bp;
     bk.out_a = dv;
     bk.out_b = dk;

@@ -44,21 +44,25 @@
 namespace lca {
 namespace {
 
-constexpr int kBM = 128;                 // rows of a tile (outer and inner)
-constexpr int kBwdThreads = 128;         // one warpgroup
-constexpr int kBwdPanel = 128 * 128;     // one 128-row x 128-byte swizzle panel
+constexpr int kBM = 128;                 // rows of an outer tile
+constexpr int kBN = 64;                  // rows of an inner tile
+constexpr int kCalcThreads = 512;        // four warpgroups: warpgroup q owns columns [16 q, 16 q + 16) of a tile
+constexpr int kBwdThreads = kCalcThreads + 32;  // plus the issuing warp
+constexpr int kYStages = 3;              // inner tiles in flight
 constexpr uint32_t kBwdTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
 struct BwdCfg {
-    static constexpr int kTileBytes = kBM * D * 2;  // one 16-bit tile: D / 64 panels
-    static constexpr int kOffX = 0;                 // X1, X2
-    static constexpr int kOffY = 2 * kTileBytes;    // [2 stages][Y1, Y2]
-    static constexpr int kOffStat = kOffY + 4 * kTileBytes;  // [2 (lse2, D)][128] floats
-    static constexpr int kOffMask = kOffStat + 2 * kBM * 4;  // 4 words: inner rows that are global
-    static constexpr int kOffBar = kOffMask + 16;            // barriers
-    static constexpr int kOffMisc = kOffBar + 8 * 8;         // TMEM base, abort flag
+    static constexpr int kXPanel = kBM * 128;       // 128 rows x 128 bytes
+    static constexpr int kYPanel = kBN * 128;       // 64 rows x 128 bytes
+    static constexpr int kXBytes = kBM * D * 2;     // one outer tile: D / 64 panels
+    static constexpr int kYBytes = kBN * D * 2;     // one inner tile
+    static constexpr int kOffX = 0;                              // X1, X2
+    static constexpr int kOffY = 2 * kXBytes;                    // [kYStages][Y1, Y2]
+    static constexpr int kOffStat = kOffY + kYStages * 2 * kYBytes;  // [kYStages][2 (lse2, D)][kBN] floats
+    static constexpr int kOffBar = kOffStat + kYStages * 2 * kBN * 4;  // 12 barriers
+    static constexpr int kOffMisc = kOffBar + 12 * 8;                   // TMEM base, abort flag
     static constexpr int kUsed = kOffMisc + 16;
     // one CTA per SM: the CTA holds 512 TMEM columns
     static constexpr int kSmemBytes = (kUsed + 1024 > 120 * 1024) ? kUsed + 1024 : 120 * 1024;
@@ -70,12 +74,16 @@ struct BwdUnit {
     int outer0;  // band: first outer row; all: first compact row
     int split;
     int inner0;  // first inner row of the contiguous tiles
-    int n_cont;  // contiguous inner tiles
+    int n_cont;  // contiguous inner tiles (kBN rows each)
     int n_comp;  // compact inner tiles after them
 };
 
+// Units [0, n_units - n_band_units) are the global-row / global-key units (the longer kind,
+// scheduled first so the short band units fill the tail), then the band units.
 __device__ __forceinline__ BwdUnit bwd_decode(const BwdParams& p, int u) {
     BwdUnit un;
+    const int n_all = p.n_units - p.n_band_units;
+    u = u < n_all ? p.n_band_units + u : u - n_all;
     if (u < p.n_band_units) {
         un.all = false;
         un.bh = u / p.n_tiles;
@@ -87,8 +95,8 @@ __device__ __forceinline__ BwdUnit bwd_decode(const BwdParams& p, int u) {
         int hi = un.outer0 + kBM - 1 + p.window;
         if (hi > p.n - 1) hi = p.n - 1;
         un.inner0 = lo;
-        un.n_cont = (hi - lo + kBM) / kBM;
-        un.n_comp = p.g_tiles;
+        un.n_cont = (hi - lo + kBN) / kBN;
+        un.n_comp = p.gi_tiles;
     } else {
         const int t = u - p.n_band_units;
         un.all = true;
@@ -96,8 +104,8 @@ __device__ __forceinline__ BwdUnit bwd_decode(const BwdParams& p, int u) {
         const int rest = t / p.n_splits;
         un.outer0 = (rest % p.g_tiles) * kBM;
         un.bh = rest / p.g_tiles;
-        un.inner0 = un.split * p.split_tiles * kBM;
-        int tiles = (p.n - un.inner0 + kBM - 1) / kBM;
+        un.inner0 = un.split * p.split_tiles * kBN;
+        int tiles = (p.n - un.inner0 + kBN - 1) / kBN;
         if (tiles > p.split_tiles) tiles = p.split_tiles;
         un.n_cont = tiles;
         un.n_comp = 0;
@@ -115,12 +123,6 @@ __device__ __forceinline__ int bwd_lower(const int* __restrict__ gl, int count, 
     return a;
 }
 
-__device__ __forceinline__ bool bwd_is_global(const BwdParams& p, int row) {
-    if (p.num_global == 0) return false;
-    const int a = bwd_lower(p.gidx, p.num_global, row);
-    return a < p.num_global && __ldg(p.gidx + a) == row;
-}
-
 // 32-bit mask of the columns [c0, c0 + 32) that lie in [lo, hi].
 __device__ __forceinline__ uint32_t range_bits(int c0, int lo, int hi) {
     const int a = lo - c0 > 0 ? lo - c0 : 0;
@@ -130,18 +132,36 @@ __device__ __forceinline__ uint32_t range_bits(int c0, int lo, int hi) {
     return upto_b & ~((1u << a) - 1u);
 }
 
+// Bits of the rows [r0, r0 + 32) that are global tokens (r0 >= 0; the bitmap has a zero
+// word past the last row).
+__device__ __forceinline__ uint32_t global_bits(const uint32_t* __restrict__ bm, int r0) {
+    const uint32_t w0 = __ldg(bm + (r0 >> 5)), w1 = __ldg(bm + (r0 >> 5) + 1);
+    return __funnelshift_r(w0, w1, r0 & 31);
+}
+
+// One tile of `rows` rows (128-byte swizzled panels of `panel` bytes, D / 64 of them).
 template <int D>
-__device__ __forceinline__ void bwd_load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, bool compact,
-                                              int row0, int bh) {
+__device__ __forceinline__ void bwd_load_tile(uint8_t* dst, int panel, const CUtensorMap* map, uint64_t* bar,
+                                              bool compact, int row0, int bh) {
 #pragma unroll
     for (int pn = 0; pn < D / 64; ++pn) {
         if (compact)
-            ptx::tma_load_3d(dst + pn * kBwdPanel, map, bar, pn * 64, bh, row0);
+            ptx::tma_load_3d(dst + pn * panel, map, bar, pn * 64, bh, row0);
         else
-            ptx::tma_load_3d(dst + pn * kBwdPanel, map, bar, pn * 64, row0, bh);
+            ptx::tma_load_3d(dst + pn * panel, map, bar, pn * 64, row0, bh);
     }
 }
 
+// Warp 8 issues (its lane 0 drives TMA and tcgen05; for the dK/dV kernel its 32 lanes also
+// stage the inner rows' LSE and D); warps 0-7 turn S and dP into P and dS.  Per inner tile t
+// (kBN rows), S / dP double-buffered in TMEM (buffer b = t & 1: S in columns
+// [128 b, 128 b + 64), dP in [128 b + 64, 128 b + 128)):
+//   issuer: S/dP of tile t + 1 as soon as tile t - 1's accumulating MMAs have finished (they
+//           read that buffer), so they run while warps 0-7 work on tile t; then, once P/dS of
+//           tile t are written (p_full), the accumulating TS MMAs of tile t;
+//   warps 0-7: wait for S/dP of tile t (s_full), write P and dS over them, signal p_full.
+// Inner tiles come through a 3-stage TMA ring: stage t % 3 is refilled with tile t + 3 once
+// tile t's accumulating MMAs are done.
 template <int D, bool BF16, bool KM>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     lca_bwd_main(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
@@ -155,26 +175,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* sX = smem + C::kOffX;
     uint8_t* sY = smem + C::kOffY;
     float* sStat = reinterpret_cast<float*>(smem + C::kOffStat);
-    uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + C::kOffMask);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
     uint64_t* bar_x = bars + 0;
-    uint64_t* bar_y = bars + 1;  // [2]
-    uint64_t* bar_s = bars + 3;
-    uint64_t* bar_o = bars + 4;
+    uint64_t* bar_y = bars + 1;   // [kYStages]
+    uint64_t* s_full = bars + 4;  // [2] S/dP of the buffer computed (and, dK/dV, its stats staged)
+    uint64_t* p_full = bars + 6;  // [2] P/dS of the buffer written
+    uint64_t* bar_o = bars + 8;   // the accumulating MMAs of the latest tile finished (one per tile)
+    uint64_t* st_full = bars + 9; // [kYStages] dK/dV kernel: LSE and D of the stage's inner rows staged
     uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
+    const int lane = tid & 31;
     const BwdUnit un = bwd_decode(p, blockIdx.x);
     const int T = un.n_cont + un.n_comp;
 
     if (tid == 0) {
         ptx::mbar_init(bar_x, 1);
-        ptx::mbar_init(&bar_y[0], 1);
-        ptx::mbar_init(&bar_y[1], 1);
-        ptx::mbar_init(bar_s, 1);
+        for (int i = 0; i < kYStages; ++i) ptx::mbar_init(&bar_y[i], 1);
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(&s_full[i], 1);
+            ptx::mbar_init(&p_full[i], kCalcThreads / 32);
+        }
         ptx::mbar_init(bar_o, 1);
+        for (int i = 0; i < kYStages; ++i) ptx::mbar_init(&st_full[i], 32);  // the issuing warp's lanes
         *abort_flag = 0;
         ptx::fence_mbar_init();
     }
@@ -186,24 +211,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *sTmem;
-    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
-    constexpr uint32_t kColS = 0, kColDP = 128, kColA = 256, kColB = 256 + D;
+    constexpr uint32_t kColA = 256, kColB = 256 + D;
 
-    // inner tile t: contiguous rows inner0 + 128 t, or compact tile t - n_cont
-    auto load_inner = [&](int t) {
-        const int st = t & 1;
-        uint8_t* y = sY + st * 2 * C::kTileBytes;
-        ptx::mbar_arrive_expect_tx(&bar_y[st], 2 * C::kTileBytes);
-        if (t < un.n_cont) {
-            const int r0 = un.inner0 + t * kBM;
-            bwd_load_tile<D>(y, &tm_y1, &bar_y[st], false, r0, un.bh);
-            bwd_load_tile<D>(y + C::kTileBytes, &tm_y2, &bar_y[st], false, r0, un.bh);
-        } else {
-            const int r0 = (t - un.n_cont) * kBM;
-            bwd_load_tile<D>(y, &tm_y1g, &bar_y[st], true, r0, un.bh);
-            bwd_load_tile<D>(y + C::kTileBytes, &tm_y2g, &bar_y[st], true, r0, un.bh);
-        }
-    };
     bool ok = true;
     auto wait = [&](uint64_t* bar, int parity) {
         if (!ok) return;
@@ -211,149 +220,214 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                             p.timeout_ns);
     };
 
-    if (tid == 0) {
-        ptx::prefetch_tmap(&tm_x1);
-        ptx::prefetch_tmap(&tm_y1);
-        ptx::mbar_arrive_expect_tx(bar_x, 2 * C::kTileBytes);
-        if (un.all) {
-            bwd_load_tile<D>(sX, &tm_x1g, bar_x, true, un.outer0, un.bh);
-            bwd_load_tile<D>(sX + C::kTileBytes, &tm_x2g, bar_x, true, un.outer0, un.bh);
-        } else {
-            bwd_load_tile<D>(sX, &tm_x1, bar_x, false, un.outer0, un.bh);
-            bwd_load_tile<D>(sX + C::kTileBytes, &tm_x2, bar_x, false, un.outer0, un.bh);
-        }
-        for (int t = 0; t < 2 && t < T; ++t) load_inner(t);
-    }
-
-    // the outer row of this thread: valid, and (dQ kernel) its LSE and D
-    const int orow = un.outer0 + tid;  // band: absolute row / key; all: compact index
-    const bool row_ok = un.all ? (orow < p.num_global) : (orow < p.n);
-    float row_lse2 = 0.f, row_d = 0.f;
-    if constexpr (!KM) {
-        if (row_ok) {
-            const size_t idx = un.all ? (size_t)un.bh * p.num_global + orow : (size_t)un.bh * p.n + orow;
-            row_lse2 = un.all ? __ldg(p.lse2g + idx) : __ldg(p.lse2 + idx);
-            row_d = un.all ? __ldg(p.dg + idx) : __ldg(p.dvec + idx);
-        }
-    }
-
-    const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
-    const uint32_t idesc_s = ptx::idesc_f16(BF16, kBM, kBM, false);
-    const uint32_t idesc_acc = ptx::idesc_f16(BF16, kBM, D, true);
-
-    // Every exit from this loop is block-uniform (__syncthreads_or on the threads' `ok`):
-    // a bounded wait that gives up in one thread ends the loop for all of them.
-    for (int t = 0; t < T; ++t) {
-        const int st = t & 1;
-        const bool cont = t < un.n_cont;
-        const int tile0 = cont ? un.inner0 + t * kBM : (t - un.n_cont) * kBM;
-        // inner rows of a contiguous band tile that are global tokens (excluded: they are
-        // counted by the global-row / global-key units or the compact tiles)
-        if (tid == 0) {
-            uint32_t m[4] = {0u, 0u, 0u, 0u};
-            if (cont && !un.all && p.num_global > 0) {
-                int a = bwd_lower(p.gidx, p.num_global, tile0);
-                for (; a < p.num_global; ++a) {
-                    const int c = __ldg(p.gidx + a) - tile0;
-                    if (c >= kBM) break;
-                    m[c >> 5] |= 1u << (c & 31);
+    if (warp == kCalcThreads / 32) {
+        // ============================================================ issuing warp
+        auto load_inner = [&](int t) {  // lane 0
+            const int st = t % kYStages;
+            uint8_t* y = sY + st * 2 * C::kYBytes;
+            ptx::mbar_arrive_expect_tx(&bar_y[st], 2 * C::kYBytes);
+            const bool cont = t < un.n_cont;
+            const int r0 = cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
+            bwd_load_tile<D>(y, C::kYPanel, cont ? &tm_y1 : &tm_y1g, &bar_y[st], !cont, r0, un.bh);
+            bwd_load_tile<D>(y + C::kYBytes, C::kYPanel, cont ? &tm_y2 : &tm_y2g, &bar_y[st], !cont, r0, un.bh);
+        };
+        // dK/dV kernel: LSE and D of tile t's inner (query) rows into stage t % 3 (all lanes),
+        // staged with the tile's loads
+        auto stage_stats = [&](int t) {
+            if constexpr (KM) {
+                float* st = sStat + (t % kYStages) * 2 * kBN;
+                const bool cont = t < un.n_cont;
+                const int tile0 = cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
+#pragma unroll
+                for (int h = 0; h < kBN / 32; ++h) {
+                    const int c = h * 32 + lane;
+                    float l2 = 0.f, dd = 0.f;
+                    if (cont) {
+                        const int i = tile0 + c;
+                        if (i < p.n) {
+                            l2 = __ldg(p.lse2 + (size_t)un.bh * p.n + i);
+                            dd = __ldg(p.dvec + (size_t)un.bh * p.n + i);
+                        }
+                    } else if (tile0 + c < p.num_global) {
+                        l2 = __ldg(p.lse2g + (size_t)un.bh * p.num_global + tile0 + c);
+                        dd = __ldg(p.dg + (size_t)un.bh * p.num_global + tile0 + c);
+                    }
+                    st[c] = l2;
+                    st[kBN + c] = dd;
+                }
+                ptx::mbar_arrive(&st_full[t % kYStages]);  // releases this lane's writes
+            }
+        };
+        const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
+        const uint32_t idesc_s = ptx::idesc_f16(BF16, kBM, kBN, false);
+        const uint32_t idesc_acc = ptx::idesc_f16(BF16, kBM, D, true);
+        // S = X1 Y1^T and dP = X2 Y2^T of tile t into buffer t & 1 (lane 0)
+        auto issue_s = [&](int t) {
+            const int st = t % kYStages;
+            const uint32_t col = (uint32_t)(t & 1) * 128;
+            const uint32_t xs = ptx::smem_u32(sX);
+            const uint32_t ys = ptx::smem_u32(sY + st * 2 * C::kYBytes);
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const uint32_t alo = ptx::smem_desc_sw128_lo(xs + m * C::kXBytes, 0);
+                const uint32_t blo = ptx::smem_desc_sw128_lo(ys + m * C::kYBytes, 0);
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    const uint32_t aoff = ((ks >> 2) * C::kXPanel + (ks & 3) * 32) >> 4;
+                    const uint32_t boff = ((ks >> 2) * C::kYPanel + (ks & 3) * 32) >> 4;
+                    ptx::mma_f16_ss(tmem + col + m * kBN, ptx::desc_join(alo + aoff, dhi),
+                                    ptx::desc_join(blo + boff, dhi), idesc_s, ks > 0 ? 1u : 0u);
                 }
             }
-            sMask[0] = m[0];
-            sMask[1] = m[1];
-            sMask[2] = m[2];
-            sMask[3] = m[3];
-        }
-        if constexpr (KM) {
-            // LSE and D of the inner (query) rows
-            float l2 = 0.f, dd = 0.f;
-            if (cont) {
-                const int i = tile0 + tid;
-                if (i >= 0 && i < p.n) {
-                    l2 = __ldg(p.lse2 + (size_t)un.bh * p.n + i);
-                    dd = __ldg(p.dvec + (size_t)un.bh * p.n + i);
-                }
-            } else {
-                const int g = tile0 + tid;
-                if (g < p.num_global) {
-                    l2 = __ldg(p.lse2g + (size_t)un.bh * p.num_global + g);
-                    dd = __ldg(p.dg + (size_t)un.bh * p.num_global + g);
+            ptx::mma_commit(&s_full[t & 1]);
+        };
+        // dQ += dS Y1 (dQ kernel); dV += P^T Y2, dK += dS^T Y1 (dK/dV kernel) for tile t (lane 0)
+        auto issue_acc = [&](int t) {
+            const uint32_t ys = ptx::smem_u32(sY + (t % kYStages) * 2 * C::kYBytes);
+            const uint32_t y1lo = ptx::smem_desc_sw128_lo(ys, C::kYPanel);
+            const uint32_t y2lo = ptx::smem_desc_sw128_lo(ys + C::kYBytes, C::kYPanel);
+            const uint32_t col_s = (uint32_t)(t & 1) * 128, col_dp = col_s + kBN;
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+                const int key = 16 * kk;
+                const uint32_t acol = key;  // keys [key, key + 16): 8 packed columns from column key
+                const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+                const uint32_t boff = (uint32_t)(key * 128) >> 4;
+                if constexpr (KM) {
+                    ptx::mma_f16_ts(tmem + kColA, tmem + col_s + acol, ptx::desc_join(y2lo + boff, dhi), idesc_acc, acc);
+                    ptx::mma_f16_ts(tmem + kColB, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi), idesc_acc,
+                                    acc);
+                } else {
+                    ptx::mma_f16_ts(tmem + kColA, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi), idesc_acc,
+                                    acc);
                 }
             }
-            sStat[tid] = l2;
-            sStat[kBM + tid] = dd;
-        }
-        if (__syncthreads_or(!ok)) {
-            ok = false;
-            break;
-        }
+            ptx::mma_commit(bar_o);
+        };
 
-        // S = X1 Y1^T, dP = X2 Y2^T
-        if (tid == 0) {
-            if (t == 0) wait(bar_x, 0);
-            wait(&bar_y[st], t >> 1);
+        if (lane == 0) {
+            ptx::prefetch_tmap(&tm_x1);
+            ptx::prefetch_tmap(&tm_y1);
+            ptx::mbar_arrive_expect_tx(bar_x, 2 * C::kXBytes);
+            bwd_load_tile<D>(sX, C::kXPanel, un.all ? &tm_x1g : &tm_x1, bar_x, un.all, un.outer0, un.bh);
+            bwd_load_tile<D>(sX + C::kXBytes, C::kXPanel, un.all ? &tm_x2g : &tm_x2, bar_x, un.all, un.outer0,
+                             un.bh);
+            for (int t = 0; t < kYStages && t < T; ++t) load_inner(t);
+        }
+        for (int t = 0; t < kYStages && t < T; ++t) stage_stats(t);
+        if (lane == 0 && T > 0) {
+            wait(bar_x, 0);
+            wait(&bar_y[0], 0);
             if (ok) {
                 ptx::tc_fence_after();
-                const uint32_t xs = ptx::smem_u32(sX);
-                const uint32_t ys = ptx::smem_u32(sY + st * 2 * C::kTileBytes);
-#pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t off = ((ks >> 2) * kBwdPanel + (ks & 3) * 32) >> 4;
-                    ptx::mma_f16_ss(tmem + kColS, ptx::desc_join(ptx::smem_desc_sw128_lo(xs, 0) + off, dhi),
-                                    ptx::desc_join(ptx::smem_desc_sw128_lo(ys, 0) + off, dhi), idesc_s,
-                                    ks > 0 ? 1u : 0u);
-                }
-#pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t off = ((ks >> 2) * kBwdPanel + (ks & 3) * 32) >> 4;
-                    ptx::mma_f16_ss(tmem + kColDP,
-                                    ptx::desc_join(ptx::smem_desc_sw128_lo(xs + C::kTileBytes, 0) + off, dhi),
-                                    ptx::desc_join(ptx::smem_desc_sw128_lo(ys + C::kTileBytes, 0) + off, dhi),
-                                    idesc_s, ks > 0 ? 1u : 0u);
-                }
-                ptx::mma_commit(bar_s);
+                issue_s(0);
             }
         }
-        wait(bar_s, t);
-        if (__syncthreads_or(!ok)) {
-            ok = false;
-            break;
+        for (int t = 0; t < T; ++t) {
+            // tile t - 1's accumulating MMAs (every completion of bar_o is waited, in order):
+            // then buffer (t + 1) & 1 and tile t - 1's stage are free
+            if (lane == 0 && t >= 1) {
+                wait(bar_o, (t - 1) & 1);
+                if (ok && t + 2 < T) load_inner(t + 2);
+            }
+            __syncwarp();
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            // the stage's stats are read by the P / dS warps until tile t - 1's p_full, before
+            // its accumulating MMAs were issued
+            if (t >= 1 && t + 2 < T) stage_stats(t + 2);
+            if (t + 1 < T) {
+                if (lane == 0) {
+                    wait(&bar_y[(t + 1) % kYStages], ((t + 1) / kYStages) & 1);
+                    if (ok) {
+                        ptx::tc_fence_after();
+                        issue_s(t + 1);
+                    }
+                }
+            }
+            if (lane == 0) {
+                wait(&p_full[t & 1], (t >> 1) & 1);
+                if (ok) {
+                    ptx::tc_fence_after();
+                    issue_acc(t);
+                }
+            }
+            __syncwarp();
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
         }
-        ptx::tc_fence_after();
-
-        // this thread's visible columns of the tile: [lo, hi], minus the mask's
-        int lo, hi;
-        if (un.all) {
-            lo = 0;
-            hi = row_ok ? p.n - 1 - tile0 : -1;
-        } else if (cont) {
-            lo = orow - tile0 - p.window;
-            if (lo < -tile0) lo = -tile0;
-            hi = orow - tile0 + p.window;
-            if (hi > p.n - 1 - tile0) hi = p.n - 1 - tile0;
-            if (!row_ok) hi = -1;
-        } else {
-            lo = 0;
-            hi = row_ok ? p.num_global - 1 - tile0 : -1;
+        // the last accumulating MMAs (a commit covers every earlier MMA of the thread)
+        if (lane == 0 && ok && T > 0) wait(bar_o, (T - 1) & 1);
+    } else {
+        // ============================================================ P / dS warps
+        const int r = tid & (kBM - 1);  // outer row <-> TMEM lane
+        const int q = tid >> 7;         // column quarter of every inner tile
+        const int c0 = q * 16;
+        const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const int orow = un.outer0 + r;  // band: absolute row / key; all: compact index
+        const bool row_ok = un.all ? (orow < p.num_global) : (orow < p.n);
+        float row_lse2 = 0.f, row_d = 0.f;
+        if constexpr (!KM) {
+            if (row_ok) {
+                const size_t idx = un.all ? (size_t)un.bh * p.num_global + orow : (size_t)un.bh * p.n + orow;
+                row_lse2 = un.all ? __ldg(p.lse2g + idx) : __ldg(p.lse2 + idx);
+                row_d = un.all ? __ldg(p.dg + idx) : __ldg(p.dvec + idx);
+            }
         }
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            const uint32_t bits = range_bits(ch * 32, lo, hi) & ~sMask[ch];
-            float s[32], dp[32];
-            ptx::tmem_ld32(t_lane + kColS + ch * 32, s);
-            ptx::tmem_ld32(t_lane + kColDP + ch * 32, dp);
+        // global rows / keys among a contiguous band tile's 16 columns of this thread (counted
+        // by the global units or the compact tiles), loaded one tile ahead
+        const bool use_bitmap = !un.all && p.num_global > 0;
+        auto gbits_of = [&](int t) -> uint32_t {
+            if (!use_bitmap || t >= un.n_cont) return 0u;
+            return global_bits(p.gbitmap, un.inner0 + t * kBN + c0);
+        };
+        uint32_t gnext = T > 0 ? gbits_of(0) : 0u;
+        for (int t = 0; t < T; ++t) {
+            const int b = t & 1;
+            const bool cont = t < un.n_cont;
+            const int tile0 = cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
+            const uint32_t gbits = gnext;
+            gnext = gbits_of(t + 1);
+            // this thread's visible columns of its 16: [lo, hi]
+            int lo, hi;
+            if (un.all) {
+                lo = 0;
+                hi = row_ok ? p.n - 1 - tile0 : -1;
+            } else if (cont) {
+                lo = orow - tile0 - p.window;
+                hi = orow - tile0 + p.window;
+                if (hi > p.n - 1 - tile0) hi = p.n - 1 - tile0;
+                if (!row_ok) hi = -1;
+            } else {
+                lo = 0;
+                hi = row_ok ? p.num_global - 1 - tile0 : -1;
+            }
+            const uint32_t bits = range_bits(c0, lo, hi) & ~gbits;
+            wait(&s_full[b], (t >> 1) & 1);
+            if constexpr (KM) wait(&st_full[t % kYStages], (t / kYStages) & 1);
+            ok = __all_sync(0xffffffffu, ok);  // warp-uniform, so the __syncwarp below is reached by all
+            if (!ok) break;
+            ptx::tc_fence_after();
+            // packed 16-bit pairs go to the first 8 of this thread's own 16 columns (other
+            // quarters may still be reading theirs)
+            const uint32_t col_s = (uint32_t)b * 128 + c0;
+            const uint32_t col_dp = col_s + kBN;
+            float s[16], dp[16];
+            ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + c0, s);
+            ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + kBN + c0, dp);
             ptx::tmem_wait_ld();
-            uint32_t pk[16], dk[16];
+            const float* st = sStat + (t % kYStages) * 2 * kBN;
+            uint32_t pk[8], dk[8];
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
+            for (int e = 0; e < 16; e += 2) {
                 float pv[2], dv[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int c = e + h;
                     float l2, dd;
                     if constexpr (KM) {
-                        l2 = sStat[ch * 32 + c];
-                        dd = sStat[kBM + ch * 32 + c];
+                        l2 = st[c0 + c];
+                        dd = st[kBN + c0 + c];
                     } else {
                         l2 = row_lse2;
                         dd = row_d;
@@ -371,83 +445,62 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     dk[e >> 1] = ptx::pack_f16x2(dv[0], dv[1]);
                 }
             }
-            // packed pairs of keys [32 ch, 32 ch + 32) in the first 16 columns of the chunk
-            if constexpr (KM) ptx::tmem_st16u(t_lane + kColS + ch * 32, pk);
-            ptx::tmem_st16u(t_lane + kColDP + ch * 32, dk);
-        }
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        __syncthreads();
-
-        // accumulate: dQ += dS Y1 (dQ kernel); dV += P^T Y2, dK += dS^T Y1 (dK/dV kernel)
-        if (tid == 0) {
-            ptx::tc_fence_after();
-            const uint32_t ys = ptx::smem_u32(sY + st * 2 * C::kTileBytes);
-            const uint32_t y1lo = ptx::smem_desc_sw128_lo(ys, kBwdPanel);
-            const uint32_t y2lo = ptx::smem_desc_sw128_lo(ys + C::kTileBytes, kBwdPanel);
-#pragma unroll
-            for (int kk = 0; kk < kBM / 16; ++kk) {
-                const int key = 16 * kk;
-                const uint32_t acol = (key >> 5) * 32 + ((key >> 4) & 1) * 8;
-                const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-                const uint32_t boff = (uint32_t)(key * 128) >> 4;
-                if constexpr (KM) {
-                    ptx::mma_f16_ts(tmem + kColA, tmem + kColS + acol, ptx::desc_join(y2lo + boff, dhi), idesc_acc,
-                                    acc);
-                    ptx::mma_f16_ts(tmem + kColB, tmem + kColDP + acol, ptx::desc_join(y1lo + boff, dhi),
-                                    idesc_acc, acc);
-                } else {
-                    ptx::mma_f16_ts(tmem + kColA, tmem + kColDP + acol, ptx::desc_join(y1lo + boff, dhi),
-                                    idesc_acc, acc);
-                }
-            }
-            ptx::mma_commit(bar_o);
-            // S / dP are overwritten by the next tile's MMAs and stage st by tile t + 2:
-            // both wait for these MMAs to finish
-            wait(bar_o, t);
-            if (ok && t + 2 < T) load_inner(t + 2);
+            // keys [16 q, 16 q + 16) as 8 packed columns from column 16 q: the A operand of one
+            // 16-key step of the accumulating MMAs
+            if constexpr (KM) ptx::tmem_st8u(t_lane + col_s, pk);
+            ptx::tmem_st8u(t_lane + col_dp, dk);
+            ptx::tmem_wait_st();
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&p_full[b]);
         }
     }
     if (__syncthreads_or(!ok) || *abort_flag) ok = false;
 
-    if (ok && T > 0) {
+    if (ok && T > 0 && warp < kCalcThreads / 32) {
         ptx::tc_fence_after();
-        // epilogue: this thread's outer row of the accumulators
+        // epilogue: this thread's outer row, columns [D/4 q, D/4 (q + 1)) of the accumulators
+        const int r = tid & (kBM - 1);
+        const int q = tid >> 7;
+        const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const int orow = un.outer0 + r;
+        const bool row_ok = un.all ? (orow < p.num_global) : (orow < p.n);
         bool write = row_ok;
         float* dst_a = nullptr;
         float* dst_b = nullptr;
         if (un.all) {
-            const size_t r = ((size_t)un.split * p.bh + un.bh) * p.num_global + orow;
-            dst_a = p.part_a + r * D;
-            if constexpr (KM) dst_b = p.part_b + r * D;
+            const size_t rr = ((size_t)un.split * p.bh + un.bh) * p.num_global + orow;
+            dst_a = p.part_a + rr * D;
+            if constexpr (KM) dst_b = p.part_b + rr * D;
         } else {
-            write = write && !bwd_is_global(p, orow);
-            const size_t r = (size_t)un.bh * p.n + orow;
-            dst_a = p.out_a + r * D;
-            if constexpr (KM) dst_b = p.out_b + r * D;
+            if (write && p.num_global > 0 && ((__ldg(p.gbitmap + (orow >> 5)) >> (orow & 31)) & 1u)) write = false;
+            const size_t rr = (size_t)un.bh * p.n + orow;
+            dst_a = p.out_a + rr * D;
+            if constexpr (KM) dst_b = p.out_b + rr * D;
         }
 #pragma unroll
-        for (int ch = 0; ch < D / 32; ++ch) {
-            float a[32];
-            ptx::tmem_ld32(t_lane + kColA + ch * 32, a);
+        for (int ch = 0; ch < D / 64; ++ch) {
+            const int cc = (q * (D / 64) + ch) * 16;
+            float a[16];
+            ptx::tmem_ld16(t_lane + kColA + cc, a);
             ptx::tmem_wait_ld();
             if (write) {
                 // dQ and dK carry the scale, dV does not
                 const float f = KM ? 1.f : p.scale;
 #pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    *reinterpret_cast<float4*>(dst_a + ch * 32 + e) =
+                for (int e = 0; e < 16; e += 4)
+                    *reinterpret_cast<float4*>(dst_a + cc + e) =
                         make_float4(a[e] * f, a[e + 1] * f, a[e + 2] * f, a[e + 3] * f);
             }
             if constexpr (KM) {
-                float b[32];
-                ptx::tmem_ld32(t_lane + kColB + ch * 32, b);
+                float bb[16];
+                ptx::tmem_ld16(t_lane + kColB + cc, bb);
                 ptx::tmem_wait_ld();
                 if (write) {
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4)
-                        *reinterpret_cast<float4*>(dst_b + ch * 32 + e) =
-                            make_float4(b[e] * p.scale, b[e + 1] * p.scale, b[e + 2] * p.scale, b[e + 3] * p.scale);
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<float4*>(dst_b + cc + e) = make_float4(
+                            bb[e] * p.scale, bb[e + 1] * p.scale, bb[e + 2] * p.scale, bb[e + 3] * p.scale);
                 }
             }
         }
@@ -458,68 +511,64 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 __global__ void __launch_bounds__(256) lca_bwd_indices(BwdIndexParams ip) {
-    for (int i = threadIdx.x; i < ip.count; i += blockDim.x) ip.dst[i] = ip.idx[i];
+    if (ip.clear_bitmap) {
+        for (int i = threadIdx.x; i < ip.bitmap_words; i += blockDim.x) ip.bitmap[i] = 0u;
+        __syncthreads();
+    }
+    for (int i = threadIdx.x; i < ip.count; i += blockDim.x) {
+        const int g = ip.idx[i];
+        ip.dst[i] = g;
+        atomicOr(ip.bitmap + (g >> 5), 1u << (g & 31));
+    }
 }
 
-// One warp per row (bh, i): D_i in fp32, the 16-bit dO row, LSE * log2 e; a global row also
-// goes to the compact buffers.
+// D / 4 threads per row (bh, i), four columns each (16-byte loads): D_i in fp32, the 16-bit
+// dO row, LSE * log2 e; a global row also goes to the compact buffers.
 template <int D>
 __global__ void __launch_bounds__(256) lca_bwd_prep(BwdPrepParams pp) {
-    constexpr int kPer = D / 32;
-    const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (w >= (long long)pp.bh * pp.n) return;
-    const int bh = (int)(w / pp.n);
-    const int i = (int)(w % pp.n);
-    const size_t off = (size_t)w * D + lane * kPer;
-    float dov[kPer], ov[kPer];
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) {
-        dov[e] = __ldg(pp.dout + off + e);
-        ov[e] = __ldg(pp.o + off + e);
+    constexpr int kLanes = D / 4;             // threads of one row
+    constexpr int kRows = 256 / kLanes;       // rows of one block
+    const int sub = threadIdx.x % kLanes;
+    const long long w = (long long)blockIdx.x * kRows + threadIdx.x / kLanes;
+    const bool live = w < (long long)pp.bh * pp.n;
+    const long long wr = live ? w : 0;
+    const int bh = (int)(wr / pp.n);
+    const int i = (int)(wr % pp.n);
+    const size_t off = (size_t)wr * D + sub * 4;
+    float4 dov = make_float4(0.f, 0.f, 0.f, 0.f), ov = dov;
+    if (live) {
+        dov = __ldg(reinterpret_cast<const float4*>(pp.dout + off));
+        ov = __ldg(reinterpret_cast<const float4*>(pp.o + off));
     }
-    float dot = 0.f;
+    float dot = dov.x * ov.x + dov.y * ov.y + dov.z * ov.z + dov.w * ov.w;
 #pragma unroll
-    for (int e = 0; e < kPer; ++e) dot = fmaf(dov[e], ov[e], dot);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    uint32_t packed[kPer / 2];
-#pragma unroll
-    for (int e = 0; e < kPer; e += 2)
-        packed[e / 2] = pp.bf16 ? ptx::pack_bf16x2(dov[e], dov[e + 1]) : ptx::pack_f16x2(dov[e], dov[e + 1]);
+    for (int o = kLanes / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o, kLanes);
+    if (!live) return;
+    const uint2 packed = pp.bf16 ? make_uint2(ptx::pack_bf16x2(dov.x, dov.y), ptx::pack_bf16x2(dov.z, dov.w))
+                                 : make_uint2(ptx::pack_f16x2(dov.x, dov.y), ptx::pack_f16x2(dov.z, dov.w));
     uint16_t* d16 = static_cast<uint16_t*>(pp.dout16) + off;
-    if constexpr (kPer == 2)
-        *reinterpret_cast<uint32_t*>(d16) = packed[0];
-    else
-        *reinterpret_cast<uint2*>(d16) = make_uint2(packed[0], packed[1]);
+    *reinterpret_cast<uint2*>(d16) = packed;
     const float l2 = __ldg(pp.lse + w) * kLog2e;
-    if (lane == 0) {
+    if (sub == 0) {
         pp.lse2[w] = l2;
         pp.dvec[w] = dot;
     }
     if (pp.num_global > 0) {
-        int g = -1;
-        if (lane == 0) {
-            const int a = bwd_lower(pp.gidx, pp.num_global, i);
-            if (a < pp.num_global && __ldg(pp.gidx + a) == i) g = a;
+        // (rows of one block share a bitmap word or two; the bitmap is written before this launch)
+        if (((__ldg(pp.gbitmap + (i >> 5)) >> (i & 31)) & 1u) == 0u) return;
+        const int g = bwd_lower(pp.gidx, pp.num_global, i);
+        // compact [G][4][bh][d]: planes q, k, v, dO16
+        uint16_t* cbase = static_cast<uint16_t*>(pp.compact);
+        const uint16_t* src[3] = {static_cast<const uint16_t*>(pp.q), static_cast<const uint16_t*>(pp.k),
+                                  static_cast<const uint16_t*>(pp.v)};
+#pragma unroll
+        for (int pl = 0; pl < 4; ++pl) {
+            uint2* dst = reinterpret_cast<uint2*>(cbase + (((size_t)g * 4 + pl) * pp.bh + bh) * D + sub * 4);
+            *dst = pl < 3 ? *reinterpret_cast<const uint2*>(src[pl] + off) : packed;
         }
-        g = __shfl_sync(0xffffffffu, g, 0);
-        if (g >= 0) {
-            // compact [G][4][bh][d]: planes q, k, v, dO16
-            uint16_t* cbase = static_cast<uint16_t*>(pp.compact);
-            const uint16_t* src[3] = {static_cast<const uint16_t*>(pp.q), static_cast<const uint16_t*>(pp.k),
-                                      static_cast<const uint16_t*>(pp.v)};
-#pragma unroll
-            for (int pl = 0; pl < 4; ++pl) {
-                uint16_t* dst = cbase + (((size_t)g * 4 + pl) * pp.bh + bh) * D + lane * kPer;
-                const uint16_t* s = pl < 3 ? src[pl] + off : d16;
-#pragma unroll
-                for (int e = 0; e < kPer; ++e) dst[e] = s[e];
-            }
-            if (lane == 0) {
-                pp.lse2g[(size_t)bh * pp.num_global + g] = l2;
-                pp.dg[(size_t)bh * pp.num_global + g] = dot;
-            }
+        if (sub == 0) {
+            pp.lse2g[(size_t)bh * pp.num_global + g] = l2;
+            pp.dg[(size_t)bh * pp.num_global + g] = dot;
         }
     }
 }
@@ -586,14 +635,14 @@ cudaError_t launch_bwd_indices(const BwdIndexParams& ip, cudaStream_t stream) {
 cudaError_t launch_bwd_prep(int head_dim, const BwdPrepParams& pp, cudaStream_t stream) {
     const long long rows = (long long)pp.bh * pp.n;
     if (rows <= 0) return cudaSuccess;
-    if ((rows + 7) / 8 > INT_MAX) return cudaErrorInvalidValue;
-    const unsigned grid = (unsigned)((rows + 7) / 8);
+    if (head_dim != 64 && head_dim != 128) return cudaErrorInvalidValue;
+    const long long per_block = 256 / (head_dim / 4);
+    if ((rows + per_block - 1) / per_block > INT_MAX) return cudaErrorInvalidValue;
+    const unsigned grid = (unsigned)((rows + per_block - 1) / per_block);
     if (head_dim == 64)
         lca_bwd_prep<64><<<grid, 256, 0, stream>>>(pp);
-    else if (head_dim == 128)
-        lca_bwd_prep<128><<<grid, 256, 0, stream>>>(pp);
     else
-        return cudaErrorInvalidValue;
+        lca_bwd_prep<128><<<grid, 256, 0, stream>>>(pp);
     return cudaGetLastError();
 }
 

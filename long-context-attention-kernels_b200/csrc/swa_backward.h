@@ -28,15 +28,17 @@ struct BwdParams {
     int bh;            // batch * heads
     int window;        // band radius, clamped to n
     int num_global;    // G: unique global tokens
-    int g_tiles;       // ceil(G / 128)
+    int g_tiles;       // ceil(G / 128): compact outer tiles
+    int gi_tiles;      // ceil(G / 64): compact inner tiles
     int n_tiles;       // ceil(n / 128): band units per (batch, head)
-    int split_tiles;   // 128-row tiles of one split of the global-row / global-key units
+    int split_tiles;   // 64-row inner tiles of one split of the global-row / global-key units
     int n_splits;      // splits per (bh, global tile)
     int n_band_units;  // bh * n_tiles
     int n_units;       // n_band_units + bh * g_tiles * n_splits
     float scale;       // softmax scale (dQ and dK carry it)
     float scale_log2;  // scale * log2(e)
     const int* gidx;   // [G] sorted absolute global indices
+    const uint32_t* gbitmap;  // bit i of word i / 32: row i is a global token (ceil(n / 32) + 3 words)
     const float* lse2;  // [bh][n] LSE * log2(e)
     const float* dvec;  // [bh][n] D_i = sum_c dO[i][c] * O[i][c]
     const float* lse2g; // [bh][G] the same for the global rows
@@ -49,7 +51,8 @@ struct BwdParams {
     unsigned long long timeout_ns;
 };
 
-// Tensor maps of one backward kernel: box 64 columns x 128 rows, 128-byte swizzle.
+// Tensor maps of one backward kernel, 128-byte swizzle, box 64 columns x 128 rows (outer
+// tiles) or x 64 rows (inner tiles):
 //   x1, x2: the outer tile's two operands over [bh][n][d] (dQ kernel: Q, dO16; dK/dV: K, V)
 //   y1, y2: the inner tiles' two operands (dQ kernel: K, V; dK/dV: Q, dO16)
 //   x1g, x2g, y1g, y2g: the same tensors' compact global rows, maps {d, bh, G}
@@ -74,6 +77,7 @@ struct BwdPrepParams {
     float* lse2g;       // [bh][G]
     float* dg;          // [bh][G]
     const int* gidx;    // [G] sorted
+    const uint32_t* gbitmap;  // global rows (lca_bwd_indices writes it first)
     int num_global;
     int n;
     int bh;
@@ -95,11 +99,15 @@ struct BwdReduceParams {
     int bh;
 };
 
-// Up to kBwdIndexChunk sorted global indices written to dst[0, count) (the host passes the
-// list in chunks through kernel parameters, so the copy is an ordinary capturable launch).
+// Up to kBwdIndexChunk sorted global indices written to dst[0, count) and set in the
+// global-row bitmap (cleared first when clear_bitmap); the host passes the list in chunks
+// through kernel parameters, so the copy is an ordinary capturable launch.
 constexpr int kBwdIndexChunk = 1024;
 struct BwdIndexParams {
     int* dst;
+    uint32_t* bitmap;
+    int bitmap_words;
+    int clear_bitmap;
     int count;
     int idx[kBwdIndexChunk];
 };
