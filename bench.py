@@ -68,6 +68,8 @@ def parse_args(argv=None):
                          "(default for context_128k_d128)")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager forward calls instead of replays of one captured forward")
+    ap.add_argument("--no-backward", action="store_true",
+                    help="skip the one-GPU measurement of the backward pass on the headline workload")
     ap.add_argument("--no-sequence", action="store_true",
                     help="skip the sequence-sharded 128K measurement added to the head-sharded line")
     ap.add_argument("--cpu-dense-all", action="store_true",
@@ -418,6 +420,10 @@ def run_ours(args):
         others = {name: measure_one_gpu(WORKLOADS[name], dev, steps=min(args.steps, 100), warmup=args.warmup)
                   for name in ("single_head_16k", "longformer_base_4k")}
 
+    backward = None
+    if world == 1 and not args.no_backward:
+        backward = measure_backward(w, dev, steps=min(args.steps, 20), warmup=args.warmup)
+
     sequence = None
     if not args.no_sequence and w.name != SEQUENCE_WORKLOAD:
         sequence = measure_sequence(WORKLOADS[SEQUENCE_WORKLOAD], world, rank, local, dev, pg,
@@ -456,6 +462,8 @@ def run_ours(args):
             line["sequence_128k"] = sequence
         if others is not None:
             line["other_configs"] = others
+        if backward is not None:
+            line["backward"] = backward
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
@@ -519,6 +527,53 @@ def measure_one_gpu(w, dev, steps: int, warmup: int) -> dict:
             "ms_per_step": ms, "main_kernel_ms": main_ms, "useful_tflops": w.useful_flops() / (ms * 1e-3) / 1e12,
             "config": config_of(w, 1, "one GPU"), "roofline": rf,
             "step_timing": "replays of one forward captured as a CUDA graph"}
+
+
+def measure_backward(w, dev, steps: int, warmup: int) -> dict:
+    """The backward pass (sliding_window_attention_backward: dQ, dK, dV from the forward's O
+    and LSE and a seeded dO) of the whole workload on this GPU, inputs resident, one call
+    captured as a CUDA graph and replayed; CUDA events around the replays.  Useful FLOPs are
+    2.5x the forward's (five products of 2 d per visible score against two)."""
+    import long_context_attention as lca
+
+    q, k, v = w.inputs(device=dev)
+    g = w.global_tokens()
+    out, lse = lca.sliding_window_attention_with_lse(q, k, v, w.window, g, w.scale)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    dout = torch.randn(out.shape, device=dev, generator=gen)
+
+    def bwd():
+        return lca.sliding_window_attention_backward(q, k, v, out, lse, dout, w.window, g, w.scale)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, 3)):
+            grads = bwd()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        grads = bwd()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        graph.replay()
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    assert lca.device_error() == 0
+    del grads, graph, q, k, v, out, lse, dout
+    torch.cuda.empty_cache()
+    flops = 2.5 * w.useful_flops()
+    # bytes the backward must move: Q, K, V (16-bit) and O, dO (fp32) read, dQ, dK, dV (fp32) written
+    elems = w.batch * w.heads * w.seq_len * w.head_dim
+    io = elems * (3 * 2 + 2 * 4 + 3 * 4)
+    rf = roofline(flops, io, ms, None, "lca_bwd_prep + lca_bwd_main (dQ, dK/dV) + lca_bwd_reduce")
+    return {"workload": w.name, "ms_per_step": ms, "useful_tflops": flops / (ms * 1e-3) / 1e12,
+            "tokens_per_s": w.tokens() / (ms * 1e-3), "roofline": rf,
+            "step_timing": "replays of one backward call captured as a CUDA graph",
+            "note": "whole backward call (5 launches); useful FLOPs = 2.5 x the forward's"}
 
 
 def measure_sequence(w, world, rank, local, dev, pg, steps, warmup, exchange, e2e_steps, cpu, heads=None,

@@ -48,12 +48,12 @@ constexpr int kBM = 128;                 // rows of an outer tile
 constexpr int kBN = 64;                  // rows of an inner tile
 constexpr int kCalcThreads = 512;        // four warpgroups: warpgroup q owns columns [16 q, 16 q + 16) of a tile
 constexpr int kBwdThreads = kCalcThreads + 32;  // plus the issuing warp
-constexpr int kYStages = 3;              // inner tiles in flight
 constexpr uint32_t kBwdTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
 struct BwdCfg {
+    static constexpr int kYStages = D == 64 ? 8 : 4;  // inner tiles in flight (TMA ring)
     static constexpr int kXPanel = kBM * 128;       // 128 rows x 128 bytes
     static constexpr int kYPanel = kBN * 128;       // 64 rows x 128 bytes
     static constexpr int kXBytes = kBM * D * 2;     // one outer tile: D / 64 panels
@@ -61,8 +61,9 @@ struct BwdCfg {
     static constexpr int kOffX = 0;                              // X1, X2
     static constexpr int kOffY = 2 * kXBytes;                    // [kYStages][Y1, Y2]
     static constexpr int kOffStat = kOffY + kYStages * 2 * kYBytes;  // [kYStages][2 (lse2, D)][kBN] floats
-    static constexpr int kOffBar = kOffStat + kYStages * 2 * kBN * 4;  // 12 barriers
-    static constexpr int kOffMisc = kOffBar + 12 * 8;                   // TMEM base, abort flag
+    static constexpr int kNumBars = 6 + 2 * kYStages;
+    static constexpr int kOffBar = kOffStat + kYStages * 2 * kBN * 4;  // kNumBars barriers
+    static constexpr int kOffMisc = kOffBar + kNumBars * 8;            // TMEM base, abort flag
     static constexpr int kUsed = kOffMisc + 16;
     // one CTA per SM: the CTA holds 512 TMEM columns
     static constexpr int kSmemBytes = (kUsed + 1024 > 120 * 1024) ? kUsed + 1024 : 120 * 1024;
@@ -160,8 +161,8 @@ __device__ __forceinline__ void bwd_load_tile(uint8_t* dst, int panel, const CUt
 //           read that buffer), so they run while warps 0-7 work on tile t; then, once P/dS of
 //           tile t are written (p_full), the accumulating TS MMAs of tile t;
 //   warps 0-7: wait for S/dP of tile t (s_full), write P and dS over them, signal p_full.
-// Inner tiles come through a 3-stage TMA ring: stage t % 3 is refilled with tile t + 3 once
-// tile t's accumulating MMAs are done.
+// Inner tiles come through a TMA ring of kYStages stages (8 at d = 64, 4 at d = 128): stage
+// t % kYStages is refilled with tile t + kYStages once tile t's accumulating MMAs are done.
 template <int D, bool BF16, bool KM>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     lca_bwd_main(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
@@ -176,12 +177,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* sY = smem + C::kOffY;
     float* sStat = reinterpret_cast<float*>(smem + C::kOffStat);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+    constexpr int kYStages = C::kYStages;
     uint64_t* bar_x = bars + 0;
-    uint64_t* bar_y = bars + 1;   // [kYStages]
-    uint64_t* s_full = bars + 4;  // [2] S/dP of the buffer computed (and, dK/dV, its stats staged)
-    uint64_t* p_full = bars + 6;  // [2] P/dS of the buffer written
-    uint64_t* bar_o = bars + 8;   // the accumulating MMAs of the latest tile finished (one per tile)
-    uint64_t* st_full = bars + 9; // [kYStages] dK/dV kernel: LSE and D of the stage's inner rows staged
+    uint64_t* s_full = bars + 1;  // [2] S/dP of the buffer computed
+    uint64_t* p_full = bars + 3;  // [2] P/dS of the buffer written
+    uint64_t* bar_o = bars + 5;   // the accumulating MMAs of the latest tile finished (one per tile)
+    uint64_t* bar_y = bars + 6;   // [kYStages] the stage's inner tiles loaded
+    uint64_t* st_full = bars + 6 + kYStages;  // [kYStages] dK/dV kernel: the stage's LSE and D staged
     uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
 
@@ -231,8 +233,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             bwd_load_tile<D>(y, C::kYPanel, cont ? &tm_y1 : &tm_y1g, &bar_y[st], !cont, r0, un.bh);
             bwd_load_tile<D>(y + C::kYBytes, C::kYPanel, cont ? &tm_y2 : &tm_y2g, &bar_y[st], !cont, r0, un.bh);
         };
-        // dK/dV kernel: LSE and D of tile t's inner (query) rows into stage t % 3 (all lanes),
-        // staged with the tile's loads
+        // dK/dV kernel: LSE and D of tile t's inner (query) rows into stage t % kYStages (all
+        // lanes), staged with the tile's loads
         auto stage_stats = [&](int t) {
             if constexpr (KM) {
                 float* st = sStat + (t % kYStages) * 2 * kBN;
@@ -325,17 +327,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         for (int t = 0; t < T; ++t) {
             // tile t - 1's accumulating MMAs (every completion of bar_o is waited, in order):
-            // then buffer (t + 1) & 1 and tile t - 1's stage are free
+            // then buffer (t + 1) & 1 and tile t - 1's stage are free, and the stage takes
+            // tile t - 1 + kYStages
+            const int refill = t - 1 + kYStages;
             if (lane == 0 && t >= 1) {
                 wait(bar_o, (t - 1) & 1);
-                if (ok && t + 2 < T) load_inner(t + 2);
+                if (ok && refill < T) load_inner(refill);
             }
             __syncwarp();
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             // the stage's stats are read by the P / dS warps until tile t - 1's p_full, before
             // its accumulating MMAs were issued
-            if (t >= 1 && t + 2 < T) stage_stats(t + 2);
+            if (t >= 1 && refill < T) stage_stats(refill);
             if (t + 1 < T) {
                 if (lane == 0) {
                     wait(&bar_y[(t + 1) % kYStages], ((t + 1) / kYStages) & 1);
