@@ -47,7 +47,7 @@ namespace {
 constexpr int kBM = 128;                 // rows of an outer tile
 constexpr int kBN = 64;                  // rows of an inner tile
 constexpr int kCalcThreads = 512;        // four warpgroups: warpgroup q owns columns [16 q, 16 q + 16) of a tile
-constexpr int kBwdThreads = kCalcThreads + 32;  // plus the issuing warp
+constexpr int kBwdThreads = kCalcThreads + 96;  // plus three control warps (S/dP issue, accumulate issue, loads)
 constexpr uint32_t kBwdTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -61,7 +61,7 @@ struct BwdCfg {
     static constexpr int kOffX = 0;                              // X1, X2
     static constexpr int kOffY = 2 * kXBytes;                    // [kYStages][Y1, Y2]
     static constexpr int kOffStat = kOffY + kYStages * 2 * kYBytes;  // [kYStages][2 (lse2, D)][kBN] floats
-    static constexpr int kNumBars = 6 + 2 * kYStages;
+    static constexpr int kNumBars = 11 + 3 * kYStages;
     static constexpr int kOffBar = kOffStat + kYStages * 2 * kBN * 4;  // kNumBars barriers
     static constexpr int kOffMisc = kOffBar + kNumBars * 8;            // TMEM base, abort flag
     static constexpr int kUsed = kOffMisc + 16;
@@ -153,16 +153,22 @@ __device__ __forceinline__ void bwd_load_tile(uint8_t* dst, int panel, const CUt
     }
 }
 
-// Warp 8 issues (its lane 0 drives TMA and tcgen05; for the dK/dV kernel its 32 lanes also
-// stage the inner rows' LSE and D); warps 0-7 turn S and dP into P and dS.  Per inner tile t
-// (kBN rows), S / dP double-buffered in TMEM (buffer b = t & 1: S in columns
-// [128 b, 128 b + 64), dP in [128 b + 64, 128 b + 128)):
-//   issuer: S/dP of tile t + 1 as soon as tile t - 1's accumulating MMAs have finished (they
-//           read that buffer), so they run while warps 0-7 work on tile t; then, once P/dS of
-//           tile t are written (p_full), the accumulating TS MMAs of tile t;
-//   warps 0-7: wait for S/dP of tile t (s_full), write P and dS over them, signal p_full.
-// Inner tiles come through a TMA ring of kYStages stages (8 at d = 64, 4 at d = 128): stage
-// t % kYStages is refilled with tile t + kYStages once tile t's accumulating MMAs are done.
+// Warps 0-15 turn S and dP into P and dS; three control warps, each on its own SM
+// sub-partition, drive the rest (one lane each, except where noted):
+//   warp 16 (S issuer): S = X1 Y1^T and dP = X2 Y2^T of tile t + NB - 1 into TMEM buffer
+//           (t - 1) % NB as soon as tile t - 1's accumulating MMAs have freed it (buf_free), so
+//           NB - 1 tiles' S/dP run ahead of warps 0-15;
+//   warp 17 (accumulate issuer): once P/dS of tile t are written (p_full), dQ += dS Y1 (dQ
+//           kernel) or dV += P^T Y2 and dK += dS^T Y1 (dK/dV kernel), then commits that free
+//           the tile's buffer (buf_free) and its ring stage (stage_free);
+//   warp 18 (producer): the outer tile, and the inner tiles through a TMA ring of kYStages
+//           stages (8 at d = 64, 4 at d = 128), stage t % kYStages refilled with tile
+//           t + kYStages once tile t's accumulating MMAs are done; for the dK/dV kernel its 32
+//           lanes also stage the inner rows' LSE and D.
+// S / dP sit in one of NB TMEM buffers (NB = 3, or 2 for the d = 128 dK/dV kernel, whose
+// accumulators take 256 columns; buffer b = t % NB: S in columns [128 b, 128 b + 64), dP in
+// [128 b + 64, 128 b + 128)).  Every barrier is waited once per phase, in order, and none can
+// complete its next phase before its waiter has passed the current one.
 template <int D, bool BF16, bool KM>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     lca_bwd_main(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
@@ -178,12 +184,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     float* sStat = reinterpret_cast<float*>(smem + C::kOffStat);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
     constexpr int kYStages = C::kYStages;
+    constexpr int NB = (KM && D == 128) ? 2 : 3;  // S/dP buffers in TMEM
     uint64_t* bar_x = bars + 0;
-    uint64_t* s_full = bars + 1;  // [2] S/dP of the buffer computed
-    uint64_t* p_full = bars + 3;  // [2] P/dS of the buffer written
-    uint64_t* bar_o = bars + 5;   // the accumulating MMAs of the latest tile finished (one per tile)
-    uint64_t* bar_y = bars + 6;   // [kYStages] the stage's inner tiles loaded
-    uint64_t* st_full = bars + 6 + kYStages;  // [kYStages] dK/dV kernel: the stage's LSE and D staged
+    uint64_t* s_full = bars + 1;     // [NB] S/dP of the buffer computed
+    uint64_t* p_full = bars + 4;     // [NB] P/dS of the buffer written
+    uint64_t* buf_free = bars + 7;   // [NB] the buffer's accumulating MMAs finished
+    uint64_t* bar_done = bars + 10;  // every accumulating MMA finished
+    uint64_t* bar_y = bars + 11;     // [kYStages] the stage's inner tiles loaded
+    uint64_t* st_full = bars + 11 + kYStages;      // [kYStages] dK/dV kernel: the stage's LSE and D staged
+    uint64_t* stage_free = bars + 11 + 2 * kYStages;  // [kYStages] the stage's accumulating MMAs finished
     uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
 
@@ -196,12 +205,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (tid == 0) {
         ptx::mbar_init(bar_x, 1);
         for (int i = 0; i < kYStages; ++i) ptx::mbar_init(&bar_y[i], 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NB; ++i) {
             ptx::mbar_init(&s_full[i], 1);
             ptx::mbar_init(&p_full[i], kCalcThreads / 32);
+            ptx::mbar_init(&buf_free[i], 1);
         }
-        ptx::mbar_init(bar_o, 1);
-        for (int i = 0; i < kYStages; ++i) ptx::mbar_init(&st_full[i], 32);  // the issuing warp's lanes
+        ptx::mbar_init(bar_done, 1);
+        for (int i = 0; i < kYStages; ++i) {
+            ptx::mbar_init(&st_full[i], 32);  // the producer warp's lanes
+            ptx::mbar_init(&stage_free[i], 1);
+        }
         *abort_flag = 0;
         ptx::fence_mbar_init();
     }
@@ -213,7 +226,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *sTmem;
-    constexpr uint32_t kColA = 256, kColB = 256 + D;
+    constexpr uint32_t kColA = 128 * NB, kColB = 128 * NB + D;
+    static_assert(128 * NB + (KM ? 2 * D : D) <= (int)kBwdTmemCols, "TMEM columns");
 
     bool ok = true;
     auto wait = [&](uint64_t* bar, int parity) {
@@ -222,8 +236,84 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                             p.timeout_ns);
     };
 
+    const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
     if (warp == kCalcThreads / 32) {
-        // ============================================================ issuing warp
+        // ============================================================ S issuer
+        const uint32_t idesc_s = ptx::idesc_f16(BF16, kBM, kBN, false);
+        // S = X1 Y1^T and dP = X2 Y2^T of tile t into buffer t % NB
+        auto issue_s = [&](int t) {
+            const int st = t % kYStages;
+            const uint32_t col = (uint32_t)(t % NB) * 128;
+            const uint32_t xs = ptx::smem_u32(sX);
+            const uint32_t ys = ptx::smem_u32(sY + st * 2 * C::kYBytes);
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const uint32_t alo = ptx::smem_desc_sw128_lo(xs + m * C::kXBytes, 0);
+                const uint32_t blo = ptx::smem_desc_sw128_lo(ys + m * C::kYBytes, 0);
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    const uint32_t aoff = ((ks >> 2) * C::kXPanel + (ks & 3) * 32) >> 4;
+                    const uint32_t boff = ((ks >> 2) * C::kYPanel + (ks & 3) * 32) >> 4;
+                    ptx::mma_f16_ss(tmem + col + m * kBN, ptx::desc_join(alo + aoff, dhi),
+                                    ptx::desc_join(blo + boff, dhi), idesc_s, ks > 0 ? 1u : 0u);
+                }
+            }
+            ptx::mma_commit(&s_full[t % NB]);
+        };
+        if (lane == 0 && T > 0) {
+            wait(bar_x, 0);
+            for (int t = 0; t < T && ok; ++t) {
+                // tile t goes into buffer t % NB, free at first, then once tile t - NB's
+                // accumulating MMAs are done
+                if (t >= NB) wait(&buf_free[t % NB], ((t - NB) / NB) & 1);
+                wait(&bar_y[t % kYStages], (t / kYStages) & 1);
+                if (!ok) break;
+                ptx::tc_fence_after();
+                issue_s(t);
+            }
+        }
+    } else if (warp == kCalcThreads / 32 + 1) {
+        // ============================================================ accumulate issuer
+        const uint32_t idesc_acc = ptx::idesc_f16(BF16, kBM, D, true);
+        if (lane == 0 && T > 0) {
+            for (int t = 0; t < T; ++t) {
+                wait(&p_full[t % NB], (t / NB) & 1);
+                // the stage's loads (already complete: S/dP of the tile read them)
+                wait(&bar_y[t % kYStages], (t / kYStages) & 1);
+                if (!ok) break;
+                ptx::tc_fence_after();
+                // dQ += dS Y1 (dQ kernel); dV += P^T Y2, dK += dS^T Y1 (dK/dV kernel)
+                const uint32_t ys = ptx::smem_u32(sY + (t % kYStages) * 2 * C::kYBytes);
+                const uint32_t y1lo = ptx::smem_desc_sw128_lo(ys, C::kYPanel);
+                const uint32_t y2lo = ptx::smem_desc_sw128_lo(ys + C::kYBytes, C::kYPanel);
+                const uint32_t col_s = (uint32_t)(t % NB) * 128, col_dp = col_s + kBN;
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; ++kk) {
+                    const int key = 16 * kk;
+                    const uint32_t acol = key;  // keys [key, key + 16): 8 packed columns from column key
+                    const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+                    const uint32_t boff = (uint32_t)(key * 128) >> 4;
+                    if constexpr (KM) {
+                        ptx::mma_f16_ts(tmem + kColA, tmem + col_s + acol, ptx::desc_join(y2lo + boff, dhi),
+                                        idesc_acc, acc);
+                        ptx::mma_f16_ts(tmem + kColB, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi),
+                                        idesc_acc, acc);
+                    } else {
+                        ptx::mma_f16_ts(tmem + kColA, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi),
+                                        idesc_acc, acc);
+                    }
+                }
+                ptx::mma_commit(&buf_free[t % NB]);
+                ptx::mma_commit(&stage_free[t % kYStages]);
+            }
+            // every accumulating MMA (a commit covers every earlier MMA of the thread)
+            if (ok) {
+                ptx::mma_commit(bar_done);
+                wait(bar_done, 0);
+            }
+        }
+    } else if (warp == kCalcThreads / 32 + 2) {
+        // ============================================================ producer
         auto load_inner = [&](int t) {  // lane 0
             const int st = t % kYStages;
             uint8_t* y = sY + st * 2 * C::kYBytes;
@@ -233,8 +323,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             bwd_load_tile<D>(y, C::kYPanel, cont ? &tm_y1 : &tm_y1g, &bar_y[st], !cont, r0, un.bh);
             bwd_load_tile<D>(y + C::kYBytes, C::kYPanel, cont ? &tm_y2 : &tm_y2g, &bar_y[st], !cont, r0, un.bh);
         };
-        // dK/dV kernel: LSE and D of tile t's inner (query) rows into stage t % kYStages (all
-        // lanes), staged with the tile's loads
+        // dK/dV kernel: LSE and D of tile t's inner (query) rows into stage t % kYStages (all lanes)
         auto stage_stats = [&](int t) {
             if constexpr (KM) {
                 float* st = sStat + (t % kYStages) * 2 * kBN;
@@ -260,53 +349,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 ptx::mbar_arrive(&st_full[t % kYStages]);  // releases this lane's writes
             }
         };
-        const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
-        const uint32_t idesc_s = ptx::idesc_f16(BF16, kBM, kBN, false);
-        const uint32_t idesc_acc = ptx::idesc_f16(BF16, kBM, D, true);
-        // S = X1 Y1^T and dP = X2 Y2^T of tile t into buffer t & 1 (lane 0)
-        auto issue_s = [&](int t) {
-            const int st = t % kYStages;
-            const uint32_t col = (uint32_t)(t & 1) * 128;
-            const uint32_t xs = ptx::smem_u32(sX);
-            const uint32_t ys = ptx::smem_u32(sY + st * 2 * C::kYBytes);
-#pragma unroll
-            for (int m = 0; m < 2; ++m) {
-                const uint32_t alo = ptx::smem_desc_sw128_lo(xs + m * C::kXBytes, 0);
-                const uint32_t blo = ptx::smem_desc_sw128_lo(ys + m * C::kYBytes, 0);
-#pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t aoff = ((ks >> 2) * C::kXPanel + (ks & 3) * 32) >> 4;
-                    const uint32_t boff = ((ks >> 2) * C::kYPanel + (ks & 3) * 32) >> 4;
-                    ptx::mma_f16_ss(tmem + col + m * kBN, ptx::desc_join(alo + aoff, dhi),
-                                    ptx::desc_join(blo + boff, dhi), idesc_s, ks > 0 ? 1u : 0u);
-                }
-            }
-            ptx::mma_commit(&s_full[t & 1]);
-        };
-        // dQ += dS Y1 (dQ kernel); dV += P^T Y2, dK += dS^T Y1 (dK/dV kernel) for tile t (lane 0)
-        auto issue_acc = [&](int t) {
-            const uint32_t ys = ptx::smem_u32(sY + (t % kYStages) * 2 * C::kYBytes);
-            const uint32_t y1lo = ptx::smem_desc_sw128_lo(ys, C::kYPanel);
-            const uint32_t y2lo = ptx::smem_desc_sw128_lo(ys + C::kYBytes, C::kYPanel);
-            const uint32_t col_s = (uint32_t)(t & 1) * 128, col_dp = col_s + kBN;
-#pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-                const int key = 16 * kk;
-                const uint32_t acol = key;  // keys [key, key + 16): 8 packed columns from column key
-                const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-                const uint32_t boff = (uint32_t)(key * 128) >> 4;
-                if constexpr (KM) {
-                    ptx::mma_f16_ts(tmem + kColA, tmem + col_s + acol, ptx::desc_join(y2lo + boff, dhi), idesc_acc, acc);
-                    ptx::mma_f16_ts(tmem + kColB, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi), idesc_acc,
-                                    acc);
-                } else {
-                    ptx::mma_f16_ts(tmem + kColA, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi), idesc_acc,
-                                    acc);
-                }
-            }
-            ptx::mma_commit(bar_o);
-        };
-
         if (lane == 0) {
             ptx::prefetch_tmap(&tm_x1);
             ptx::prefetch_tmap(&tm_y1);
@@ -317,51 +359,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int t = 0; t < kYStages && t < T; ++t) load_inner(t);
         }
         for (int t = 0; t < kYStages && t < T; ++t) stage_stats(t);
-        if (lane == 0 && T > 0) {
-            wait(bar_x, 0);
-            wait(&bar_y[0], 0);
-            if (ok) {
-                ptx::tc_fence_after();
-                issue_s(0);
-            }
-        }
-        for (int t = 0; t < T; ++t) {
-            // tile t - 1's accumulating MMAs (every completion of bar_o is waited, in order):
-            // then buffer (t + 1) & 1 and tile t - 1's stage are free, and the stage takes
-            // tile t - 1 + kYStages
-            const int refill = t - 1 + kYStages;
-            if (lane == 0 && t >= 1) {
-                wait(bar_o, (t - 1) & 1);
-                if (ok && refill < T) load_inner(refill);
-            }
+        // stage t % kYStages takes tile t + kYStages once tile t's accumulating MMAs are done
+        // (the P / dS warps read the stage's stats before tile t's p_full, so before those MMAs)
+        for (int t = 0; t + kYStages < T; ++t) {
+            if (lane == 0) wait(&stage_free[t % kYStages], (t / kYStages) & 1);
             __syncwarp();
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
-            // the stage's stats are read by the P / dS warps until tile t - 1's p_full, before
-            // its accumulating MMAs were issued
-            if (t >= 1 && refill < T) stage_stats(refill);
-            if (t + 1 < T) {
-                if (lane == 0) {
-                    wait(&bar_y[(t + 1) % kYStages], ((t + 1) / kYStages) & 1);
-                    if (ok) {
-                        ptx::tc_fence_after();
-                        issue_s(t + 1);
-                    }
-                }
-            }
-            if (lane == 0) {
-                wait(&p_full[t & 1], (t >> 1) & 1);
-                if (ok) {
-                    ptx::tc_fence_after();
-                    issue_acc(t);
-                }
-            }
-            __syncwarp();
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            if (!ok) break;
+            if (lane == 0) load_inner(t + kYStages);
+            stage_stats(t + kYStages);
         }
-        // the last accumulating MMAs (a commit covers every earlier MMA of the thread)
-        if (lane == 0 && ok && T > 0) wait(bar_o, (T - 1) & 1);
     } else {
         // ============================================================ P / dS warps
         const int r = tid & (kBM - 1);  // outer row <-> TMEM lane
@@ -387,7 +394,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         };
         uint32_t gnext = T > 0 ? gbits_of(0) : 0u;
         for (int t = 0; t < T; ++t) {
-            const int b = t & 1;
+            const int b = t % NB;
             const bool cont = t < un.n_cont;
             const int tile0 = cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
             const uint32_t gbits = gnext;
@@ -407,7 +414,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 hi = row_ok ? p.num_global - 1 - tile0 : -1;
             }
             const uint32_t bits = range_bits(c0, lo, hi) & ~gbits;
-            wait(&s_full[b], (t >> 1) & 1);
+            wait(&s_full[b], (t / NB) & 1);
             if constexpr (KM) wait(&st_full[t % kYStages], (t / kYStages) & 1);
             ok = __all_sync(0xffffffffu, ok);  // warp-uniform, so the __syncwarp below is reached by all
             if (!ok) break;
