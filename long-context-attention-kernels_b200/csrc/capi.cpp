@@ -1640,6 +1640,7 @@ int lca_swa_backward(const void* q, const void* k, const void* v, const float* o
     const long long units = (long long)bp.n_band_units + (long long)P.bh * B.g_tiles * B.n_splits;
     if (units > INT_MAX) return fail(LCA_ERR_UNSUPPORTED, "problem too large (%lld backward units)", units);
     bp.n_units = (int)units;
+    bp.grid = g_dev_sms[dev] > 0 ? g_dev_sms[dev] : 148;
     bp.scale = scale;
     bp.scale_log2 = scale * 1.4426950408889634f;
     bp.gidx = gidx;

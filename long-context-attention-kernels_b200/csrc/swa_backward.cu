@@ -22,14 +22,14 @@
 //                      roles of rows and keys exchanged.
 //   lca_bwd_reduce   : sums the split partials into the global tokens' rows.
 //
-// One CTA = one warpgroup (128 threads; thread r <-> TMEM lane r <-> outer row r).  Per inner
-// tile: thread 0 issues S = X1 Y1^T and dP = X2 Y2^T (tcgen05.mma, SS, both operands K-major
-// from shared memory, 128 x 128 fp32 in TMEM); every thread turns its row of S and dP into P
-// and dS, packs them to 16-bit pairs and stores them back over S and dP (tcgen05.st); thread
-// 0 then issues the TS MMAs that accumulate in TMEM (dQ += dS Y1; or dV += P^T Y2 and
-// dK += dS^T Y1), with Y1 / Y2 read as MN-major B operands from the same shared tiles.  The
-// inner tiles are double-buffered and loaded by TMA.  TMEM columns: S [0, 128), dP [128, 256),
-// accumulators [256, 256 + D) and [256 + D, 256 + 2D).
+// The main kernels run a persistent grid (one CTA per SM, units taken round-robin).  Per
+// 64-row inner tile, S = X1 Y1^T and dP = X2 Y2^T (tcgen05.mma, SS, both operands K-major from
+// shared memory, 128 x 64 fp32 in TMEM) are turned by 16 warps into P and dS, packed to 16-bit
+// pairs and stored back over S and dP (tcgen05.st); the TS MMAs then accumulate in TMEM
+// (dQ += dS Y1; or dV += P^T Y2 and dK += dS^T Y1), reading Y1 / Y2 as MN-major B operands from
+// the same shared tiles.  Three control warps issue the S/dP MMAs, issue the accumulating MMAs
+// and load (TMA), each on its own SM sub-partition: a tcgen05.mma of M = 128, K = 16 takes ~96
+// cycles of issue at N = 64, so one thread issuing both kinds set the pace.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -54,14 +54,15 @@ constexpr float kLog2e = 1.4426950408889634f;
 template <int D>
 struct BwdCfg {
     static constexpr int kYStages = D == 64 ? 8 : 4;  // inner tiles in flight (TMA ring)
+    static constexpr int kXBufs = D == 64 ? 2 : 1;    // outer tiles in flight (the next unit's)
     static constexpr int kXPanel = kBM * 128;       // 128 rows x 128 bytes
     static constexpr int kYPanel = kBN * 128;       // 64 rows x 128 bytes
     static constexpr int kXBytes = kBM * D * 2;     // one outer tile: D / 64 panels
     static constexpr int kYBytes = kBN * D * 2;     // one inner tile
-    static constexpr int kOffX = 0;                              // X1, X2
-    static constexpr int kOffY = 2 * kXBytes;                    // [kYStages][Y1, Y2]
+    static constexpr int kOffX = 0;                              // [kXBufs][X1, X2]
+    static constexpr int kOffY = kXBufs * 2 * kXBytes;           // [kYStages][Y1, Y2]
     static constexpr int kOffStat = kOffY + kYStages * 2 * kYBytes;  // [kYStages][2 (lse2, D)][kBN] floats
-    static constexpr int kNumBars = 11 + 3 * kYStages;
+    static constexpr int kNumBars = 2 * kXBufs + 11 + 3 * kYStages;
     static constexpr int kOffBar = kOffStat + kYStages * 2 * kBN * 4;  // kNumBars barriers
     static constexpr int kOffMisc = kOffBar + kNumBars * 8;            // TMEM base, abort flag
     static constexpr int kUsed = kOffMisc + 16;
@@ -153,20 +154,26 @@ __device__ __forceinline__ void bwd_load_tile(uint8_t* dst, int panel, const CUt
     }
 }
 
-// Warps 0-15 turn S and dP into P and dS; three control warps, each on its own SM
-// sub-partition, drive the rest (one lane each, except where noted):
-//   warp 16 (S issuer): S = X1 Y1^T and dP = X2 Y2^T of tile t + NB - 1 into TMEM buffer
-//           (t - 1) % NB as soon as tile t - 1's accumulating MMAs have freed it (buf_free), so
-//           NB - 1 tiles' S/dP run ahead of warps 0-15;
-//   warp 17 (accumulate issuer): once P/dS of tile t are written (p_full), dQ += dS Y1 (dQ
+// A persistent grid: CTA c takes units c, c + gridDim.x, ... (the longer global units come
+// first, so the short band units fill the tail).  Warps 0-15 turn S and dP into P and dS and
+// write each unit's result; three control warps, each on its own SM sub-partition, drive the
+// rest (one lane each, except where noted):
+//   warp 16 (S issuer): S = X1 Y1^T and dP = X2 Y2^T of every inner tile into TMEM buffer
+//           g % NB (g counts the CTA's inner tiles across its units) once that buffer's
+//           previous accumulating MMAs have finished (buf_free), so S/dP run up to NB - 1
+//           tiles ahead of warps 0-15, into the next unit too;
+//   warp 17 (accumulate issuer): once P/dS of a tile are written (p_full), dQ += dS Y1 (dQ
 //           kernel) or dV += P^T Y2 and dK += dS^T Y1 (dK/dV kernel), then commits that free
-//           the tile's buffer (buf_free) and its ring stage (stage_free);
-//   warp 18 (producer): the outer tile, and the inner tiles through a TMA ring of kYStages
-//           stages (8 at d = 64, 4 at d = 128), stage t % kYStages refilled with tile
-//           t + kYStages once tile t's accumulating MMAs are done; for the dK/dV kernel its 32
-//           lanes also stage the inner rows' LSE and D.
+//           the tile's buffer (buf_free) and ring stage (stage_free); a unit's first MMAs wait
+//           until the previous unit's accumulators have been read out (acc_free), and its
+//           last commit tells warps 0-15 that the accumulators are complete (acc_full);
+//   warp 18 (producer): the outer tiles (kXBufs buffers, so the next unit's loads early at
+//           d = 64) and the inner tiles through a TMA ring of kYStages stages (8 at d = 64, 4
+//           at d = 128), stage g % kYStages refilled with tile g + kYStages once tile g's
+//           accumulating MMAs are done; for the dK/dV kernel its 32 lanes also stage the inner
+//           rows' LSE and D.
 // S / dP sit in one of NB TMEM buffers (NB = 3, or 2 for the d = 128 dK/dV kernel, whose
-// accumulators take 256 columns; buffer b = t % NB: S in columns [128 b, 128 b + 64), dP in
+// accumulators take 256 columns; S in columns [128 b, 128 b + 64), dP in
 // [128 b + 64, 128 b + 128)).  Every barrier is waited once per phase, in order, and none can
 // complete its next phase before its waiter has passed the current one.
 template <int D, bool BF16, bool KM>
@@ -184,34 +191,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     float* sStat = reinterpret_cast<float*>(smem + C::kOffStat);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
     constexpr int kYStages = C::kYStages;
+    constexpr int NX = C::kXBufs;
     constexpr int NB = (KM && D == 128) ? 2 : 3;  // S/dP buffers in TMEM
-    uint64_t* bar_x = bars + 0;
-    uint64_t* s_full = bars + 1;     // [NB] S/dP of the buffer computed
-    uint64_t* p_full = bars + 4;     // [NB] P/dS of the buffer written
-    uint64_t* buf_free = bars + 7;   // [NB] the buffer's accumulating MMAs finished
-    uint64_t* bar_done = bars + 10;  // every accumulating MMA finished
-    uint64_t* bar_y = bars + 11;     // [kYStages] the stage's inner tiles loaded
-    uint64_t* st_full = bars + 11 + kYStages;      // [kYStages] dK/dV kernel: the stage's LSE and D staged
-    uint64_t* stage_free = bars + 11 + 2 * kYStages;  // [kYStages] the stage's accumulating MMAs finished
+    uint64_t* bar_x = bars;                 // [NX] the buffer's outer tiles loaded
+    uint64_t* x_free = bars + NX;           // [NX] every S/dP MMA reading the buffer finished
+    uint64_t* s_full = bars + 2 * NX;       // [NB] S/dP of the buffer computed
+    uint64_t* p_full = s_full + 3;          // [NB] P/dS of the buffer written
+    uint64_t* buf_free = p_full + 3;        // [NB] the buffer's accumulating MMAs finished
+    uint64_t* acc_full = buf_free + 3;      // the unit's accumulating MMAs finished
+    uint64_t* acc_free = acc_full + 1;      // the unit's accumulators read out
+    uint64_t* bar_y = acc_free + 1;         // [kYStages] the stage's inner tiles loaded
+    uint64_t* st_full = bar_y + kYStages;   // [kYStages] dK/dV kernel: the stage's LSE and D staged
+    uint64_t* stage_free = st_full + kYStages;  // [kYStages] the stage's accumulating MMAs finished
     uint32_t* sTmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const BwdUnit un = bwd_decode(p, blockIdx.x);
-    const int T = un.n_cont + un.n_comp;
+    const int u_first = blockIdx.x, u_step = gridDim.x;
 
     if (tid == 0) {
-        ptx::mbar_init(bar_x, 1);
-        for (int i = 0; i < kYStages; ++i) ptx::mbar_init(&bar_y[i], 1);
+        for (int i = 0; i < NX; ++i) {
+            ptx::mbar_init(&bar_x[i], 1);
+            ptx::mbar_init(&x_free[i], 1);
+        }
         for (int i = 0; i < NB; ++i) {
             ptx::mbar_init(&s_full[i], 1);
             ptx::mbar_init(&p_full[i], kCalcThreads / 32);
             ptx::mbar_init(&buf_free[i], 1);
         }
-        ptx::mbar_init(bar_done, 1);
+        ptx::mbar_init(acc_full, 1);
+        ptx::mbar_init(acc_free, kCalcThreads / 32);
         for (int i = 0; i < kYStages; ++i) {
+            ptx::mbar_init(&bar_y[i], 1);
             ptx::mbar_init(&st_full[i], 32);  // the producer warp's lanes
             ptx::mbar_init(&stage_free[i], 1);
         }
@@ -235,100 +248,99 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = ptx::mbar_wait(bar, (uint32_t)parity & 1u, abort_flag, p.err, LCA_DEVERR_TIMEOUT_BACKWARD,
                             p.timeout_ns);
     };
+    // inner tile t of unit un: contiguous rows inner0 + kBN t, or compact tile t - n_cont
+    auto tile_row0 = [&](const BwdUnit& un, int t) {
+        return t < un.n_cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
+    };
 
     const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
     if (warp == kCalcThreads / 32) {
         // ============================================================ S issuer
         const uint32_t idesc_s = ptx::idesc_f16(BF16, kBM, kBN, false);
-        // S = X1 Y1^T and dP = X2 Y2^T of tile t into buffer t % NB
-        auto issue_s = [&](int t) {
-            const int st = t % kYStages;
-            const uint32_t col = (uint32_t)(t % NB) * 128;
-            const uint32_t xs = ptx::smem_u32(sX);
-            const uint32_t ys = ptx::smem_u32(sY + st * 2 * C::kYBytes);
+        if (lane == 0) {
+            int g = 0;
+            for (int k = 0, u = u_first; u < p.n_units && ok; ++k, u += u_step) {
+                const BwdUnit un = bwd_decode(p, u);
+                const int T = un.n_cont + un.n_comp;
+                const int xb = k % NX;
+                wait(&bar_x[xb], (k / NX) & 1);
+                const uint32_t xs = ptx::smem_u32(sX + xb * 2 * C::kXBytes);
+                for (int t = 0; t < T; ++t, ++g) {
+                    if (g >= NB) wait(&buf_free[g % NB], ((g - NB) / NB) & 1);
+                    wait(&bar_y[g % kYStages], (g / kYStages) & 1);
+                    if (!ok) break;
+                    ptx::tc_fence_after();
+                    const uint32_t col = (uint32_t)(g % NB) * 128;
+                    const uint32_t ys = ptx::smem_u32(sY + (g % kYStages) * 2 * C::kYBytes);
 #pragma unroll
-            for (int m = 0; m < 2; ++m) {
-                const uint32_t alo = ptx::smem_desc_sw128_lo(xs + m * C::kXBytes, 0);
-                const uint32_t blo = ptx::smem_desc_sw128_lo(ys + m * C::kYBytes, 0);
+                    for (int m = 0; m < 2; ++m) {
+                        const uint32_t alo = ptx::smem_desc_sw128_lo(xs + m * C::kXBytes, 0);
+                        const uint32_t blo = ptx::smem_desc_sw128_lo(ys + m * C::kYBytes, 0);
 #pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t aoff = ((ks >> 2) * C::kXPanel + (ks & 3) * 32) >> 4;
-                    const uint32_t boff = ((ks >> 2) * C::kYPanel + (ks & 3) * 32) >> 4;
-                    ptx::mma_f16_ss(tmem + col + m * kBN, ptx::desc_join(alo + aoff, dhi),
-                                    ptx::desc_join(blo + boff, dhi), idesc_s, ks > 0 ? 1u : 0u);
+                        for (int ks = 0; ks < D / 16; ++ks) {
+                            const uint32_t aoff = ((ks >> 2) * C::kXPanel + (ks & 3) * 32) >> 4;
+                            const uint32_t boff = ((ks >> 2) * C::kYPanel + (ks & 3) * 32) >> 4;
+                            ptx::mma_f16_ss(tmem + col + m * kBN, ptx::desc_join(alo + aoff, dhi),
+                                            ptx::desc_join(blo + boff, dhi), idesc_s, ks > 0 ? 1u : 0u);
+                        }
+                    }
+                    ptx::mma_commit(&s_full[g % NB]);
                 }
-            }
-            ptx::mma_commit(&s_full[t % NB]);
-        };
-        if (lane == 0 && T > 0) {
-            wait(bar_x, 0);
-            for (int t = 0; t < T && ok; ++t) {
-                // tile t goes into buffer t % NB, free at first, then once tile t - NB's
-                // accumulating MMAs are done
-                if (t >= NB) wait(&buf_free[t % NB], ((t - NB) / NB) & 1);
-                wait(&bar_y[t % kYStages], (t / kYStages) & 1);
                 if (!ok) break;
-                ptx::tc_fence_after();
-                issue_s(t);
+                ptx::mma_commit(&x_free[xb]);  // the unit's outer tile is no longer read
             }
         }
     } else if (warp == kCalcThreads / 32 + 1) {
         // ============================================================ accumulate issuer
         const uint32_t idesc_acc = ptx::idesc_f16(BF16, kBM, D, true);
-        if (lane == 0 && T > 0) {
-            for (int t = 0; t < T; ++t) {
-                wait(&p_full[t % NB], (t / NB) & 1);
-                // the stage's loads (already complete: S/dP of the tile read them)
-                wait(&bar_y[t % kYStages], (t / kYStages) & 1);
-                if (!ok) break;
-                ptx::tc_fence_after();
-                // dQ += dS Y1 (dQ kernel); dV += P^T Y2, dK += dS^T Y1 (dK/dV kernel)
-                const uint32_t ys = ptx::smem_u32(sY + (t % kYStages) * 2 * C::kYBytes);
-                const uint32_t y1lo = ptx::smem_desc_sw128_lo(ys, C::kYPanel);
-                const uint32_t y2lo = ptx::smem_desc_sw128_lo(ys + C::kYBytes, C::kYPanel);
-                const uint32_t col_s = (uint32_t)(t % NB) * 128, col_dp = col_s + kBN;
+        if (lane == 0) {
+            int g = 0;
+            for (int k = 0, u = u_first; u < p.n_units && ok; ++k, u += u_step) {
+                const BwdUnit un = bwd_decode(p, u);
+                const int T = un.n_cont + un.n_comp;
+                if (k >= 1) wait(acc_free, (k - 1) & 1);  // the previous unit's accumulators read out
+                for (int t = 0; t < T; ++t, ++g) {
+                    wait(&p_full[g % NB], (g / NB) & 1);
+                    // the stage's loads (already complete: S/dP of the tile read them)
+                    wait(&bar_y[g % kYStages], (g / kYStages) & 1);
+                    if (!ok) break;
+                    ptx::tc_fence_after();
+                    // dQ += dS Y1 (dQ kernel); dV += P^T Y2, dK += dS^T Y1 (dK/dV kernel)
+                    const uint32_t ys = ptx::smem_u32(sY + (g % kYStages) * 2 * C::kYBytes);
+                    const uint32_t y1lo = ptx::smem_desc_sw128_lo(ys, C::kYPanel);
+                    const uint32_t y2lo = ptx::smem_desc_sw128_lo(ys + C::kYBytes, C::kYPanel);
+                    const uint32_t col_s = (uint32_t)(g % NB) * 128, col_dp = col_s + kBN;
 #pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk) {
-                    const int key = 16 * kk;
-                    const uint32_t acol = key;  // keys [key, key + 16): 8 packed columns from column key
-                    const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-                    const uint32_t boff = (uint32_t)(key * 128) >> 4;
-                    if constexpr (KM) {
-                        ptx::mma_f16_ts(tmem + kColA, tmem + col_s + acol, ptx::desc_join(y2lo + boff, dhi),
-                                        idesc_acc, acc);
-                        ptx::mma_f16_ts(tmem + kColB, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi),
-                                        idesc_acc, acc);
-                    } else {
-                        ptx::mma_f16_ts(tmem + kColA, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi),
-                                        idesc_acc, acc);
+                    for (int kk = 0; kk < kBN / 16; ++kk) {
+                        const int key = 16 * kk;
+                        const uint32_t acol = key;  // keys [key, key + 16): 8 packed columns from column key
+                        const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t boff = (uint32_t)(key * 128) >> 4;
+                        if constexpr (KM) {
+                            ptx::mma_f16_ts(tmem + kColA, tmem + col_s + acol, ptx::desc_join(y2lo + boff, dhi),
+                                            idesc_acc, acc);
+                            ptx::mma_f16_ts(tmem + kColB, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi),
+                                            idesc_acc, acc);
+                        } else {
+                            ptx::mma_f16_ts(tmem + kColA, tmem + col_dp + acol, ptx::desc_join(y1lo + boff, dhi),
+                                            idesc_acc, acc);
+                        }
                     }
+                    ptx::mma_commit(&buf_free[g % NB]);
+                    ptx::mma_commit(&stage_free[g % kYStages]);
                 }
-                ptx::mma_commit(&buf_free[t % NB]);
-                ptx::mma_commit(&stage_free[t % kYStages]);
-            }
-            // every accumulating MMA (a commit covers every earlier MMA of the thread)
-            if (ok) {
-                ptx::mma_commit(bar_done);
-                wait(bar_done, 0);
+                if (!ok) break;
+                ptx::mma_commit(acc_full);  // every accumulating MMA of the unit (and before it)
             }
         }
     } else if (warp == kCalcThreads / 32 + 2) {
         // ============================================================ producer
-        auto load_inner = [&](int t) {  // lane 0
-            const int st = t % kYStages;
-            uint8_t* y = sY + st * 2 * C::kYBytes;
-            ptx::mbar_arrive_expect_tx(&bar_y[st], 2 * C::kYBytes);
-            const bool cont = t < un.n_cont;
-            const int r0 = cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
-            bwd_load_tile<D>(y, C::kYPanel, cont ? &tm_y1 : &tm_y1g, &bar_y[st], !cont, r0, un.bh);
-            bwd_load_tile<D>(y + C::kYBytes, C::kYPanel, cont ? &tm_y2 : &tm_y2g, &bar_y[st], !cont, r0, un.bh);
-        };
-        // dK/dV kernel: LSE and D of tile t's inner (query) rows into stage t % kYStages (all lanes)
-        auto stage_stats = [&](int t) {
+        // dK/dV kernel: LSE and D of inner tile t of unit un into stage g % kYStages (all lanes)
+        auto stage_stats = [&](const BwdUnit& un, int t, int g) {
             if constexpr (KM) {
-                float* st = sStat + (t % kYStages) * 2 * kBN;
+                float* st = sStat + (g % kYStages) * 2 * kBN;
                 const bool cont = t < un.n_cont;
-                const int tile0 = cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
+                const int tile0 = tile_row0(un, t);
 #pragma unroll
                 for (int h = 0; h < kBN / 32; ++h) {
                     const int c = h * 32 + lane;
@@ -346,28 +358,48 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     st[c] = l2;
                     st[kBN + c] = dd;
                 }
-                ptx::mbar_arrive(&st_full[t % kYStages]);  // releases this lane's writes
+                ptx::mbar_arrive(&st_full[g % kYStages]);  // releases this lane's writes
             }
         };
         if (lane == 0) {
             ptx::prefetch_tmap(&tm_x1);
             ptx::prefetch_tmap(&tm_y1);
-            ptx::mbar_arrive_expect_tx(bar_x, 2 * C::kXBytes);
-            bwd_load_tile<D>(sX, C::kXPanel, un.all ? &tm_x1g : &tm_x1, bar_x, un.all, un.outer0, un.bh);
-            bwd_load_tile<D>(sX + C::kXBytes, C::kXPanel, un.all ? &tm_x2g : &tm_x2, bar_x, un.all, un.outer0,
-                             un.bh);
-            for (int t = 0; t < kYStages && t < T; ++t) load_inner(t);
         }
-        for (int t = 0; t < kYStages && t < T; ++t) stage_stats(t);
-        // stage t % kYStages takes tile t + kYStages once tile t's accumulating MMAs are done
-        // (the P / dS warps read the stage's stats before tile t's p_full, so before those MMAs)
-        for (int t = 0; t + kYStages < T; ++t) {
-            if (lane == 0) wait(&stage_free[t % kYStages], (t / kYStages) & 1);
-            __syncwarp();
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        int g = 0;
+        for (int k = 0, u = u_first; u < p.n_units; ++k, u += u_step) {
+            const BwdUnit un = bwd_decode(p, u);
+            const int T = un.n_cont + un.n_comp;
+            const int xb = k % NX;
+            if (lane == 0) {
+                if (k >= NX) wait(&x_free[xb], ((k - NX) / NX) & 1);
+                if (ok) {
+                    uint8_t* x = sX + xb * 2 * C::kXBytes;
+                    ptx::mbar_arrive_expect_tx(&bar_x[xb], 2 * C::kXBytes);
+                    bwd_load_tile<D>(x, C::kXPanel, un.all ? &tm_x1g : &tm_x1, &bar_x[xb], un.all, un.outer0, un.bh);
+                    bwd_load_tile<D>(x + C::kXBytes, C::kXPanel, un.all ? &tm_x2g : &tm_x2, &bar_x[xb], un.all,
+                                     un.outer0, un.bh);
+                }
+            }
+            for (int t = 0; t < T; ++t, ++g) {
+                // stage g % kYStages is free once tile g - kYStages's accumulating MMAs are done
+                // (the P / dS warps read its stats before that tile's p_full, so before those MMAs)
+                if (lane == 0 && g >= kYStages) wait(&stage_free[g % kYStages], ((g - kYStages) / kYStages) & 1);
+                __syncwarp();
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                if (lane == 0) {
+                    const int st = g % kYStages;
+                    uint8_t* y = sY + st * 2 * C::kYBytes;
+                    ptx::mbar_arrive_expect_tx(&bar_y[st], 2 * C::kYBytes);
+                    const bool cont = t < un.n_cont;
+                    const int r0 = tile_row0(un, t);
+                    bwd_load_tile<D>(y, C::kYPanel, cont ? &tm_y1 : &tm_y1g, &bar_y[st], !cont, r0, un.bh);
+                    bwd_load_tile<D>(y + C::kYBytes, C::kYPanel, cont ? &tm_y2 : &tm_y2g, &bar_y[st], !cont, r0,
+                                     un.bh);
+                }
+                stage_stats(un, t, g);
+            }
             if (!ok) break;
-            if (lane == 0) load_inner(t + kYStages);
-            stage_stats(t + kYStages);
         }
     } else {
         // ============================================================ P / dS warps
@@ -375,147 +407,151 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int q = tid >> 7;         // column quarter of every inner tile
         const int c0 = q * 16;
         const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const int orow = un.outer0 + r;  // band: absolute row / key; all: compact index
-        const bool row_ok = un.all ? (orow < p.num_global) : (orow < p.n);
-        float row_lse2 = 0.f, row_d = 0.f;
-        if constexpr (!KM) {
-            if (row_ok) {
-                const size_t idx = un.all ? (size_t)un.bh * p.num_global + orow : (size_t)un.bh * p.n + orow;
-                row_lse2 = un.all ? __ldg(p.lse2g + idx) : __ldg(p.lse2 + idx);
-                row_d = un.all ? __ldg(p.dg + idx) : __ldg(p.dvec + idx);
+        int g = 0;
+        for (int k = 0, u = u_first; u < p.n_units && ok; ++k, u += u_step) {
+            const BwdUnit un = bwd_decode(p, u);
+            const int T = un.n_cont + un.n_comp;
+            const int orow = un.outer0 + r;  // band: absolute row / key; all: compact index
+            const bool row_ok = un.all ? (orow < p.num_global) : (orow < p.n);
+            float row_lse2 = 0.f, row_d = 0.f;
+            if constexpr (!KM) {
+                if (row_ok) {
+                    const size_t idx = un.all ? (size_t)un.bh * p.num_global + orow : (size_t)un.bh * p.n + orow;
+                    row_lse2 = un.all ? __ldg(p.lse2g + idx) : __ldg(p.lse2 + idx);
+                    row_d = un.all ? __ldg(p.dg + idx) : __ldg(p.dvec + idx);
+                }
             }
-        }
-        // global rows / keys among a contiguous band tile's 16 columns of this thread (counted
-        // by the global units or the compact tiles), loaded one tile ahead
-        const bool use_bitmap = !un.all && p.num_global > 0;
-        auto gbits_of = [&](int t) -> uint32_t {
-            if (!use_bitmap || t >= un.n_cont) return 0u;
-            return global_bits(p.gbitmap, un.inner0 + t * kBN + c0);
-        };
-        uint32_t gnext = T > 0 ? gbits_of(0) : 0u;
-        for (int t = 0; t < T; ++t) {
-            const int b = t % NB;
-            const bool cont = t < un.n_cont;
-            const int tile0 = cont ? un.inner0 + t * kBN : (t - un.n_cont) * kBN;
-            const uint32_t gbits = gnext;
-            gnext = gbits_of(t + 1);
-            // this thread's visible columns of its 16: [lo, hi]
-            int lo, hi;
-            if (un.all) {
-                lo = 0;
-                hi = row_ok ? p.n - 1 - tile0 : -1;
-            } else if (cont) {
-                lo = orow - tile0 - p.window;
-                hi = orow - tile0 + p.window;
-                if (hi > p.n - 1 - tile0) hi = p.n - 1 - tile0;
-                if (!row_ok) hi = -1;
-            } else {
-                lo = 0;
-                hi = row_ok ? p.num_global - 1 - tile0 : -1;
+            // global rows / keys among a contiguous band tile's 16 columns of this thread (counted
+            // by the global units or the compact tiles), loaded one tile ahead
+            const bool use_bitmap = !un.all && p.num_global > 0;
+            auto gbits_of = [&](int t) -> uint32_t {
+                if (!use_bitmap || t >= un.n_cont) return 0u;
+                return global_bits(p.gbitmap, un.inner0 + t * kBN + c0);
+            };
+            uint32_t gnext = gbits_of(0);
+            for (int t = 0; t < T; ++t, ++g) {
+                const int b = g % NB;
+                const bool cont = t < un.n_cont;
+                const int tile0 = tile_row0(un, t);
+                const uint32_t gbits = gnext;
+                gnext = gbits_of(t + 1);
+                // this thread's visible columns of its 16: [lo, hi]
+                int lo, hi;
+                if (un.all) {
+                    lo = 0;
+                    hi = row_ok ? p.n - 1 - tile0 : -1;
+                } else if (cont) {
+                    lo = orow - tile0 - p.window;
+                    hi = orow - tile0 + p.window;
+                    if (hi > p.n - 1 - tile0) hi = p.n - 1 - tile0;
+                    if (!row_ok) hi = -1;
+                } else {
+                    lo = 0;
+                    hi = row_ok ? p.num_global - 1 - tile0 : -1;
+                }
+                const uint32_t bits = range_bits(c0, lo, hi) & ~gbits;
+                wait(&s_full[b], (g / NB) & 1);
+                if constexpr (KM) wait(&st_full[g % kYStages], (g / kYStages) & 1);
+                ok = __all_sync(0xffffffffu, ok);  // warp-uniform, so the __syncwarp below is reached by all
+                if (!ok) break;
+                ptx::tc_fence_after();
+                // packed 16-bit pairs go to the first 8 of this thread's own 16 columns (other
+                // quarters may still be reading theirs)
+                const uint32_t col_s = (uint32_t)b * 128 + c0;
+                const uint32_t col_dp = col_s + kBN;
+                float s[16], dp[16];
+                ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + c0, s);
+                ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + kBN + c0, dp);
+                ptx::tmem_wait_ld();
+                const float* st = sStat + (g % kYStages) * 2 * kBN;
+                uint32_t pk[8], dk[8];
+#pragma unroll
+                for (int e = 0; e < 16; e += 2) {
+                    float pv[2], dv[2];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int c = e + h;
+                        float l2, dd;
+                        if constexpr (KM) {
+                            l2 = st[c0 + c];
+                            dd = st[kBN + c0 + c];
+                        } else {
+                            l2 = row_lse2;
+                            dd = row_d;
+                        }
+                        const float pr = ptx::ex2(fmaf(s[c], p.scale_log2, -l2));
+                        const float pm = ((bits >> c) & 1u) ? pr : 0.f;
+                        pv[h] = pm;
+                        dv[h] = pm * (dp[c] - dd);
+                    }
+                    if constexpr (BF16) {
+                        pk[e >> 1] = ptx::pack_bf16x2(pv[0], pv[1]);
+                        dk[e >> 1] = ptx::pack_bf16x2(dv[0], dv[1]);
+                    } else {
+                        pk[e >> 1] = ptx::pack_f16x2(pv[0], pv[1]);
+                        dk[e >> 1] = ptx::pack_f16x2(dv[0], dv[1]);
+                    }
+                }
+                // keys [16 q, 16 q + 16) as 8 packed columns from column 16 q: the A operand of
+                // one 16-key step of the accumulating MMAs
+                if constexpr (KM) ptx::tmem_st8u(t_lane + col_s, pk);
+                ptx::tmem_st8u(t_lane + col_dp, dk);
+                ptx::tmem_wait_st();
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&p_full[b]);
             }
-            const uint32_t bits = range_bits(c0, lo, hi) & ~gbits;
-            wait(&s_full[b], (t / NB) & 1);
-            if constexpr (KM) wait(&st_full[t % kYStages], (t / kYStages) & 1);
-            ok = __all_sync(0xffffffffu, ok);  // warp-uniform, so the __syncwarp below is reached by all
+            if (!ok) break;
+            // the unit's result: this thread's outer row, columns [D/4 q, D/4 (q + 1)) of the
+            // accumulators, once every accumulating MMA of the unit has finished
+            wait(acc_full, k & 1);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             ptx::tc_fence_after();
-            // packed 16-bit pairs go to the first 8 of this thread's own 16 columns (other
-            // quarters may still be reading theirs)
-            const uint32_t col_s = (uint32_t)b * 128 + c0;
-            const uint32_t col_dp = col_s + kBN;
-            float s[16], dp[16];
-            ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + c0, s);
-            ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + kBN + c0, dp);
-            ptx::tmem_wait_ld();
-            const float* st = sStat + (t % kYStages) * 2 * kBN;
-            uint32_t pk[8], dk[8];
+            bool write = row_ok;
+            float* dst_a = nullptr;
+            float* dst_b = nullptr;
+            if (un.all) {
+                const size_t rr = ((size_t)un.split * p.bh + un.bh) * p.num_global + orow;
+                dst_a = p.part_a + rr * D;
+                if constexpr (KM) dst_b = p.part_b + rr * D;
+            } else {
+                if (write && p.num_global > 0 && ((__ldg(p.gbitmap + (orow >> 5)) >> (orow & 31)) & 1u))
+                    write = false;
+                const size_t rr = (size_t)un.bh * p.n + orow;
+                dst_a = p.out_a + rr * D;
+                if constexpr (KM) dst_b = p.out_b + rr * D;
+            }
 #pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-                float pv[2], dv[2];
+            for (int ch = 0; ch < D / 64; ++ch) {
+                const int cc = (q * (D / 64) + ch) * 16;
+                float a[16];
+                ptx::tmem_ld16(t_lane + kColA + cc, a);
+                float bb[16];
+                if constexpr (KM) ptx::tmem_ld16(t_lane + kColB + cc, bb);
+                ptx::tmem_wait_ld();
+                if (write) {
+                    // dQ and dK carry the scale, dV does not
+                    const float f = KM ? 1.f : p.scale;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int c = e + h;
-                    float l2, dd;
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<float4*>(dst_a + cc + e) =
+                            make_float4(a[e] * f, a[e + 1] * f, a[e + 2] * f, a[e + 3] * f);
                     if constexpr (KM) {
-                        l2 = st[c0 + c];
-                        dd = st[kBN + c0 + c];
-                    } else {
-                        l2 = row_lse2;
-                        dd = row_d;
+#pragma unroll
+                        for (int e = 0; e < 16; e += 4)
+                            *reinterpret_cast<float4*>(dst_b + cc + e) = make_float4(
+                                bb[e] * p.scale, bb[e + 1] * p.scale, bb[e + 2] * p.scale, bb[e + 3] * p.scale);
                     }
-                    const float pr = ptx::ex2(fmaf(s[c], p.scale_log2, -l2));
-                    const float pm = ((bits >> c) & 1u) ? pr : 0.f;
-                    pv[h] = pm;
-                    dv[h] = pm * (dp[c] - dd);
-                }
-                if constexpr (BF16) {
-                    pk[e >> 1] = ptx::pack_bf16x2(pv[0], pv[1]);
-                    dk[e >> 1] = ptx::pack_bf16x2(dv[0], dv[1]);
-                } else {
-                    pk[e >> 1] = ptx::pack_f16x2(pv[0], pv[1]);
-                    dk[e >> 1] = ptx::pack_f16x2(dv[0], dv[1]);
                 }
             }
-            // keys [16 q, 16 q + 16) as 8 packed columns from column 16 q: the A operand of one
-            // 16-key step of the accumulating MMAs
-            if constexpr (KM) ptx::tmem_st8u(t_lane + col_s, pk);
-            ptx::tmem_st8u(t_lane + col_dp, dk);
-            ptx::tmem_wait_st();
+            // the accumulators may be overwritten by the next unit
             ptx::tc_fence_before();
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&p_full[b]);
+            if (lane == 0) ptx::mbar_arrive(acc_free);
         }
     }
     if (__syncthreads_or(!ok) || *abort_flag) ok = false;
-
-    if (ok && T > 0 && warp < kCalcThreads / 32) {
-        ptx::tc_fence_after();
-        // epilogue: this thread's outer row, columns [D/4 q, D/4 (q + 1)) of the accumulators
-        const int r = tid & (kBM - 1);
-        const int q = tid >> 7;
-        const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const int orow = un.outer0 + r;
-        const bool row_ok = un.all ? (orow < p.num_global) : (orow < p.n);
-        bool write = row_ok;
-        float* dst_a = nullptr;
-        float* dst_b = nullptr;
-        if (un.all) {
-            const size_t rr = ((size_t)un.split * p.bh + un.bh) * p.num_global + orow;
-            dst_a = p.part_a + rr * D;
-            if constexpr (KM) dst_b = p.part_b + rr * D;
-        } else {
-            if (write && p.num_global > 0 && ((__ldg(p.gbitmap + (orow >> 5)) >> (orow & 31)) & 1u)) write = false;
-            const size_t rr = (size_t)un.bh * p.n + orow;
-            dst_a = p.out_a + rr * D;
-            if constexpr (KM) dst_b = p.out_b + rr * D;
-        }
-#pragma unroll
-        for (int ch = 0; ch < D / 64; ++ch) {
-            const int cc = (q * (D / 64) + ch) * 16;
-            float a[16];
-            ptx::tmem_ld16(t_lane + kColA + cc, a);
-            ptx::tmem_wait_ld();
-            if (write) {
-                // dQ and dK carry the scale, dV does not
-                const float f = KM ? 1.f : p.scale;
-#pragma unroll
-                for (int e = 0; e < 16; e += 4)
-                    *reinterpret_cast<float4*>(dst_a + cc + e) =
-                        make_float4(a[e] * f, a[e + 1] * f, a[e + 2] * f, a[e + 3] * f);
-            }
-            if constexpr (KM) {
-                float bb[16];
-                ptx::tmem_ld16(t_lane + kColB + cc, bb);
-                ptx::tmem_wait_ld();
-                if (write) {
-#pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4*>(dst_b + cc + e) = make_float4(
-                            bb[e] * p.scale, bb[e + 1] * p.scale, bb[e + 2] * p.scale, bb[e + 3] * p.scale);
-                }
-            }
-        }
-    }
     ptx::tc_fence_before();
     __syncthreads();
     if (warp == 0) ptx::tmem_dealloc(tmem, kBwdTmemCols);
@@ -630,7 +666,8 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < kDevices) attr_set[dev] = true;
     }
-    kern<<<(unsigned)p.n_units, kBwdThreads, smem, stream>>>(m.x1, m.x2, m.y1, m.y2, m.x1g, m.x2g, m.y1g, m.y2g, p);
+    const unsigned grid = (unsigned)(p.n_units < p.grid ? p.n_units : p.grid);
+    kern<<<grid, kBwdThreads, smem, stream>>>(m.x1, m.x2, m.y1, m.y2, m.x1g, m.x2g, m.y1g, m.y2g, p);
     return cudaGetLastError();
 }
 

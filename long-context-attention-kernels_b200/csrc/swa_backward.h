@@ -35,6 +35,7 @@ struct BwdParams {
     int n_splits;      // splits per (bh, global tile)
     int n_band_units;  // bh * n_tiles
     int n_units;       // n_band_units + bh * g_tiles * n_splits
+    int grid;          // CTAs of the persistent grid (the SM count), at most n_units
     float scale;       // softmax scale (dQ and dK carry it)
     float scale_log2;  // scale * log2(e)
     const int* gidx;   // [G] sorted absolute global indices
