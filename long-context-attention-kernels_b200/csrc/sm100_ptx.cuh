@@ -122,6 +122,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// ---------------------------------------------------------------- cp.async
+
+// 4-byte asynchronous copy global -> shared; `valid` false zero-fills the destination (no
+// bytes are read from `gsrc`, which must still be a mapped address).
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued before has completed (the arrival
+// counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

@@ -335,30 +335,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
     } else if (warp == kCalcThreads / 32 + 2) {
         // ============================================================ producer
-        // dK/dV kernel: LSE and D of inner tile t of unit un into stage g % kYStages (all lanes)
+        // dK/dV kernel: LSE and D of inner tile t of unit un into stage g % kYStages (all lanes;
+        // asynchronous copies, each lane's arrival on st_full fires when its copies have landed,
+        // so the producer does not wait for the loads)
         auto stage_stats = [&](const BwdUnit& un, int t, int g) {
             if constexpr (KM) {
                 float* st = sStat + (g % kYStages) * 2 * kBN;
                 const bool cont = t < un.n_cont;
                 const int tile0 = tile_row0(un, t);
+                const float* l2src = cont ? p.lse2 + (size_t)un.bh * p.n : p.lse2g + (size_t)un.bh * p.num_global;
+                const float* ddsrc = cont ? p.dvec + (size_t)un.bh * p.n : p.dg + (size_t)un.bh * p.num_global;
+                const int rows = cont ? p.n : p.num_global;
 #pragma unroll
                 for (int h = 0; h < kBN / 32; ++h) {
                     const int c = h * 32 + lane;
-                    float l2 = 0.f, dd = 0.f;
-                    if (cont) {
-                        const int i = tile0 + c;
-                        if (i < p.n) {
-                            l2 = __ldg(p.lse2 + (size_t)un.bh * p.n + i);
-                            dd = __ldg(p.dvec + (size_t)un.bh * p.n + i);
-                        }
-                    } else if (tile0 + c < p.num_global) {
-                        l2 = __ldg(p.lse2g + (size_t)un.bh * p.num_global + tile0 + c);
-                        dd = __ldg(p.dg + (size_t)un.bh * p.num_global + tile0 + c);
-                    }
-                    st[c] = l2;
-                    st[kBN + c] = dd;
+                    const bool valid = tile0 + c < rows;
+                    const int i = valid ? tile0 + c : 0;  // (rows past the end are zero-filled)
+                    ptx::cp_async_4(st + c, l2src + i, valid);
+                    ptx::cp_async_4(st + kBN + c, ddsrc + i, valid);
                 }
-                ptx::mbar_arrive(&st_full[g % kYStages]);  // releases this lane's writes
+                ptx::cp_async_mbar_arrive(&st_full[g % kYStages]);
             }
         };
         if (lane == 0) {
