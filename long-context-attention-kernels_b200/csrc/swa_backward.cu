@@ -46,7 +46,7 @@ namespace {
 
 constexpr int kBM = 128;                 // rows of an outer tile
 constexpr int kBN = 64;                  // rows of an inner tile
-constexpr int kCalcThreads = 512;        // four warpgroups: warpgroup q owns columns [16 q, 16 q + 16) of a tile
+constexpr int kCalcThreads = 512;        // four warpgroups, two per group of alternate inner tiles
 constexpr int kBwdThreads = kCalcThreads + 96;  // plus three control warps (S/dP issue, accumulate issue, loads)
 constexpr uint32_t kBwdTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         for (int i = 0; i < NB; ++i) {
             ptx::mbar_init(&s_full[i], 1);
-            ptx::mbar_init(&p_full[i], kCalcThreads / 32);
+            ptx::mbar_init(&p_full[i], kCalcThreads / 64);  // the warps of the tile's group
             ptx::mbar_init(&buf_free[i], 1);
         }
         ptx::mbar_init(acc_full, 1);
@@ -399,9 +399,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
     } else {
         // ============================================================ P / dS warps
+        // Two groups of eight warps take alternate inner tiles (tile g goes to group g % 2), so
+        // one group's TMEM loads and stores and barrier waits overlap the other group's
+        // arithmetic, and each thread's per-tile bookkeeping covers 32 columns.  Warpgroups
+        // 2 grp and 2 grp + 1 form group grp; both span the 128 TMEM lanes, one per column half.
         const int r = tid & (kBM - 1);  // outer row <-> TMEM lane
-        const int q = tid >> 7;         // column quarter of every inner tile
-        const int c0 = q * 16;
+        const int q = tid >> 7;         // warpgroup; the epilogue's column quarter
+        const int grp = q >> 1;
+        const int c0 = (q & 1) * 32;    // this thread's columns of its group's tiles
         const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         int g = 0;
         for (int k = 0, u = u_first; u < p.n_units && ok; ++k, u += u_step) {
@@ -417,21 +422,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     row_d = un.all ? __ldg(p.dg + idx) : __ldg(p.dvec + idx);
                 }
             }
-            // global rows / keys among a contiguous band tile's 16 columns of this thread (counted
-            // by the global units or the compact tiles), loaded one tile ahead
             const bool use_bitmap = !un.all && p.num_global > 0;
-            auto gbits_of = [&](int t) -> uint32_t {
-                if (!use_bitmap || t >= un.n_cont) return 0u;
-                return global_bits(p.gbitmap, un.inner0 + t * kBN + c0);
-            };
-            uint32_t gnext = gbits_of(0);
             for (int t = 0; t < T; ++t, ++g) {
+                if ((g & 1) != grp) continue;
                 const int b = g % NB;
                 const bool cont = t < un.n_cont;
                 const int tile0 = tile_row0(un, t);
-                const uint32_t gbits = gnext;
-                gnext = gbits_of(t + 1);
-                // this thread's visible columns of its 16: [lo, hi]
+                // global rows / keys among a contiguous band tile's 32 columns of this thread
+                // (counted by the global units or the compact tiles)
+                const uint32_t gbits = (use_bitmap && cont) ? global_bits(p.gbitmap, tile0 + c0) : 0u;
+                // the outer row's visible columns of the tile (this thread's are [c0, c0 + 32)): [lo, hi]
                 int lo, hi;
                 if (un.all) {
                     lo = 0;
@@ -451,47 +451,53 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 ok = __all_sync(0xffffffffu, ok);  // warp-uniform, so the __syncwarp below is reached by all
                 if (!ok) break;
                 ptx::tc_fence_after();
-                // packed 16-bit pairs go to the first 8 of this thread's own 16 columns (other
-                // quarters may still be reading theirs)
+                // the packed 16-bit pairs of each 16 columns go to the first 8 of them (the other
+                // column half may still be reading its own)
                 const uint32_t col_s = (uint32_t)b * 128 + c0;
                 const uint32_t col_dp = col_s + kBN;
-                float s[16], dp[16];
-                ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + c0, s);
-                ptx::tmem_ld16(t_lane + (uint32_t)b * 128 + kBN + c0, dp);
-                ptx::tmem_wait_ld();
                 const float* st = sStat + (g % kYStages) * 2 * kBN;
-                uint32_t pk[8], dk[8];
+                uint32_t pk[2][8], dk[2][8];
 #pragma unroll
-                for (int e = 0; e < 16; e += 2) {
-                    float pv[2], dv[2];
+                for (int j = 0; j < 2; ++j) {
+                    float s[16], dp[16];
+                    ptx::tmem_ld16(t_lane + col_s + 16 * j, s);
+                    ptx::tmem_ld16(t_lane + col_dp + 16 * j, dp);
+                    ptx::tmem_wait_ld();
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int c = e + h;
-                        float l2, dd;
-                        if constexpr (KM) {
-                            l2 = st[c0 + c];
-                            dd = st[kBN + c0 + c];
-                        } else {
-                            l2 = row_lse2;
-                            dd = row_d;
+                    for (int e = 0; e < 16; e += 2) {
+                        float pv[2], dv[2];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int c = 16 * j + e + h;
+                            float l2, dd;
+                            if constexpr (KM) {
+                                l2 = st[c0 + c];
+                                dd = st[kBN + c0 + c];
+                            } else {
+                                l2 = row_lse2;
+                                dd = row_d;
+                            }
+                            const float pr = ptx::ex2(fmaf(s[e + h], p.scale_log2, -l2));
+                            const float pm = ((bits >> c) & 1u) ? pr : 0.f;
+                            pv[h] = pm;
+                            dv[h] = pm * (dp[e + h] - dd);
                         }
-                        const float pr = ptx::ex2(fmaf(s[c], p.scale_log2, -l2));
-                        const float pm = ((bits >> c) & 1u) ? pr : 0.f;
-                        pv[h] = pm;
-                        dv[h] = pm * (dp[c] - dd);
-                    }
-                    if constexpr (BF16) {
-                        pk[e >> 1] = ptx::pack_bf16x2(pv[0], pv[1]);
-                        dk[e >> 1] = ptx::pack_bf16x2(dv[0], dv[1]);
-                    } else {
-                        pk[e >> 1] = ptx::pack_f16x2(pv[0], pv[1]);
-                        dk[e >> 1] = ptx::pack_f16x2(dv[0], dv[1]);
+                        if constexpr (BF16) {
+                            pk[j][e >> 1] = ptx::pack_bf16x2(pv[0], pv[1]);
+                            dk[j][e >> 1] = ptx::pack_bf16x2(dv[0], dv[1]);
+                        } else {
+                            pk[j][e >> 1] = ptx::pack_f16x2(pv[0], pv[1]);
+                            dk[j][e >> 1] = ptx::pack_f16x2(dv[0], dv[1]);
+                        }
                     }
                 }
-                // keys [16 q, 16 q + 16) as 8 packed columns from column 16 q: the A operand of
-                // one 16-key step of the accumulating MMAs
-                if constexpr (KM) ptx::tmem_st8u(t_lane + col_s, pk);
-                ptx::tmem_st8u(t_lane + col_dp, dk);
+                // keys [c0 + 16 j, c0 + 16 j + 16) as 8 packed columns from column c0 + 16 j: the
+                // A operand of one 16-key step of the accumulating MMAs
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if constexpr (KM) ptx::tmem_st8u(t_lane + col_s + 16 * j, pk[j]);
+                    ptx::tmem_st8u(t_lane + col_dp + 16 * j, dk[j]);
+                }
                 ptx::tmem_wait_st();
                 ptx::tc_fence_before();
                 __syncwarp();
