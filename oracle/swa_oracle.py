@@ -159,3 +159,54 @@ def sliding_window_attention_backward(Q, K, V, dO, window_size: int, global_toke
                 dK[b, h] += dtype(scale) * (ds.T @ q)
                 dV[b, h] += p.T @ do
     return dQ, dK, dV
+
+
+def sliding_window_attention_backward_banded(Q, K, V, dO, window_size: int, global_tokens: Sequence[int],
+                                             scale: float, dtype=np.float64, block_rows: int = 512):
+    """The gradients of :func:`sliding_window_attention_backward` in O(n (block + 2w + G) d)
+    instead of O(n^2 d), for full-length checks.
+
+    A block of non-global rows [s, e) sees only the band keys [s - w, e + w) and the global
+    keys, so its scores are taken over those columns alone.  The global rows see every key
+    (python/long_context_attention/__init__.py:46-47) and take one dense pass.  Same
+    definition, same arithmetic per visible pair; all arrays [B, H, n, d].
+    """
+    Q, K, V, dO = (np.asarray(x) for x in (Q, K, V, dO))
+    B, H, n, d = Q.shape
+    g = normalize_global_tokens(global_tokens, n)
+    w = int(window_size)
+    is_global = np.zeros(n, dtype=bool)
+    is_global[g] = True
+    dQ = np.zeros((B, H, n, d), dtype=dtype)
+    dK = np.zeros((B, H, n, d), dtype=dtype)
+    dV = np.zeros((B, H, n, d), dtype=dtype)
+
+    def rows_pass(b, h, r, cols, mask):
+        k = K[b, h, cols].astype(dtype, copy=False)
+        v = V[b, h, cols].astype(dtype, copy=False)
+        q = Q[b, h, r].astype(dtype, copy=False)
+        do = dO[b, h, r].astype(dtype, copy=False)
+        scores = np.where(mask, (q @ k.T) * dtype(scale), -np.inf)
+        m = scores.max(axis=1, keepdims=True)
+        p = np.exp(scores - m)
+        p /= p.sum(axis=1, keepdims=True)
+        o = p @ v
+        dvec = (do * o).sum(axis=1, keepdims=True)
+        ds = p * (do @ v.T - dvec)
+        dQ[b, h, r] = dtype(scale) * (ds @ k)
+        dK[b, h, cols] += dtype(scale) * (ds.T @ q)   # cols are unique
+        dV[b, h, cols] += p.T @ do
+
+    for b in range(B):
+        for h in range(H):
+            for s in range(0, n, block_rows):
+                r = np.arange(s, min(n, s + block_rows), dtype=np.int64)
+                r = r[~is_global[r]]
+                if r.size == 0:
+                    continue
+                cols = np.union1d(np.arange(max(0, int(r[0]) - w), min(n, int(r[-1]) + w + 1), dtype=np.int64), g)
+                mask = (np.abs(r[:, None] - cols[None, :]) <= w) | is_global[cols][None, :]
+                rows_pass(b, h, r, cols, mask)
+            if g.size:
+                rows_pass(b, h, g, np.arange(n, dtype=np.int64), np.ones((g.size, n), dtype=bool))
+    return dQ, dK, dV

@@ -134,3 +134,30 @@ def test_backward_through_the_c_abi():
     assert c.backward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), LSE.data_ptr(), dO.data_ptr(),
                       dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), c.DTYPE_F16, 1, 1, 512, 64, 30, 0.125,
                       [2, 300], ws.data_ptr(), nbytes - 1, None) == c.ERR_WORKSPACE
+
+
+def test_backward_full_size_against_the_banded_oracle():
+    """One head of the 64K bf16 problem the benchmark times (w = 256, 65 global tokens), every
+    row of dQ, dK and dV against the banded fp64 oracle, with the tolerance of the small
+    cases; the global tokens' rows (split partials summed by the reduce) are also checked on
+    their own, since they are 0.1 % of the rows."""
+    import long_context_attention as lca
+    from long_context_attention.workloads import WORKLOADS
+    wl = WORKLOADS["many_globals_64k"]
+    Q, K, V = (t.cuda() for t in wl.inputs(heads_slice=slice(0, 1)))
+    tokens = wl.global_tokens()
+    dO = torch.randn(Q.shape, generator=torch.Generator().manual_seed(64)).cuda()
+    O, LSE = lca.sliding_window_attention_with_lse(Q, K, V, wl.window, tokens, wl.scale)
+    got = lca.sliding_window_attention_backward(Q, K, V, O, LSE, dO, wl.window, tokens, wl.scale)
+    torch.cuda.synchronize()
+    assert lca.device_error() == 0
+    args = [t.double().cpu().numpy() for t in (Q, K, V, dO)]
+    want = swa_oracle.sliding_window_attention_backward_banded(*args, wl.window, tokens, wl.scale)
+    grows = np.asarray(sorted(set(tokens)))
+    for name, g, ref in zip(("dQ", "dK", "dV"), got, want):
+        g = g.double().cpu().numpy()
+        assert np.isfinite(g).all(), name
+        err = rel_l2(g, ref)
+        assert err <= TOL[torch.bfloat16], f"{name}: rel-L2 {err:.2e}"
+        err = rel_l2(g[:, :, grows], ref[:, :, grows])
+        assert err <= TOL[torch.bfloat16], f"{name} (global rows): rel-L2 {err:.2e}"

@@ -164,3 +164,18 @@ def test_backward_oracle_matches_finite_differences():
             args[which][idx] -= 2 * eps
             down = loss(*args)
             assert abs((up - down) / (2 * eps) - grad[idx]) < 1e-6
+
+
+@pytest.mark.parametrize("B,H,n,d,w,g,block", [(1, 2, 37, 8, 3, [0, 5, -1], 8), (2, 1, 64, 16, 0, [], 16),
+                                               (1, 1, 50, 4, 100, [7, 7], 16), (1, 2, 130, 8, 9, [129, 0, 64], 32),
+                                               (1, 1, 300, 8, 20, list(range(0, 300, 3)), 64),
+                                               (1, 1, 257, 4, 30, [256], 512)])
+def test_banded_backward_oracle_matches_the_dense_one(B, H, n, d, w, g, block):
+    """The banded restatement (full-length checks) against the dense-mask backward: row
+    blocks that hold global rows, blocks of only global rows, window 0 and >= n."""
+    rng = np.random.default_rng(n + w)
+    Q, K, V, dO = (rng.standard_normal((B, H, n, d)) for _ in range(4))
+    want = swa_oracle.sliding_window_attention_backward(Q, K, V, dO, w, g, 0.45)
+    got = swa_oracle.sliding_window_attention_backward_banded(Q, K, V, dO, w, g, 0.45, block_rows=block)
+    for a, b in zip(got, want):
+        assert max_abs(a, b) < 1e-12
