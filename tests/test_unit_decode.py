@@ -33,6 +33,8 @@ def cdiv(a, b):
 def params(n, window, G, bh, q_off=0, n_total=None, world=1, causal=False, head_window=()):
     sharded = world > 1
     n_total = n if n_total is None else n_total
+    window = min(window, n_total)                      # the host clamps radii to the sequence
+    head_window = [min(h, n_total) for h in head_window]
     lead = cdiv(window, T) * T if sharded else window
     p = dict(n=n, q_off=q_off, n_total=n_total, sharded=sharded, window=window, lead=lead, bh=bh, G=G,
              causal=causal, head_window=list(head_window), halo=window if sharded else 0)
